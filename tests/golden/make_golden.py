@@ -1,0 +1,130 @@
+"""Writes the golden vectors under tests/golden/ by running the REFERENCE's own Python code.
+
+    python tests/golden/make_golden.py [--ref /path/to/OpenFlowLM-Next]
+
+Needs the reference tree (read in place; nothing is copied) and ``gguf`` 0.19.0. The GPU box has
+neither, so the fixtures are committed and the tests read only the ``.npz`` files. Each fixture
+stores the reference's outputs and, for large inputs that a seeded generator reproduces, a
+SHA-256 of the input bytes so a test can prove its regenerated inputs are the very bytes the
+reference saw.
+
+Fixtures:
+  q4_1.npz    reference ``q4_1_pack.random_q4_1_blocks`` (seed 0) bytes and its ``dequant_q4_1``;
+              ``gguf.quantize(.., Q4_1)`` bytes of a seeded f32 matrix and ``gguf.dequantize``;
+              the reference pool packers' bytes (``pack_q4_1_pool`` rs=2, ``gguf_pool.pack_q4_pool``).
+  router.npz  ``replica_block.random_case(0)`` router inputs/outputs (E=8, topk=3); the tie KAT of
+              ``test_prefill_batch.py:363-369``; a config-1 router (T=16, H=2048, E=128, k=8) on
+              seeded bf16 inputs.
+  moe.npz     ``replica.moe_decode`` (fp64, HF-faithful) over 4 tokens of a small Qwen3.6-shaped
+              block (H=2048 as replica.py fixes it, E=16, F=128, shared F=128, top-8) whose Q4_1
+              experts come from the reference's block generator (seed 0).
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def bf16_vals(a: np.ndarray) -> np.ndarray:
+    from ml_dtypes import bfloat16
+    return np.asarray(a, np.float32).astype(bfloat16).astype(np.float32)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    a = ap.parse_args()
+    ref = Path(a.ref)
+    sys.path[:0] = [str(ref / "open_kernels"), str(ref / "open_kernels" / "model"), str(ref)]
+    import gguf
+    import q4_1_pack as QP                       # open_kernels/q4_1_pack.py
+    from open_kernels.gguf_pool import gguf_pool as GP   # open_kernels/gguf_pool/gguf_pool.py
+    import replica_block as RB                   # open_kernels/model/replica_block.py
+    import replica as RP                         # open_kernels/model/replica.py
+    from ml_dtypes import bfloat16
+
+    # ---- q4_1
+    rng = np.random.default_rng(0)
+    blocks = QP.random_q4_1_blocks(64, 256, rng)
+    deq = QP.dequant_q4_1(blocks)
+    deq_bf16s = QP.dequant_q4_1(blocks, bfloat16)
+    pool_bf16 = QP.pack_q4_1_pool(blocks, 2)
+    pool_f32 = GP.pack_q4_pool(blocks, 2, "Q4_1")
+    wq = np.random.default_rng(1).normal(0, 0.02, (32, 256)).astype(np.float32)
+    wq[0, :32] = 0.0                               # a constant block (d == 0)
+    gq = gguf.quantize(wq, gguf.GGMLQuantizationType.Q4_1)
+    gdq = gguf.dequantize(gq, gguf.GGMLQuantizationType.Q4_1)
+    np.savez_compressed(HERE / "q4_1.npz", blocks=blocks, dequant=deq, dequant_bf16_scales=deq_bf16s,
+                        pool_bf16_rs2=pool_bf16, pool_f32_rs2=pool_f32, gguf_in=wq,
+                        gguf_q4_1=np.asarray(gq, np.uint8), gguf_dequant=np.asarray(gdq, np.float32))
+
+    # ---- router
+    case = RB.random_case(0)
+    p, idx, w = RB.router_block(case["xm"], case["Wr"], case["topk"])
+    tie_x = np.array([[1.0, 0.0]])
+    tie_W = np.array([[0.5, 0.5, 0.2, 0.5], [0.0, 0.0, 0.0, 0.0]])
+    tp, tidx, tw = RB.router_block(tie_x, tie_W, 2)
+    r2 = np.random.default_rng(0)
+    x1 = bf16_vals(r2.standard_normal((16, 2048), dtype=np.float32))
+    W1 = bf16_vals(r2.normal(0, 0.02, (2048, 128)).astype(np.float32))
+    p1, idx1, w1 = RB.router_block(x1.astype(np.float64), W1.astype(np.float64), 8)
+    np.savez_compressed(HERE / "router.npz",
+                        rc_xm=case["xm"], rc_Wr=case["Wr"], rc_topk=case["topk"], rc_probs=p, rc_idx=idx, rc_w=w,
+                        tie_x=tie_x, tie_W=tie_W, tie_probs=tp, tie_idx=tidx, tie_w=tw,
+                        c1_x_sha=sha(x1), c1_W_sha=sha(W1), c1_probs=p1, c1_idx=idx1, c1_w=w1)
+
+    # ---- moe_decode over 4 tokens
+    H, E, F, FS, T = 2048, 16, 128, 128, 4
+    rng = np.random.default_rng(0)
+    gate = [QP.random_q4_1_blocks(F, H, rng) for _ in range(E)]
+    up = [QP.random_q4_1_blocks(F, H, rng) for _ in range(E)]
+    down = [QP.random_q4_1_blocks(H, F, rng, scale=0.05) for _ in range(E)]
+    sg, su, sd = (QP.random_q4_1_blocks(FS, H, rng), QP.random_q4_1_blocks(FS, H, rng),
+                  QP.random_q4_1_blocks(H, FS, rng, scale=0.05))
+    postln = bf16_vals(1 + rng.normal(0, 0.01, H).astype(np.float32))
+    Wr = bf16_vals(rng.normal(0, 0.02, (H, E)).astype(np.float32))
+    sgw = bf16_vals(rng.normal(0, 0.02, H).astype(np.float32))
+    xres = rng.standard_normal((T, H)).astype(np.float32)
+
+    class Model:
+        """The accessors replica.moe_decode reads, over the seeded blocks above."""
+        def bf16(self, name):
+            return {"model.layer.0.post_attention_layernorm.weight": postln,
+                    "model.layer.0.moe_router.weight": Wr,
+                    "model.layer.0.shared_expert_gate.weight": sgw}[name]
+
+        def expert_w(self, layer, kind, e):
+            return QP.dequant_q4_1({"gate": gate, "up": up, "down": down}[kind][e])
+
+        def shared_w(self, layer, kind):
+            return QP.dequant_q4_1({"gate": sg, "up": su, "down": sd}[kind])
+
+    m = Model()
+    outs, xms, tops, probs = [], [], [], []
+    for t in range(T):
+        xm, pt, top = RP.route(m, 0, xres[t].astype(np.float64))
+        outs.append(RP.moe_decode(m, 0, xres[t].astype(np.float64)))
+        xms.append(xm)
+        tops.append(top)
+        probs.append(pt)
+    allb = np.concatenate([b.reshape(-1) for b in gate + up + down + [sg, su, sd]])
+    np.savez_compressed(HERE / "moe.npz", H=H, E=E, F=F, FS=FS, T=T, blocks_sha=sha(allb),
+                        postln=postln, Wr=Wr, sgw=sgw, xres=xres, xm=np.array(xms, np.float32),
+                        top=np.array(tops, np.int32), probs=np.array(probs), out=np.array(outs))
+    for f in ("q4_1.npz", "router.npz", "moe.npz"):
+        print(f"wrote {HERE / f} ({(HERE / f).stat().st_size} B)")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

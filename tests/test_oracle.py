@@ -1,0 +1,146 @@
+"""The CPU oracle pinned against the reference's own golden vectors (tests/golden/*.npz)."""
+import ctypes
+import hashlib
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import moe as OM
+from oracle import q4_1 as OQ
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def test_generator_matches_reference_bytes(golden):
+    blocks = OQ.random_q4_1_blocks(64, 256, np.random.default_rng(0))
+    assert np.array_equal(blocks, golden["q4_1"]["blocks"])
+
+
+def test_dequant_bit_exact(golden):
+    g = golden["q4_1"]
+    assert np.array_equal(OQ.dequant_q4_1(g["blocks"]), g["dequant"])
+
+
+def test_quantizer_matches_gguf_bytes(golden):
+    g = golden["q4_1"]
+    got = OQ.quantize_q4_1(g["gguf_in"])
+    assert np.array_equal(got.reshape(-1), g["gguf_q4_1"].reshape(-1))
+    assert np.array_equal(OQ.dequant_q4_1(got).reshape(-1), g["gguf_dequant"].reshape(-1))
+
+
+def test_router_random_case(golden):
+    r = golden["router"]
+    p, idx, w = OM.router_block(r["rc_xm"], r["rc_Wr"], int(r["rc_topk"]))
+    np.testing.assert_allclose(p, r["rc_probs"], rtol=1e-12, atol=1e-15)
+    assert np.array_equal(idx, r["rc_idx"])
+    np.testing.assert_allclose(w, r["rc_w"], rtol=1e-12)
+
+
+def test_router_tie_lowest_index(golden):
+    r = golden["router"]
+    p, idx, w = OM.router_block(r["tie_x"], r["tie_W"], 2)
+    assert idx.tolist() == r["tie_idx"].tolist() == [[0, 1]]
+    np.testing.assert_allclose(w, r["tie_w"])
+
+
+def _c1_inputs():
+    from oracle.moe import bf16_round
+    r2 = np.random.default_rng(0)
+    x1 = bf16_round(r2.standard_normal((16, 2048), dtype=np.float32))
+    W1 = bf16_round(r2.normal(0, 0.02, (2048, 128)).astype(np.float32))
+    return x1, W1
+
+
+def test_router_config1(golden):
+    r = golden["router"]
+    x1, W1 = _c1_inputs()
+    assert _sha(x1) == str(r["c1_x_sha"]) and _sha(W1) == str(r["c1_W_sha"])
+    p, idx, w = OM.router_block(x1, W1, 8)
+    assert np.array_equal(idx, r["c1_idx"])
+    np.testing.assert_allclose(w, r["c1_w"], rtol=1e-12)
+
+
+def test_router_topk_past_experts_raises():
+    with pytest.raises(ValueError):
+        OM.router_block(np.zeros((1, 4)), np.zeros((4, 3)), 4)
+
+
+def _moe_inputs(g):
+    H, E, F, FS = int(g["H"]), int(g["E"]), int(g["F"]), int(g["FS"])
+    rng = np.random.default_rng(0)
+    gate = [OQ.random_q4_1_blocks(F, H, rng) for _ in range(E)]
+    up = [OQ.random_q4_1_blocks(F, H, rng) for _ in range(E)]
+    down = [OQ.random_q4_1_blocks(H, F, rng, scale=0.05) for _ in range(E)]
+    sg, su, sd = (OQ.random_q4_1_blocks(FS, H, rng), OQ.random_q4_1_blocks(FS, H, rng),
+                  OQ.random_q4_1_blocks(H, FS, rng, scale=0.05))
+    allb = np.concatenate([b.reshape(-1) for b in gate + up + down + [sg, su, sd]])
+    assert _sha(allb) == str(g["blocks_sha"]), "regenerated blocks differ from the reference's"
+    return gate, up, down, (sg, su, sd, g["sgw"])
+
+
+def test_moe_block_matches_replica_fp64(golden):
+    g = golden["moe"]
+    gate, up, down, shared = _moe_inputs(g)
+    xm, top, probs = g["xm"], g["top"], g["probs"]
+    w = np.take_along_axis(probs, top, -1)
+    w = w / w.sum(-1, keepdims=True)
+    out = OM.moe_block_f64(xm, g["xres"], top, w, gate, up, down, shared=shared, engine_rounding=False)
+    # replica.moe_decode multiplies f32 matrices (numpy f32 matmuls), the oracle in f64: agree to f32 roundoff
+    assert np.abs(out - g["out"]).max() / np.abs(g["out"]).max() < 1e-5
+    # the router the block consumed is the oracle's own
+    p, idx, w2 = OM.router_block(xm, g["Wr"], 8)
+    assert np.array_equal(idx, top)
+    # the engine's bf16 rounding points move the result by far less than the parity tolerance
+    out_r = OM.moe_block_f64(xm, g["xres"], top, w, gate, up, down, shared=shared)
+    assert np.abs(out_r - out).max() / np.abs(out - g["xres"]).max() < 2e-2
+
+
+def test_dispatch_stable_and_checked():
+    idx = np.array([[2, 0], [0, 1], [2, 1]], np.int32)
+    counts, offsets, pos, pair = OM.dispatch(idx, 3)
+    assert counts.tolist() == [2, 2, 2]
+    assert pair.tolist() == [1, 2, 3, 5, 0, 4]
+    assert pos.reshape(-1)[pair].tolist() == list(range(6))
+    with pytest.raises(ValueError):
+        OM.dispatch(np.array([[3]], np.int32), 3)
+
+
+def test_cpu_baseline_matches_fp64():
+    rng = np.random.default_rng(3)
+    H, E, F, T = 256, 8, 128, 12
+    gate = [OQ.random_q4_1_blocks(F, H, rng) for _ in range(E)]
+    up = [OQ.random_q4_1_blocks(F, H, rng) for _ in range(E)]
+    down = [OQ.random_q4_1_blocks(H, F, rng, scale=0.05) for _ in range(E)]
+    Wr = OM.bf16_round(rng.normal(0, 0.2, (H, E)).astype(np.float32))
+    x = OM.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    res = rng.standard_normal((T, H)).astype(np.float32)
+    layer = OM.MoeLayerF32(Wr, gate, up, down, topk=3)
+    out, idx, w = layer.forward(x, res)
+    ref = OM.moe_block_f64(x, res, idx, w, gate, up, down)
+    assert np.abs(out - ref).max() / np.abs(ref - res).max() < 1e-3
+
+
+_REF = ROOT / "oracle" / "_ref" / "libref_router.so"
+
+
+@pytest.mark.skipif(not _REF.exists(), reason="reference router not built (make -C oracle)")
+def test_reference_cpp_router_agrees_with_oracle(golden):
+    lib = ctypes.CDLL(str(_REF))
+    x1, W1 = _c1_inputs()
+    T, H = x1.shape
+    E, k = W1.shape[1], 8
+    probs = np.zeros((T, E), np.float32)
+    idx = np.zeros((T, k), np.int32)
+    w = np.zeros((T, k), np.float32)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    rc = lib.ref_router_block(ctypes.c_size_t(T), ctypes.c_size_t(H), ctypes.c_size_t(E), ctypes.c_size_t(k),
+                              P(np.ascontiguousarray(x1)), P(np.ascontiguousarray(W1)), P(probs), P(idx), P(w))
+    assert rc == 0
+    r = golden["router"]
+    assert np.array_equal(idx, r["c1_idx"])
+    np.testing.assert_allclose(w, r["c1_w"], rtol=1e-4)
