@@ -1,0 +1,145 @@
+/*
+ * flowmoe.h -- C ABI of libflowmoe.so, the B200 (sm_100a) Qwen3.6-MoE expert block.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t (passed as void*), returns
+ * an int status (FM_OK or an FM_E* code) and never throws. fm_last_error() returns the message of the
+ * calling thread's last failure. No entry point synchronises the stream unless its comment says so.
+ *
+ * Weights live on the device in the "tile" layout produced by fm_q4_1_to_tiles() from GGUF Q4_1
+ * blocks (the reference's open_kernels/q4_1_pack.py:1-14 block format: fp16 d | fp16 m | 16 nibble
+ * bytes, 32 values along K). The tile layout is a byte permutation of the same blocks (nothing is
+ * re-quantised): a matrix W[N, K] (N % 128 == 0, K % 64 == 0) is cut into tiles of 128 rows x 64 K;
+ * tile (band b, slab s) sits at byte ((b * K/64) + s) * 5120 and holds
+ *     [0, 4096)    row r (0..127): 32 nibble bytes = the 16 nibble bytes of block 2s, then of block 2s+1
+ *     [4096, 5120) row r: 8 bytes = d(2s) m(2s) d(2s+1) m(2s+1), fp16
+ * Per expert, the gate and up matrices [F, H] are stored back to back (gate tiles, then up tiles) in
+ * the "gate_up" array and the down matrix [H, F] in the "down" array.
+ */
+#ifndef FLOWMOE_H
+#define FLOWMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FM_API __attribute__((visibility("default")))
+#else
+#define FM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The reference throws std::runtime_error where these are returned. */
+#define FM_OK 0
+#define FM_EINVAL_SHAPE 1  /* shapes/alignment/topk > E (block_host.cpp:768) */
+#define FM_EINVAL_EXPERT 2 /* an expert id out of range (core.cpp:5159-5160, :2368-2369) */
+#define FM_ECUDA 3         /* a CUDA launch or runtime call failed */
+#define FM_ENCCL 4         /* an NCCL call failed */
+#define FM_ETIMEOUT 5      /* a bounded device wait gave up */
+#define FM_EWORKSPACE 6    /* the caller's workspace is smaller than fm_workspace_size() */
+
+/* Activation dtypes accepted for xm. */
+#define FM_F32 0
+#define FM_BF16 1
+
+/* Geometry and device weights of one MoE layer (the reference's MoeGeometry / ModelSpec MoE fields,
+ * open_kernels/harness/stream_patch.hpp:33-45, recipes/spec.py:96). All pointers are device pointers
+ * owned by the caller; the struct itself is read on the host only. */
+typedef struct fm_layer {
+    int32_t hidden;     /* H (% 128 == 0) */
+    int32_t n_experts;  /* E, the router width (all experts, all ranks) */
+    int32_t top_k;      /* k <= E, k <= 16 */
+    int32_t ffn;        /* F, routed expert intermediate (% 128 == 0) */
+    int32_t shared_ffn; /* F_s of the always-on shared expert; 0 = none */
+    int32_t e_begin;    /* first expert held by this rank (expert parallel); 0 on one GPU */
+    int32_t e_local;    /* experts held by this rank; E on one GPU */
+    int32_t flags;      /* reserved, 0 */
+    const uint8_t* gate_up;   /* tiles, e_local x (2 x F x H x 5/8 B): gate then up, per expert */
+    const uint8_t* down;      /* tiles, e_local x (H x F x 5/8 B) */
+    const uint8_t* shared_gate_up; /* tiles of the shared expert, or NULL */
+    const uint8_t* shared_down;
+    const uint16_t* router;   /* bf16 [E + 1, H]: router rows (Wr transposed), then the shared-gate row */
+    const float* router_bias; /* f32 [E] added to the logits before the softmax, or NULL (none) */
+} fm_layer;
+
+/* Message of this thread's last failure ("" after success). Returns FM_OK. */
+FM_API int fm_last_error(char* buf, size_t n);
+
+/* Library build identity (sm arch, version). Returns FM_OK. */
+FM_API int fm_version(char* buf, size_t n);
+
+/* GGUF Q4_1 blocks uint8[rows, k/32, 20] (device) -> tile layout (device, same byte count).
+ * Replaces the reference's pool packer open_kernels/q4_1_pack.py:124-142 (pack_q4_1_pool) /
+ * gguf_pool/gguf_pool.py:191-213 (pack_q4_pool) for this device. rows % 128 == 0, k % 64 == 0. */
+FM_API int fm_q4_1_to_tiles(const uint8_t* blocks, int32_t rows, int32_t k, uint8_t* tiles, void* stream);
+
+/* Tile layout -> GGUF Q4_1 blocks (the inverse; used to prove the repack is a permutation). */
+FM_API int fm_tiles_to_q4_1(const uint8_t* tiles, int32_t rows, int32_t k, uint8_t* blocks, void* stream);
+
+/* Router weight bf16 Wr [H, E] row-major (the reference's layout, block_host.cpp:775-777) and the
+ * shared-expert gate bf16 sgw [H] (or NULL) -> the layer's router array bf16 [E + 1, H]. */
+FM_API int fm_router_pack(const uint16_t* wr, const uint16_t* sgw, int32_t hidden, int32_t n_experts, uint16_t* router,
+                   void* stream);
+
+/* Device workspace bytes for fm_router_topk / fm_moe_block / fm_moe_layer over T tokens. */
+FM_API int fm_workspace_size(const fm_layer* L, int32_t T, size_t* bytes);
+
+/* The router over a block: logits = bf16(xm) . Wr (fp32 accumulate), softmax, top-k by probability
+ * with the lowest index on a tie, renormalised; shared_gate[t] = sigmoid(bf16(xm[t]) . sgw).
+ * Replaces host::router_block (src/open_qwen36/block_host.hpp:155-159, block_host.cpp:766-803).
+ * xm [T, H] f32 or bf16; probs [T, E] (may be NULL); idx int32 [T, k]; w [T, k];
+ * shared_gate [T] (may be NULL). */
+FM_API int fm_router_topk(const fm_layer* L, const void* xm, int32_t xm_dtype, int32_t T, float* probs, int32_t* idx,
+                   float* w, float* shared_gate, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The expert block: out[t] = res[t] + shared_gate[t] * shared(xm[t]) + sum over t's k experts in
+ * ascending expert order of w[t,s] * down_e(bf16(silu(gate_e x) * up_e x)), x = bf16(xm[t]).
+ * Rows t >= t_real are copied from res. shared_gate may be NULL (no shared expert term; the shared
+ * term is also skipped when the layer has no shared expert). Expert ids outside [e_begin,
+ * e_begin + e_local) are skipped on the device and counted; fm_moe_check() reports them.
+ * Replaces Core::moe_block (src/open_qwen36/core.hpp:844-848, core.cpp:5150-5259) together with the
+ * gated shared-expert add of Core::ffn_block (core.cpp:4342-4380). */
+FM_API int fm_moe_block(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, const int32_t* idx,
+                 const float* w, const float* shared_gate, int32_t T, int32_t t_real, float* out, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* Router + shared expert + experts in one call (the engine's staged_tail -> ffn_block ->
+ * block_layer_moe sequence, core.cpp:4934-4957 and :3685-3700). idx/w (may be NULL) receive the
+ * routing. */
+FM_API int fm_moe_layer(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, int32_t T, int32_t t_real,
+                 float* out, int32_t* idx, float* w, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The dispatch stage alone: per local expert counts [e_local], exclusive offsets [e_local + 1] (the
+ * last = routed pair count), pos [t_real, k] = row of each (token, slot) pair in the expert-sorted
+ * order (-1 for an id outside the local range) and pair [offsets[e_local]] = its inverse (t * k + s).
+ * Within an expert, pairs keep token-then-slot order: the owed lists of core.cpp:5155-5165. Any
+ * output pointer may be NULL. */
+FM_API int fm_moe_dispatch(const fm_layer* L, const int32_t* idx, int32_t T, int32_t t_real, int32_t* counts,
+                           int32_t* offsets, int32_t* pos, int32_t* pair, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* Synchronises `stream` and returns FM_EINVAL_EXPERT if the last fm_moe_block on this workspace met
+ * an expert id outside the range the block accepts (the check core.cpp:5159-5160 throws on). */
+FM_API int fm_moe_check(void* workspace, void* stream);
+
+/* Kernel launches this library has made in this process (the driver-visible proof that the device
+ * path ran). */
+FM_API int fm_launch_count(unsigned long long* n);
+
+/* Stage profiler (the reference's OFLM_OPEN_PROFILE stage timings, core.cpp:592-600, :850-935, on
+ * CUDA events): while enabled, each call records a timing event pair around every stage on its
+ * stream. Stages: 0 to_bf16, 1 router, 2 dispatch, 3 gather, 4 gate_up, 5 down, 6 combine.
+ * fm_profile(1) creates the events on first use; do not enable it during stream capture. */
+FM_API int fm_profile(int32_t enable);
+
+/* Waits for the recorded events and writes the summed milliseconds per stage into ms[0..n_stages),
+ * then clears the record. */
+FM_API int fm_profile_read(double* ms, int32_t n_stages);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLOWMOE_H */

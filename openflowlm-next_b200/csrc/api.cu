@@ -1,0 +1,380 @@
+// The C ABI of libflowmoe.so (declared in include/flowmoe.h): argument checks, the workspace layout
+// and the launch sequence of each entry point. No entry point allocates device memory: the caller
+// passes the workspace (fm_workspace_size) and every output buffer.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace fm {
+
+static thread_local char g_err[512];
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// Stage profiler: pairs of timing events recorded around each stage while enabled; read back (and
+// summed per stage) by fm_profile_read. Events are created when profiling is first enabled.
+struct Profiler {
+    bool on = false;
+    static constexpr int kPairs = 256;
+    cudaEvent_t ev[kPairs][2] = {};
+    int stage[kPairs] = {};
+    int n = 0;
+    int open[kStageCount] = {};
+};
+static thread_local Profiler g_prof;
+
+void prof_begin(int stage, cudaStream_t st) {
+    if (!g_prof.on || g_prof.n >= Profiler::kPairs) return;
+    const int i = g_prof.n++;
+    g_prof.stage[i] = stage;
+    g_prof.open[stage] = i;
+    cudaEventRecord(g_prof.ev[i][0], st);
+}
+
+void prof_end(int stage, cudaStream_t st) {
+    if (!g_prof.on) return;
+    const int i = g_prof.open[stage];
+    if (i < g_prof.n && g_prof.stage[i] == stage) cudaEventRecord(g_prof.ev[i][1], st);
+}
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return FM_ECUDA;
+}
+
+// kernels: see kernels.cuh
+
+constexpr int kBN = 64;        // rows per expert work item (expert_mma)
+constexpr int kChunk = 2048;   // dispatch chunk (dispatch.cu)
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Layout {
+    size_t err, xb, logits, counts, offsets, blk_hist, pos, pair, gu_list, dn_list, xperm, hperm, yperm, sgate, idx, w;
+    size_t total;
+    int nblk, max_gu, max_dn, P, rows, fmax;
+};
+
+static int validate(const fm_layer* L, int T) {
+    if (!L) {
+        set_error("null layer");
+        return FM_EINVAL_SHAPE;
+    }
+    const int H = L->hidden, E = L->n_experts, k = L->top_k, F = L->ffn, FS = L->shared_ffn;
+    if (H <= 0 || H % kTileRows || E <= 0 || E > 1024 || F <= 0 || F % kTileRows || FS < 0 || FS % kTileRows ||
+        T < 0) {
+        set_error("bad geometry H=%d E=%d F=%d F_s=%d T=%d (H, F, F_s %% 128 == 0, E <= 1024)", H, E, F, FS, T);
+        return FM_EINVAL_SHAPE;
+    }
+    if (k <= 0 || k > E || k > kMaxTopK) {
+        set_error("router_block: topk %d past the expert count %d (or > %d)", k, E, kMaxTopK);
+        return FM_EINVAL_SHAPE;
+    }
+    if (L->e_begin < 0 || L->e_local < 0 || L->e_begin + L->e_local > E) {
+        set_error("bad local expert range [%d, %d) of %d", L->e_begin, L->e_begin + L->e_local, E);
+        return FM_EINVAL_SHAPE;
+    }
+    return FM_OK;
+}
+
+static Layout make_layout(const fm_layer* L, int T) {
+    Layout o{};
+    const int H = L->hidden, E = L->n_experts, k = L->top_k;
+    o.P = T * k;
+    o.rows = o.P + T;
+    o.fmax = L->ffn > L->shared_ffn ? L->ffn : L->shared_ffn;
+    o.nblk = (o.P + kChunk - 1) / kChunk;
+    const int G = L->e_local + 1;
+    const int rt_routed = o.P / kBN + L->e_local;       // >= sum over routed groups of ceil(cnt / kBN)
+    const int rt_shared = (T + kBN - 1) / kBN;
+    o.max_gu = rt_routed * (L->ffn / kTileRows) + rt_shared * (L->shared_ffn / kTileRows);
+    o.max_dn = (rt_routed + (L->shared_ffn ? rt_shared : 0)) * (H / kTileRows);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t at = off; off = align256(off + bytes); return at; };
+    o.err = take(16);   // first: fm_moe_check reads the counter at the workspace start
+    o.xb = take((size_t)T * H * 2);
+    o.logits = take((size_t)T * (E + 1) * 4);
+    o.counts = take((size_t)G * 4);
+    o.offsets = take((size_t)(G + 1) * 4);
+    o.blk_hist = take((size_t)o.nblk * L->e_local * 4);
+    o.pos = take((size_t)o.P * 4);
+    o.pair = take((size_t)o.P * 4);
+    o.gu_list = take((size_t)(4 + 4 * o.max_gu) * 4);
+    o.dn_list = take((size_t)(4 + 4 * o.max_dn) * 4);
+    o.xperm = take((size_t)o.rows * H * 2);
+    o.hperm = take((size_t)o.rows * o.fmax * 2);
+    o.yperm = take((size_t)o.rows * H * 4);
+    o.sgate = take((size_t)T * 4);
+    o.idx = take((size_t)o.P * 4);
+    o.w = take((size_t)o.P * 4);
+    o.total = off;
+    return o;
+}
+
+template <class T>
+static T* at(void* ws, size_t off) { return reinterpret_cast<T*>(static_cast<char*>(ws) + off); }
+
+static int check_ws(const Layout& lo, void* ws, size_t bytes) {
+    if (lo.total > 0 && (!ws || bytes < lo.total)) {
+        set_error("workspace of %zu B is smaller than the %zu B needed", bytes, lo.total);
+        return FM_EWORKSPACE;
+    }
+    if (reinterpret_cast<uintptr_t>(ws) & 255) {
+        set_error("workspace must be 256-byte aligned");
+        return FM_EWORKSPACE;
+    }
+    return FM_OK;
+}
+
+static int xm_to_bf16(const fm_layer* L, const void* xm, int dtype, int T, void* ws, const Layout& lo,
+                      const uint16_t** xb, cudaStream_t st) {
+    if (dtype == FM_BF16) {
+        *xb = static_cast<const uint16_t*>(xm);
+        return FM_OK;
+    }
+    if (dtype != FM_F32) {
+        set_error("xm dtype %d is neither FM_F32 nor FM_BF16", dtype);
+        return FM_EINVAL_SHAPE;
+    }
+    *xb = at<uint16_t>(ws, lo.xb);
+    prof_begin(kStageToBf16, st);
+    const int rc = launch_to_bf16(static_cast<const float*>(xm), at<uint16_t>(ws, lo.xb), (long long)T * L->hidden, st);
+    prof_end(kStageToBf16, st);
+    return rc;
+}
+
+static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, const int32_t* idx, const float* w,
+                     const float* sgate, int T, int t_real, float* out, void* ws, const Layout& lo, cudaStream_t st) {
+    const int H = L->hidden, k = L->top_k, E = L->n_experts;
+    const bool shared_on = L->shared_ffn > 0 && sgate && L->shared_gate_up && L->shared_down && t_real > 0;
+    const int P = t_real * k;
+    if (cudaMemsetAsync(at<int>(ws, lo.err), 0, 16, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
+    const int nblk = (P + kChunk - 1) / kChunk;
+    // rows of the sorted space: routed [0, P), shared [P_cap, P_cap + t_real) with P_cap = T * k
+    const int Pcap = lo.P;
+    prof_begin(kStageDispatch, st);
+    int rc = launch_dispatch(idx, P, L->e_begin, L->e_local, E, Pcap, shared_on ? t_real : 0, at<int>(ws, lo.blk_hist), nblk,
+                             at<int>(ws, lo.counts), at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
+                             at<int>(ws, lo.gu_list), L->ffn / kTileRows,
+                             shared_on ? L->shared_ffn / kTileRows : 0, at<int>(ws, lo.dn_list), H / kTileRows, kBN,
+                             at<int>(ws, lo.err), st);
+    if (rc) return rc;
+    prof_end(kStageDispatch, st);
+    prof_begin(kStageGather, st);
+    if ((rc = launch_gather(xb, at<int>(ws, lo.pair), at<int>(ws, lo.counts), at<int>(ws, lo.offsets), L->e_local, Pcap,
+                            k, H, lo.rows, at<uint16_t>(ws, lo.xperm), st)))
+        return rc;
+    prof_end(kStageGather, st);
+    GroupedArgs a{};
+    a.list = at<int>(ws, lo.gu_list);
+    a.act = at<uint16_t>(ws, lo.xperm);
+    a.act_ld = H;
+    a.w_routed = L->gate_up;
+    a.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
+    a.w_shared = L->shared_gate_up;
+    a.shared_group = L->e_local;
+    a.K_routed = H;
+    a.K_shared = H;
+    a.N_routed = L->ffn;
+    a.N_shared = L->shared_ffn;
+    a.out = at<uint16_t>(ws, lo.hperm);
+    a.out_ld = lo.fmax;
+    prof_begin(kStageGateUp, st);
+    if ((rc = launch_expert_mma(true, a, lo.max_gu, st))) return rc;
+    prof_end(kStageGateUp, st);
+    GroupedArgs d{};
+    d.list = at<int>(ws, lo.dn_list);
+    d.act = at<uint16_t>(ws, lo.hperm);
+    d.act_ld = lo.fmax;
+    d.w_routed = L->down;
+    d.w_routed_stride = (size_t)H * L->ffn / 32 * 20;
+    d.w_shared = L->shared_down;
+    d.shared_group = L->e_local;
+    d.K_routed = L->ffn;
+    d.K_shared = L->shared_ffn;
+    d.N_routed = H;
+    d.N_shared = H;
+    d.out = at<float>(ws, lo.yperm);
+    d.out_ld = H;
+    prof_begin(kStageDown, st);
+    if ((rc = launch_expert_mma(false, d, lo.max_dn, st))) return rc;
+    prof_end(kStageDown, st);
+    prof_begin(kStageCombine, st);
+    rc = launch_combine(res, at<float>(ws, lo.yperm), at<int>(ws, lo.pos), idx, w, sgate, shared_on ? 1 : 0, T,
+                        t_real, k, H, Pcap, out, st);
+    prof_end(kStageCombine, st);
+    return rc;
+}
+
+}  // namespace fm
+
+using namespace fm;
+
+extern "C" FM_API int fm_last_error(char* buf, size_t n) {
+    if (buf && n) {
+        std::strncpy(buf, g_err, n - 1);
+        buf[n - 1] = 0;
+    }
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_version(char* buf, size_t n) {
+    if (buf && n) std::snprintf(buf, n, "flowmoe 0.1 sm_100a");
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_workspace_size(const fm_layer* L, int32_t T, size_t* bytes) {
+    g_err[0] = 0;
+    if (int rc = validate(L, T)) return rc;
+    *bytes = make_layout(L, T).total;
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_router_topk(const fm_layer* L, const void* xm, int32_t xm_dtype, int32_t T, float* probs,
+                              int32_t* idx, float* w, float* shared_gate, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+    g_err[0] = 0;
+    if (int rc = validate(L, T)) return rc;
+    if (T == 0) return FM_OK;
+    const Layout lo = make_layout(L, T);
+    if (int rc = check_ws(lo, workspace, workspace_bytes)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    const uint16_t* xb = nullptr;
+    if (int rc = xm_to_bf16(L, xm, xm_dtype, T, workspace, lo, &xb, st)) return rc;
+    return launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k, at<float>(workspace, lo.logits), probs,
+                         idx, w, shared_gate, st);
+}
+
+extern "C" FM_API int fm_moe_block(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, const int32_t* idx,
+                            const float* w, const float* shared_gate, int32_t T, int32_t t_real, float* out,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+    g_err[0] = 0;
+    if (int rc = validate(L, T)) return rc;
+    if (t_real < 0 || t_real > T) {
+        set_error("t_real %d outside [0, T=%d]", t_real, T);
+        return FM_EINVAL_SHAPE;
+    }
+    if (T == 0) return FM_OK;
+    const Layout lo = make_layout(L, T);
+    if (int rc = check_ws(lo, workspace, workspace_bytes)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    const uint16_t* xb = nullptr;
+    if (int rc = xm_to_bf16(L, xm, xm_dtype, T, workspace, lo, &xb, st)) return rc;
+    return run_block(L, xb, res, idx, w, shared_gate, T, t_real, out, workspace, lo, st);
+}
+
+extern "C" FM_API int fm_moe_layer(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, int32_t T,
+                            int32_t t_real, float* out, int32_t* idx, float* w, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+    g_err[0] = 0;
+    if (int rc = validate(L, T)) return rc;
+    if (t_real < 0 || t_real > T) {
+        set_error("t_real %d outside [0, T=%d]", t_real, T);
+        return FM_EINVAL_SHAPE;
+    }
+    if (T == 0) return FM_OK;
+    const Layout lo = make_layout(L, T);
+    if (int rc = check_ws(lo, workspace, workspace_bytes)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    const uint16_t* xb = nullptr;
+    if (int rc = xm_to_bf16(L, xm, xm_dtype, T, workspace, lo, &xb, st)) return rc;
+    int32_t* ids = idx ? idx : at<int32_t>(workspace, lo.idx);
+    float* ws_w = w ? w : at<float>(workspace, lo.w);
+    float* sg = at<float>(workspace, lo.sgate);
+    prof_begin(kStageRouter, st);
+    if (int rc = launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k, at<float>(workspace, lo.logits),
+                               nullptr, ids, ws_w, sg, st))
+        return rc;
+    prof_end(kStageRouter, st);
+    return run_block(L, xb, res, ids, ws_w, sg, T, t_real, out, workspace, lo, st);
+}
+
+extern "C" FM_API int fm_moe_dispatch(const fm_layer* L, const int32_t* idx, int32_t T, int32_t t_real, int32_t* counts,
+                                       int32_t* offsets, int32_t* pos, int32_t* pair, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+    g_err[0] = 0;
+    if (int rc = validate(L, T)) return rc;
+    if (t_real < 0 || t_real > T) {
+        set_error("t_real %d outside [0, T=%d]", t_real, T);
+        return FM_EINVAL_SHAPE;
+    }
+    if (T == 0) return FM_OK;
+    const Layout lo = make_layout(L, T);
+    if (int rc = check_ws(lo, workspace, workspace_bytes)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int k = L->top_k, P = t_real * k, nblk = (P + kChunk - 1) / kChunk;
+    if (cudaMemsetAsync(at<int>(workspace, lo.err), 0, 16, st) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "memset");
+    if (int rc = launch_dispatch(idx, P, L->e_begin, L->e_local, L->n_experts, lo.P, 0, at<int>(workspace, lo.blk_hist),
+                                 nblk, at<int>(workspace, lo.counts), at<int>(workspace, lo.offsets),
+                                 at<int>(workspace, lo.pos), at<int>(workspace, lo.pair), at<int>(workspace, lo.gu_list),
+                                 L->ffn / kTileRows, 0, at<int>(workspace, lo.dn_list), L->hidden / kTileRows, kBN,
+                                 at<int>(workspace, lo.err), st))
+        return rc;
+    const size_t E = (size_t)L->e_local;
+    cudaError_t e = cudaSuccess;
+    if (counts && e == cudaSuccess) e = cudaMemcpyAsync(counts, at<int>(workspace, lo.counts), E * 4, cudaMemcpyDeviceToDevice, st);
+    if (offsets && e == cudaSuccess)
+        e = cudaMemcpyAsync(offsets, at<int>(workspace, lo.offsets), (E + 1) * 4, cudaMemcpyDeviceToDevice, st);
+    if (pos && P && e == cudaSuccess) e = cudaMemcpyAsync(pos, at<int>(workspace, lo.pos), (size_t)P * 4, cudaMemcpyDeviceToDevice, st);
+    if (pair && P && e == cudaSuccess) e = cudaMemcpyAsync(pair, at<int>(workspace, lo.pair), (size_t)P * 4, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return cuda_status(e, "copy dispatch results");
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_launch_count(unsigned long long* n) {
+    *n = g_launches.load(std::memory_order_relaxed);
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_profile(int32_t enable) {
+    g_err[0] = 0;
+    if (enable && !g_prof.ev[0][0]) {
+        for (auto& p : g_prof.ev)
+            for (auto& e : p)
+                if (cudaEventCreate(&e) != cudaSuccess) return cuda_status(cudaGetLastError(), "cudaEventCreate");
+    }
+    g_prof.on = enable != 0;
+    g_prof.n = 0;
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_profile_read(double* ms, int32_t n_stages) {
+    g_err[0] = 0;
+    for (int i = 0; i < n_stages; ++i) ms[i] = 0.0;
+    for (int i = 0; i < g_prof.n; ++i) {
+        float t = 0.f;
+        if (cudaEventSynchronize(g_prof.ev[i][1]) != cudaSuccess) return cuda_status(cudaGetLastError(), "event sync");
+        if (cudaEventElapsedTime(&t, g_prof.ev[i][0], g_prof.ev[i][1]) != cudaSuccess)
+            return cuda_status(cudaGetLastError(), "event elapsed");
+        if (g_prof.stage[i] < n_stages) ms[g_prof.stage[i]] += t;
+    }
+    g_prof.n = 0;
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_moe_check(void* workspace, void* stream) {
+    g_err[0] = 0;
+    int bad = 0;   // the error counter sits at the start of every workspace layout
+    cudaStream_t st = (cudaStream_t)stream;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return cuda_status(cudaGetLastError(), "stream sync");
+    if (cudaMemcpy(&bad, workspace, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "read error counter");
+    if (bad) {
+        set_error("router produced %d expert index(es) outside the experts this block holds", bad);
+        return FM_EINVAL_EXPERT;
+    }
+    return FM_OK;
+}

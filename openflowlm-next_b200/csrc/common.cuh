@@ -1,0 +1,82 @@
+// Shared device helpers of libflowmoe (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "flowmoe.h"
+
+namespace fm {
+
+constexpr int kTileRows = 128;       // rows of a weight tile (one tcgen05 M=128 band)
+constexpr int kTileK = 64;           // K of a weight tile (two Q4_1 blocks, one 128 B bf16 row)
+constexpr int kTileBytes = 5120;     // 128 rows x (32 nibble bytes + 8 scale bytes)
+constexpr int kTileNibBytes = 4096;  // nibble area of a tile
+constexpr int kMaxTopK = 16;
+
+// Status recorded by the host API for the calling thread.
+void set_error(const char* fmt, ...);
+int cuda_status(cudaError_t e, const char* what);
+
+// Kernel launches made by this library in this process (reported by fm_launch_count).
+void note_launch();
+
+// Launch-error check after each kernel launch: counts the launch, returns FM_ECUDA with the message
+// of the last launch error.
+#define FM_LAUNCH_CHECK(what)                                        \
+    do {                                                             \
+        ::fm::note_launch();                                         \
+        cudaError_t e_ = cudaGetLastError();                         \
+        if (e_ != cudaSuccess) return ::fm::cuda_status(e_, what);   \
+    } while (0)
+
+// Stage timing (fm_profile): CUDA events around each stage on the launching stream.
+enum Stage { kStageToBf16 = 0, kStageRouter, kStageDispatch, kStageGather, kStageGateUp, kStageDown, kStageCombine,
+             kStageCount };
+void prof_begin(int stage, cudaStream_t st);
+void prof_end(int stage, cudaStream_t st);
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+
+// f32 -> bf16 bits, round to nearest even (the reference's f32_to_bf16 / replica_block.bf16_round;
+// NaN is not produced by the block's arithmetic on finite inputs).
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Workspace layout shared by the entry points (byte offsets, 256-aligned). Built on the host.
+struct Workspace {
+    size_t logits;      // f32 [T, E+1]
+    size_t err;         // i32 [4]: [0] bad expert ids seen
+    size_t counts;      // i32 [G] per group rows (G = e_local + 1, the shared expert last)
+    size_t offsets;     // i32 [G + 1]
+    size_t blk_hist;    // i32 [nblk, e_local]
+    size_t pos;         // i32 [T * k]: sorted row of each (token, slot) pair, -1 when skipped
+    size_t pair;        // i32 [T * k]: sorted row -> pair id
+    size_t tiles;       // i32 [max_tiles * 4]: (group, band, row0, nrows) work list + header
+    size_t xperm;       // bf16 [T * k, H] gathered activations, sorted by expert
+    size_t hperm;       // bf16 [T * k + T, F_max] SwiGLU outputs, sorted rows then the shared rows
+    size_t yperm;       // f32 [T * k + T, H] down outputs, same rows as hperm
+    size_t sgate;       // f32 [T] shared gate
+    size_t total;
+    int nblk;
+    int max_tiles;
+};
+
+}  // namespace fm

@@ -1,0 +1,194 @@
+// Grouped Q4_1 expert GEMM on the warp-level tensor-core path (mma.sync m16n8k16 bf16).
+//
+// The general-size kernel and the correctness baseline for the tcgen05 kernel: one CTA per work
+// item (group, 128-row band, up to 64 sorted rows), K walked in 64-wide slabs. Each slab's weight
+// tile (5120 B) is staged in shared memory and dequantised in registers straight into mma A
+// fragments: w = q * d + m in f32 with the fp16 d/m widened exactly, rounded once to bf16 (the
+// reference's "Q4_1 nibble -> bf16" of designs/moe_batch/moe_batch.h:98-137, with exact scales).
+//   GATE_UP: two weight tiles (gate rows, up rows) share the activation tile; the epilogue is
+//            h = bf16(silu(g) * u) (moe_batch.h:181-202, designs/moe_batch/make_test.py:96).
+//   DOWN:    y rows in f32 (the reference's C tiles, core.cpp:5230-5255 reads them back as f32).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace fm {
+
+constexpr int XM_BN = 64;               // sorted rows per work item
+constexpr int XM_LDB = kTileK + 8;      // padded bf16 row of the activation tile
+
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Two adjacent K values of one row from a 16-bit nibble word u (bytes j, j+1 of a block's 16
+// nibble bytes): hi == 0 -> values j, j+1 (low nibbles), hi == 1 -> values j+16, j+17.
+__device__ __forceinline__ uint32_t deq_pair(uint32_t u, int hi, float d, float m) {
+    const int sh = hi ? 4 : 0;
+    const float q0 = (float)((u >> sh) & 0xF), q1 = (float)((u >> (8 + sh)) & 0xF);
+    return pack_bf16x2(fmaf(q0, d, m), fmaf(q1, d, m));
+}
+
+// A fragments (m16n8k16 row-major) for the warp's 16 rows, k16 step kk of the slab.
+// Slab k = kk*16 + {2c, 2c+1, 2c+8, 2c+9}: block kk/2, values j = k % 32 -> byte j % 16, high
+// nibble when j >= 16 (kk odd).
+__device__ __forceinline__ void load_a_frag(const uint8_t* tile, int r0, int g, int c, int kk, uint32_t* a) {
+    const int blk = kk >> 1, hi = kk & 1;
+    const uint8_t* nibA = tile + (r0 + g) * 32 + blk * 16;
+    const uint8_t* nibB = tile + (r0 + g + 8) * 32 + blk * 16;
+    const __half2 scA = *reinterpret_cast<const __half2*>(tile + kTileNibBytes + (r0 + g) * 8 + blk * 4);
+    const __half2 scB = *reinterpret_cast<const __half2*>(tile + kTileNibBytes + (r0 + g + 8) * 8 + blk * 4);
+    const float dA = __low2float(scA), mA = __high2float(scA);
+    const float dB = __low2float(scB), mB = __high2float(scB);
+    const uint32_t uA0 = *reinterpret_cast<const uint16_t*>(nibA + 2 * c);
+    const uint32_t uA1 = *reinterpret_cast<const uint16_t*>(nibA + 2 * c + 8);
+    const uint32_t uB0 = *reinterpret_cast<const uint16_t*>(nibB + 2 * c);
+    const uint32_t uB1 = *reinterpret_cast<const uint16_t*>(nibB + 2 * c + 8);
+    a[0] = deq_pair(uA0, hi, dA, mA);
+    a[1] = deq_pair(uB0, hi, dB, mB);
+    a[2] = deq_pair(uA1, hi, dA, mA);
+    a[3] = deq_pair(uB1, hi, dB, mB);
+}
+
+
+template <bool GATE_UP>
+__global__ void __launch_bounds__(256) expert_mma_kernel(GroupedArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* wt = smem;                                                   // 1 or 2 weight tiles
+    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + (GATE_UP ? 2 : 1) * kTileBytes);   // [64][72]
+    const int n_items = a.list[0];
+    if ((int)blockIdx.x >= n_items) return;
+    const int4 it = reinterpret_cast<const int4*>(a.list + 4)[blockIdx.x];
+    const int g = it.x, band = it.y, row0 = it.z, nrows = it.w;
+    const bool sh = g == a.shared_group;
+    const int K = sh ? a.K_shared : a.K_routed;
+    const int N = sh ? a.N_shared : a.N_routed;
+    const uint8_t* wbase = sh ? a.w_shared : a.w_routed + (size_t)g * a.w_routed_stride;
+    const int slabs = K / kTileK;
+    const uint8_t* wg = wbase + (size_t)band * slabs * kTileBytes;              // gate (or down) band
+    const uint8_t* wu = wg + (size_t)N * K / 32 * 20;                           // up band (GATE_UP)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, cq = lane & 3;
+    float accg[8][4] = {}, accu[8][4] = {};
+    for (int s = 0; s < slabs; ++s) {
+        const uint4* src_g = reinterpret_cast<const uint4*>(wg + (size_t)s * kTileBytes);
+        for (int i = threadIdx.x; i < kTileBytes / 16; i += 256) {
+            reinterpret_cast<uint4*>(wt)[i] = src_g[i];
+            if (GATE_UP)
+                reinterpret_cast<uint4*>(wt + kTileBytes)[i] =
+                    reinterpret_cast<const uint4*>(wu + (size_t)s * kTileBytes)[i];
+        }
+        for (int i = threadIdx.x; i < XM_BN * 8; i += 256) {
+            const int r = i >> 3, q = i & 7;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r < nrows) v = *reinterpret_cast<const uint4*>(a.act + (size_t)(row0 + r) * a.act_ld + s * kTileK + q * 8);
+            *reinterpret_cast<uint4*>(xs + r * XM_LDB + q * 8) = v;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t ag[4], au[4];
+            load_a_frag(wt, warp * 16, gq, cq, kk, ag);
+            if (GATE_UP) load_a_frag(wt + kTileBytes, warp * 16, gq, cq, kk, au);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint16_t* xr = xs + (j * 8 + gq) * XM_LDB + kk * 16 + 2 * cq;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xr);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(xr + 8);
+                mma16816(accg[j], ag, b0, b1);
+                if (GATE_UP) mma16816(accu[j], au, b0, b1);
+            }
+        }
+        __syncthreads();
+    }
+    // C fragment: c0,c1 = (row gq, cols 2cq, 2cq+1), c2,c3 = (row gq+8, same cols); row = weight row
+    // (output feature), col = sorted activation row.
+    const int f0 = band * kTileRows + warp * 16 + gq;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const int n = j * 8 + 2 * cq + (h & 1);
+            const int f = f0 + (h >> 1) * 8;
+            if (n >= nrows) continue;
+            if (GATE_UP) {
+                const float v = silu_f(accg[j][h]) * accu[j][h];
+                reinterpret_cast<uint16_t*>(a.out)[(size_t)(row0 + n) * a.out_ld + f] = f32_to_bf16_bits(v);
+            } else {
+                reinterpret_cast<float*>(a.out)[(size_t)(row0 + n) * a.out_ld + f] = accg[j][h];
+            }
+        }
+    }
+}
+
+int launch_expert_mma(bool gate_up, const GroupedArgs& a, int max_items, cudaStream_t st) {
+    if (max_items <= 0) return FM_OK;
+    const size_t sm = (gate_up ? 2 : 1) * kTileBytes + XM_BN * XM_LDB * 2;
+    if (gate_up) expert_mma_kernel<true><<<max_items, 256, sm, st>>>(a);
+    else expert_mma_kernel<false><<<max_items, 256, sm, st>>>(a);
+    FM_LAUNCH_CHECK(gate_up ? "expert_mma<gate_up>" : "expert_mma<down>");
+    return FM_OK;
+}
+
+// out[t] = res[t] + sgate[t] * y[P + t] + sum over t's pairs in ascending expert order of w * y[pos].
+// Rows t >= t_real: out = res. One block per token, 256 threads x float4.
+__global__ void combine_kernel(const float* __restrict__ res, const float* __restrict__ y, const int* __restrict__ pos,
+                               const int32_t* __restrict__ idx, const float* __restrict__ w,
+                               const float* __restrict__ sgate, int shared_on, int T, int t_real, int k, int H, int P,
+                               float* __restrict__ out) {
+    const int t = blockIdx.x;
+    __shared__ int srow[kMaxTopK];
+    __shared__ float sw[kMaxTopK];
+    __shared__ int n_sel;
+    if (threadIdx.x == 0) {
+        int n = 0;
+        if (t < t_real) {
+            // insertion order by expert id (ascending), the visit order of core.cpp:5163-5165
+            int ord[kMaxTopK], ids[kMaxTopK];
+            for (int s = 0; s < k; ++s) {
+                const int e = idx[(size_t)t * k + s];
+                int j = n;
+                while (j > 0 && ids[j - 1] > e) { ids[j] = ids[j - 1]; ord[j] = ord[j - 1]; --j; }
+                ids[j] = e;
+                ord[j] = s;
+                ++n;
+            }
+            int m = 0;
+            for (int j = 0; j < n; ++j) {
+                const int p = pos[(size_t)t * k + ord[j]];
+                if (p >= 0) { srow[m] = p; sw[m] = w[(size_t)t * k + ord[j]]; ++m; }
+            }
+            n = m;
+        }
+        n_sel = n;
+    }
+    __syncthreads();
+    const int n = n_sel;
+    const float g = (t < t_real && shared_on) ? sgate[t] : 0.0f;
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+        float4 o = reinterpret_cast<const float4*>(res + (size_t)t * H)[i];
+        if (t < t_real) {
+            if (shared_on) {
+                const float4 v = reinterpret_cast<const float4*>(y + (size_t)(P + t) * H)[i];
+                o.x += g * v.x; o.y += g * v.y; o.z += g * v.z; o.w += g * v.w;
+            }
+            for (int j = 0; j < n; ++j) {
+                const float4 v = reinterpret_cast<const float4*>(y + (size_t)srow[j] * H)[i];
+                const float ww = sw[j];
+                o.x += ww * v.x; o.y += ww * v.y; o.z += ww * v.z; o.w += ww * v.w;
+            }
+        }
+        reinterpret_cast<float4*>(out + (size_t)t * H)[i] = o;
+    }
+}
+
+int launch_combine(const float* res, const float* y, const int* pos, const int32_t* idx, const float* w,
+                   const float* sgate, int shared_on, int T, int t_real, int k, int H, int P, float* out, cudaStream_t st) {
+    if (T <= 0) return FM_OK;
+    combine_kernel<<<T, 256, 0, st>>>(res, y, pos, idx, w, sgate, shared_on, T, t_real, k, H, P, out);
+    FM_LAUNCH_CHECK("combine");
+    return FM_OK;
+}
+
+}  // namespace fm

@@ -1,0 +1,35 @@
+// Host-side launch wrappers of the kernels (router.cu, dispatch.cu, expert_mma.cu). Each returns an
+// FM_* status and records the message with set_error on failure.
+#pragma once
+#include "common.cuh"
+
+namespace fm {
+
+int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st);
+int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
+                  float* logits, float* probs, int32_t* idx, float* w, float* sgate, cudaStream_t st);
+int launch_dispatch(const int32_t* idx, int P, int e_begin, int e_local, int E, int shared_base, int shared_rows,
+                    int* blk_hist, int nblk,
+                    int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
+                    int* dn_list, int dn_bands, int bn, int* err, cudaStream_t st);
+int launch_gather(const uint16_t* xb, const int* pair, const int* counts, const int* offsets, int e_local, int shared_base,
+                  int k, int H, int max_rows, uint16_t* xperm, cudaStream_t st);
+struct GroupedArgs {
+    const int* list;
+    const uint16_t* act;
+    int act_ld;
+    const uint8_t* w_routed;
+    size_t w_routed_stride;
+    const uint8_t* w_shared;
+    int shared_group;
+    int K_routed, K_shared;
+    int N_routed, N_shared;
+    void* out;
+    int out_ld;
+};
+int launch_expert_mma(bool gate_up, const GroupedArgs& a, int max_items, cudaStream_t st);
+int launch_combine(const float* res, const float* y, const int* pos, const int32_t* idx, const float* w,
+                   const float* sgate, int shared_on, int T, int t_real, int k, int H, int P, float* out, cudaStream_t st);
+
+
+}  // namespace fm

@@ -1,0 +1,168 @@
+// Router: logits GEMM (bf16 x bf16 -> f32 on the tensor cores) and the per-token softmax / top-k.
+//
+// Follows host::router_block (src/open_qwen36/block_host.cpp:766-803): float logits, max
+// subtraction, float exp with a double denominator, p = e * float(1/denom), top-k by probability
+// (strictly greater wins, so the lowest index wins a tie), weights renormalised by a double sum.
+// The shared-expert gate (core.cpp:4370-4373) rides along as router row E.
+#include "common.cuh"
+
+namespace fm {
+
+// xb[t][h] = bf16(xm[t][h]) for f32 input (the rounding the reference applies at the device
+// boundary, core.cpp:5204).
+__global__ void to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict__ xb, long long n4) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        uint2 o;
+        o.x = pack_bf16x2(v.x, v.y);
+        o.y = pack_bf16x2(v.z, v.w);
+        reinterpret_cast<uint2*>(xb)[i] = o;
+    }
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, const uint32_t* b) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// C[M, N] (ldc) = A[M, K] . B[N, K]^T, bf16 in, f32 out. 64x64 CTA tile, 4 warps of 32x32, K step 32.
+// K % 32 == 0. A plain tensor-core GEMM: the router is ~2% of the block's FLOPs.
+constexpr int RG_BM = 64, RG_BN = 64, RG_BK = 32, RG_LD = RG_BK + 8;
+
+__global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __restrict__ A, const uint16_t* __restrict__ B,
+                                                            float* __restrict__ C, int M, int N, int K, int ldc) {
+    __shared__ __align__(16) uint16_t sa[RG_BM][RG_LD];
+    __shared__ __align__(16) uint16_t sb[RG_BN][RG_LD];
+    const int m0 = blockIdx.y * RG_BM, n0 = blockIdx.x * RG_BN;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
+    const int g = lane >> 2, c = lane & 3;
+    float acc[2][4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += RG_BK) {
+        // 64 rows x 32 K bf16 = 64 x 4 uint4 per operand; 128 threads -> 2 each
+        for (int i = threadIdx.x; i < RG_BM * 4; i += 128) {
+            const int r = i >> 2, q = i & 3;
+            uint4 va = make_uint4(0, 0, 0, 0), vb = make_uint4(0, 0, 0, 0);
+            if (m0 + r < M) va = *reinterpret_cast<const uint4*>(A + (size_t)(m0 + r) * K + k0 + q * 8);
+            if (n0 + r < N) vb = *reinterpret_cast<const uint4*>(B + (size_t)(n0 + r) * K + k0 + q * 8);
+            *reinterpret_cast<uint4*>(&sa[r][q * 8]) = va;
+            *reinterpret_cast<uint4*>(&sb[r][q * 8]) = vb;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < RG_BK; kk += 16) {
+            uint32_t af[2][4], bf[4][2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int r = wm + i * 16 + g;
+                af[i][0] = *reinterpret_cast<const uint32_t*>(&sa[r][kk + 2 * c]);
+                af[i][1] = *reinterpret_cast<const uint32_t*>(&sa[r + 8][kk + 2 * c]);
+                af[i][2] = *reinterpret_cast<const uint32_t*>(&sa[r][kk + 2 * c + 8]);
+                af[i][3] = *reinterpret_cast<const uint32_t*>(&sa[r + 8][kk + 2 * c + 8]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int n = wn + j * 8 + g;
+                bf[j][0] = *reinterpret_cast<const uint32_t*>(&sb[n][kk + 2 * c]);
+                bf[j][1] = *reinterpret_cast<const uint32_t*>(&sb[n][kk + 2 * c + 8]);
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) mma_bf16_16816(acc[i][j], af[i], bf[j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int r = m0 + wm + i * 16 + g, n = n0 + wn + j * 8 + 2 * c;
+            if (r < M) {
+                if (n < N) C[(size_t)r * ldc + n] = acc[i][j][0];
+                if (n + 1 < N) C[(size_t)r * ldc + n + 1] = acc[i][j][1];
+            }
+            if (r + 8 < M) {
+                if (n < N) C[(size_t)(r + 8) * ldc + n] = acc[i][j][2];
+                if (n + 1 < N) C[(size_t)(r + 8) * ldc + n + 1] = acc[i][j][3];
+            }
+        }
+}
+
+// One warp per token. logits row has E + 1 entries (the last is the shared-gate logit).
+__global__ void router_topk_kernel(float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
+                                   float* __restrict__ probs, int32_t* __restrict__ idx, float* __restrict__ w,
+                                   float* __restrict__ sgate) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    float* lg = logits + (size_t)warp * (E + 1);
+    if (bias) {
+        for (int e = lane; e < E; e += 32) lg[e] += bias[e];
+        __syncwarp();
+    }
+    float mx = -1e30f;
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    double den = 0.0;
+    for (int e = lane; e < E; e += 32) den += (double)expf(lg[e] - mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    const float inv = (float)(1.0 / den);
+    if (probs)
+        for (int e = lane; e < E; e += 32) probs[(size_t)warp * E + e] = expf(lg[e] - mx) * inv;
+    // top-k: k rounds of a warp arg-max over the untaken experts (p strictly greater wins; equal p
+    // keeps the lower index). A lane owns experts lane, lane + 32, ...; `taken` bit i = expert lane+32i.
+    uint32_t taken = 0;
+    float ws[kMaxTopK];
+    int ids[kMaxTopK];
+    double wsum = 0.0;
+    for (int s = 0; s < k; ++s) {
+        float bp = -1.0f;
+        int be = 0x7fffffff;
+        for (int i = 0, e = lane; e < E; ++i, e += 32) {
+            if (taken >> i & 1u) continue;
+            const float p = expf(lg[e] - mx) * inv;
+            if (p > bp) { bp = p; be = e; }   // ascending e within a lane: ties keep the lower index
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (op > bp || (op == bp && oe < be)) { bp = op; be = oe; }
+        }
+        if ((be & 31) == lane) taken |= 1u << (be >> 5);
+        ids[s] = be;
+        ws[s] = bp;
+        wsum += (double)bp;
+    }
+    if (lane == 0) {
+        for (int s = 0; s < k; ++s) {
+            idx[(size_t)warp * k + s] = ids[s];
+            w[(size_t)warp * k + s] = (float)((double)ws[s] / wsum);
+        }
+        if (sgate) sgate[warp] = 1.0f / (1.0f + expf(-lg[E]));
+    }
+}
+
+int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st) {
+    const long long n4 = n / 4;
+    const int grid = (int)((n4 + 255) / 256 < 2048 ? (n4 + 255) / 256 : 2048);
+    to_bf16_kernel<<<grid > 0 ? grid : 1, 256, 0, st>>>(x, xb, n4);
+    FM_LAUNCH_CHECK("to_bf16");
+    return FM_OK;
+}
+
+int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
+                  float* logits, float* probs, int32_t* idx, float* w, float* sgate, cudaStream_t st) {
+    dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM);
+    router_logits_kernel<<<grid, 128, 0, st>>>(xb, router, logits, T, E + 1, H, E + 1);
+    FM_LAUNCH_CHECK("router_logits");
+    router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, E, k, probs, idx, w, sgate);
+    FM_LAUNCH_CHECK("router_topk");
+    return FM_OK;
+}
+
+}  // namespace fm

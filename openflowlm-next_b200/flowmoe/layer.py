@@ -1,0 +1,272 @@
+"""The drop-in host API of the MoE expert block.
+
+Mirrors the reference's engine boundary for this path:
+  * ``router_block(xm, Wr, topk) -> (probs, idx, w)``  -- ``host::router_block``
+    (src/open_qwen36/block_host.hpp:155-159) / ``replica_block.router_block``
+    (open_kernels/model/replica_block.py:160-169);
+  * ``MoELayer.moe_block(xm, res, idx, w, t_real)``   -- ``Core::moe_block`` (core.hpp:844-848), with
+    the gated shared expert of ``Core::ffn_block`` (core.cpp:4342-4380) folded in;
+  * ``MoELayer.forward(xm, res, t_real)``             -- router + shared + experts (core.cpp:4934-4957,
+    :3685-3700).
+Weights are accepted in the reference's GGUF Q4_1 block layout (``q4_1_pack.random_q4_1_blocks`` /
+``gguf_pool.unpack_q4`` shape ``uint8[rows, K/32, 20]``). Torch tensors appear only here, at the
+boundary: device memory and the current stream are handed to libflowmoe as raw pointers.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import FM_BF16, FM_F32, FmLayer, call
+
+Q4_1_BYTES = 20
+
+
+@dataclass(frozen=True)
+class MoEConfig:
+    """The layer geometry (C30 = 2048/128/8/768/0, C36 = 2048/256/8/512/512)."""
+    hidden: int = 2048
+    n_experts: int = 128
+    top_k: int = 8
+    ffn: int = 768
+    shared_ffn: int = 0
+    e_begin: int = 0
+    e_local: int | None = None      # None: all experts (one GPU)
+
+    @property
+    def local(self) -> int:
+        return self.n_experts if self.e_local is None else self.e_local
+
+    def q4_bytes(self, rows: int, k: int) -> int:
+        return rows * k // 32 * Q4_1_BYTES
+
+    @property
+    def gate_up_bytes(self) -> int:
+        return 2 * self.q4_bytes(self.ffn, self.hidden)
+
+    @property
+    def down_bytes(self) -> int:
+        return self.q4_bytes(self.hidden, self.ffn)
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _as_dev_u8(blocks, device) -> torch.Tensor:
+    if isinstance(blocks, np.ndarray):
+        blocks = torch.from_numpy(np.ascontiguousarray(blocks, np.uint8))
+    return blocks.to(device=device, dtype=torch.uint8).contiguous()
+
+
+def q4_1_to_tiles(blocks, rows: int, k: int, device="cuda", out: torch.Tensor | None = None) -> torch.Tensor:
+    """GGUF Q4_1 blocks (numpy or torch, any leading expert dims) -> the device tile layout, per matrix."""
+    src = _as_dev_u8(blocks, device).reshape(-1)
+    per = rows * k // 32 * Q4_1_BYTES
+    if src.numel() % per:
+        raise ValueError(f"{src.numel()} block bytes is not a whole number of [{rows}, {k}] matrices")
+    dst = torch.empty_like(src) if out is None else out.reshape(-1)
+    st = _stream(src.device)
+    for i in range(src.numel() // per):
+        call("fm_q4_1_to_tiles", src[i * per:].data_ptr(), rows, k, dst[i * per:].data_ptr(), st)
+    return dst
+
+
+def tiles_to_q4_1(tiles: torch.Tensor, rows: int, k: int) -> torch.Tensor:
+    """The inverse permutation (tile layout -> GGUF blocks), per matrix."""
+    src = tiles.reshape(-1)
+    per = rows * k // 32 * Q4_1_BYTES
+    dst = torch.empty_like(src)
+    st = _stream(src.device)
+    for i in range(src.numel() // per):
+        call("fm_tiles_to_q4_1", src[i * per:].data_ptr(), rows, k, dst[i * per:].data_ptr(), st)
+    return dst
+
+
+def _bf16(t, device) -> torch.Tensor:
+    if isinstance(t, np.ndarray):
+        if t.dtype == np.uint16:
+            return torch.from_numpy(t.astype(np.int16, copy=False).view(np.int16)).view(torch.bfloat16).to(device)
+        t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
+    return t.to(device=device, dtype=torch.bfloat16).contiguous()
+
+
+class MoELayer:
+    """One Qwen3.6-MoE expert block resident on a B200: router, routed experts, shared expert."""
+
+    def __init__(self, cfg: MoEConfig, gate_up: torch.Tensor, down: torch.Tensor, router: torch.Tensor,
+                 shared_gate_up: torch.Tensor | None = None, shared_down: torch.Tensor | None = None,
+                 router_bias: torch.Tensor | None = None):
+        self.cfg = cfg
+        self.device = router.device
+        self.gate_up, self.down, self.router = gate_up, down, router
+        self.shared_gate_up, self.shared_down = shared_gate_up, shared_down
+        self.router_bias = None if router_bias is None else router_bias.to(self.device, torch.float32).contiguous()
+        self._L = FmLayer(cfg.hidden, cfg.n_experts, cfg.top_k, cfg.ffn, cfg.shared_ffn, cfg.e_begin, cfg.local, 0,
+                          gate_up.data_ptr(), down.data_ptr(), _ptr(shared_gate_up), _ptr(shared_down),
+                          router.data_ptr(), _ptr(self.router_bias))
+        self._ws: torch.Tensor | None = None
+
+    # ---- construction from the reference's block layout
+    @classmethod
+    def from_q4_1(cls, cfg: MoEConfig, gate_blocks, up_blocks, down_blocks, router_w, shared=None, device="cuda",
+                  router_bias=None):
+        """gate/up blocks [E_local, F, H/32, 20], down [E_local, H, F/32, 20] (numpy or torch uint8),
+        router_w [H, E] (bf16 values), shared = (gate, up, down blocks, sgw [H]) or None,
+        router_bias [E] f32 added to the logits (or None)."""
+        H, F, E = cfg.hidden, cfg.ffn, cfg.local
+        g = _as_dev_u8(gate_blocks, device).reshape(E, -1)
+        u = _as_dev_u8(up_blocks, device).reshape(E, -1)
+        if g.shape[1] != cfg.q4_bytes(F, H) or u.shape[1] != cfg.q4_bytes(F, H):
+            raise ValueError("gate/up blocks do not match [E_local, F, H/32, 20]")
+        gate_up = torch.empty(E, cfg.gate_up_bytes, dtype=torch.uint8, device=device)
+        half = cfg.q4_bytes(F, H)
+        tg = q4_1_to_tiles(g, F, H, device).reshape(E, half)
+        tu = q4_1_to_tiles(u, F, H, device).reshape(E, half)
+        gate_up[:, :half] = tg
+        gate_up[:, half:] = tu
+        down = q4_1_to_tiles(_as_dev_u8(down_blocks, device), H, F, device).reshape(E, -1)
+        if down.shape[1] != cfg.down_bytes:
+            raise ValueError("down blocks do not match [E_local, H, F/32, 20]")
+        sgu = sdn = None
+        sgw = None
+        if shared is not None:
+            if cfg.shared_ffn <= 0:
+                raise ValueError("shared expert weights given but cfg.shared_ffn == 0")
+            sg, su, sd, sgw = shared
+            FS = cfg.shared_ffn
+            sgu = torch.cat([q4_1_to_tiles(sg, FS, H, device), q4_1_to_tiles(su, FS, H, device)])
+            sdn = q4_1_to_tiles(sd, H, FS, device)
+        wr = _bf16(router_w, device)
+        if tuple(wr.shape) != (H, cfg.n_experts):
+            raise ValueError(f"router weight shape {tuple(wr.shape)} != (H, E) = {(H, cfg.n_experts)}")
+        router = torch.empty(cfg.n_experts + 1, H, dtype=torch.bfloat16, device=device)
+        sgw_t = None if sgw is None else _bf16(sgw, device).reshape(H)
+        call("fm_router_pack", wr.data_ptr(), _ptr(sgw_t), H, cfg.n_experts, router.data_ptr(), _stream(device))
+        if router_bias is not None and not isinstance(router_bias, torch.Tensor):
+            router_bias = torch.from_numpy(np.asarray(router_bias, np.float32))
+        return cls(cfg, gate_up.reshape(-1), down.reshape(-1), router, sgu, sdn, router_bias)
+
+    # ---- workspace
+    def workspace_bytes(self, T: int) -> int:
+        n = ctypes.c_size_t(0)
+        call("fm_workspace_size", ctypes.byref(self._L), T, ctypes.byref(n))
+        return n.value
+
+    def workspace(self, T: int) -> torch.Tensor:
+        need = self.workspace_bytes(T)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    @staticmethod
+    def _dtype(xm: torch.Tensor) -> int:
+        if xm.dtype == torch.float32:
+            return FM_F32
+        if xm.dtype == torch.bfloat16:
+            return FM_BF16
+        raise TypeError(f"xm must be float32 or bfloat16, not {xm.dtype}")
+
+    def _check_x(self, xm: torch.Tensor):
+        if xm.device != self.device or xm.dim() != 2 or xm.shape[1] != self.cfg.hidden or not xm.is_contiguous():
+            raise ValueError(f"xm must be a contiguous [T, {self.cfg.hidden}] tensor on {self.device}")
+
+    # ---- the reference's entry points
+    def router_block(self, xm: torch.Tensor, want_probs: bool = True):
+        """(probs [T, E] f32, idx [T, k] int32, w [T, k] f32): softmax top-k, lowest index on a tie."""
+        self._check_x(xm)
+        T, E, k = xm.shape[0], self.cfg.n_experts, self.cfg.top_k
+        probs = torch.empty(T, E, dtype=torch.float32, device=self.device) if want_probs else None
+        idx = torch.empty(T, k, dtype=torch.int32, device=self.device)
+        w = torch.empty(T, k, dtype=torch.float32, device=self.device)
+        self.shared_gate_buf = torch.empty(T, dtype=torch.float32, device=self.device)
+        ws = self.workspace(T)
+        call("fm_router_topk", ctypes.byref(self._L), xm.data_ptr(), self._dtype(xm), T, _ptr(probs), idx.data_ptr(),
+             w.data_ptr(), self.shared_gate_buf.data_ptr(), ws.data_ptr(), ws.numel(), _stream(self.device))
+        return probs, idx, w
+
+    def shared_gate(self, xm: torch.Tensor) -> torch.Tensor:
+        """sigmoid(bf16(xm) . sgw) per token (core.cpp:4370-4373)."""
+        self.router_block(xm, want_probs=False)
+        return self.shared_gate_buf
+
+    def moe_block(self, xm: torch.Tensor, res: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
+                  t_real: int | None = None, shared_gate: torch.Tensor | None = None, check: bool = True,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+        """out = res + shared_gate * shared(xm) + sum_e w_e * expert_e(xm), ascending expert order.
+        ``check`` synchronises and raises on expert ids outside [e_begin, e_begin + e_local)
+        (the reference throws, core.cpp:5159-5160)."""
+        self._check_x(xm)
+        T = xm.shape[0]
+        t_real = T if t_real is None else t_real
+        for name, t, dt, shape in (("res", res, torch.float32, (T, self.cfg.hidden)),
+                                   ("idx", idx, torch.int32, (T, self.cfg.top_k)),
+                                   ("w", w, torch.float32, (T, self.cfg.top_k))):
+            if t.dtype != dt or tuple(t.shape) != shape or not t.is_contiguous() or t.device != self.device:
+                raise ValueError(f"{name} must be a contiguous {dt} tensor of shape {shape} on {self.device}")
+        out = torch.empty_like(res) if out is None else out
+        ws = self.workspace(T)
+        st = _stream(self.device)
+        call("fm_moe_block", ctypes.byref(self._L), xm.data_ptr(), self._dtype(xm), res.data_ptr(), idx.data_ptr(),
+             w.data_ptr(), _ptr(shared_gate), T, t_real, out.data_ptr(), ws.data_ptr(), ws.numel(), st)
+        if check:
+            call("fm_moe_check", ws.data_ptr(), st)
+        return out
+
+    def dispatch(self, idx: torch.Tensor, t_real: int | None = None):
+        """(counts [e_local], offsets [e_local + 1], pos [t_real, k], pair [P]) of the stable
+        expert-sorted order (the owed lists and ascending visits of core.cpp:5155-5165)."""
+        T, k = idx.shape
+        t_real = T if t_real is None else t_real
+        E = self.cfg.local
+        counts = torch.empty(E, dtype=torch.int32, device=self.device)
+        offsets = torch.empty(E + 1, dtype=torch.int32, device=self.device)
+        pos = torch.empty(t_real, k, dtype=torch.int32, device=self.device)
+        pair = torch.empty(max(t_real * k, 1), dtype=torch.int32, device=self.device)
+        ws = self.workspace(T)
+        call("fm_moe_dispatch", ctypes.byref(self._L), idx.data_ptr(), T, t_real, counts.data_ptr(),
+             offsets.data_ptr(), pos.data_ptr(), pair.data_ptr(), ws.data_ptr(), ws.numel(), _stream(self.device))
+        torch.cuda.current_stream(self.device).synchronize()
+        return counts, offsets, pos, pair[:int(offsets[-1].item())]
+
+    def forward(self, xm: torch.Tensor, res: torch.Tensor, t_real: int | None = None, out: torch.Tensor | None = None,
+                idx: torch.Tensor | None = None, w: torch.Tensor | None = None) -> torch.Tensor:
+        """Router + shared expert + routed experts (fm_moe_layer)."""
+        self._check_x(xm)
+        T = xm.shape[0]
+        t_real = T if t_real is None else t_real
+        out = torch.empty(T, self.cfg.hidden, dtype=torch.float32, device=self.device) if out is None else out
+        ws = self.workspace(T)
+        call("fm_moe_layer", ctypes.byref(self._L), xm.data_ptr(), self._dtype(xm), res.data_ptr(), T, t_real,
+             out.data_ptr(), _ptr(idx), _ptr(w), ws.data_ptr(), ws.numel(), _stream(self.device))
+        return out
+
+    __call__ = forward
+
+
+def router_block(xm: torch.Tensor, Wr: torch.Tensor, topk: int):
+    """Functional ``host::router_block``: (probs, idx, w) for xm [T, H] and Wr [H, E] on the device.
+    H is zero-padded to a multiple of 128 (exact for the dot products)."""
+    H0, E = Wr.shape
+    if topk > E:
+        raise _lib.FlowMoeError(_lib.FM_EINVAL_SHAPE, "router_block: topk past the expert count")
+    H = (H0 + 127) // 128 * 128
+    dev = xm.device
+    if H != H0:
+        xm = torch.nn.functional.pad(xm, (0, H - H0))
+        Wr = torch.nn.functional.pad(Wr, (0, 0, 0, H - H0))
+    cfg = MoEConfig(hidden=H, n_experts=E, top_k=topk, ffn=128, shared_ffn=0)
+    router = torch.empty(E + 1, H, dtype=torch.bfloat16, device=dev)
+    wr = Wr.to(torch.bfloat16).contiguous()
+    call("fm_router_pack", wr.data_ptr(), None, H, E, router.data_ptr(), _stream(dev))
+    dummy = torch.empty(256, dtype=torch.uint8, device=dev)
+    layer = MoELayer(cfg, dummy, dummy, router)
+    return layer.router_block(xm.contiguous())

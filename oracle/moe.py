@@ -51,7 +51,7 @@ def sigmoid(x):
     return 1 / (1 + np.exp(-x))
 
 
-def router_block(xm: np.ndarray, Wr: np.ndarray, topk: int):
+def router_block(xm: np.ndarray, Wr: np.ndarray, topk: int, bias: np.ndarray | None = None):
     """(probs [T, E], idx int32 [T, topk], w [T, topk]) in fp64.
 
     ``open_kernels/model/replica_block.py:160-169``: softmax over the experts, top-k by probability
@@ -61,6 +61,8 @@ def router_block(xm: np.ndarray, Wr: np.ndarray, topk: int):
     if topk > Wr.shape[1]:
         raise ValueError("router_block: topk past the expert count")   # block_host.cpp:768
     lg = np.asarray(xm, np.float64) @ np.asarray(Wr, np.float64)
+    if bias is not None:   # the synthetic Zipf skew of the prefill configs (not in the reference)
+        lg = lg + np.asarray(bias, np.float64)
     p = np.exp(lg - lg.max(-1, keepdims=True))
     p /= p.sum(-1, keepdims=True)
     idx = np.argsort(-p, axis=-1, kind="stable")[:, :topk]
@@ -69,9 +71,11 @@ def router_block(xm: np.ndarray, Wr: np.ndarray, topk: int):
     return p, idx.astype(np.int32), w
 
 
-def router_margins(xm: np.ndarray, Wr: np.ndarray, topk: int) -> np.ndarray:
+def router_margins(xm: np.ndarray, Wr: np.ndarray, topk: int, bias: np.ndarray | None = None) -> np.ndarray:
     """Per token, p[k-th] - p[(k+1)-th] (fp64): where this exceeds 1e-3 the ids must be bit-exact."""
     lg = np.asarray(xm, np.float64) @ np.asarray(Wr, np.float64)
+    if bias is not None:
+        lg = lg + np.asarray(bias, np.float64)
     p = np.exp(lg - lg.max(-1, keepdims=True))
     p /= p.sum(-1, keepdims=True)
     ps = -np.sort(-p, axis=-1)

@@ -1,0 +1,77 @@
+"""The C-ABI library loads and exports what include/flowmoe.h declares; host-side argument checks
+(no GPU needed: every call here fails validation before any device work)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared():
+    txt = (ROOT / "include" / "flowmoe.h").read_text()
+    return sorted(set(re.findall(r"FM_API int (fm_\w+)\(", txt)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "fm_moe_block" in names and "fm_router_topk" in names and len(names) >= 10
+
+
+def test_library_exports_every_declared_symbol():
+    from flowmoe import _lib
+    so = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in _declared() if not hasattr(so, n)]
+    assert not missing, missing
+    assert set(_declared()) == set(_lib.SIGNATURES), "ctypes signatures out of step with the header"
+
+
+def test_version_and_error_buffer():
+    from flowmoe import _lib
+    buf = ctypes.create_string_buffer(64)
+    assert _lib.lib.fm_version(buf, 64) == 0 and b"sm_100a" in buf.value
+
+
+def _layer(**kw):
+    from flowmoe._lib import FmLayer
+    g = dict(hidden=2048, n_experts=128, top_k=8, ffn=768, shared_ffn=0, e_begin=0, e_local=128, flags=0)
+    g.update(kw)
+    return FmLayer(g["hidden"], g["n_experts"], g["top_k"], g["ffn"], g["shared_ffn"], g["e_begin"], g["e_local"],
+                   0, None, None, None, None, None)
+
+
+def test_workspace_size_grows_with_tokens():
+    from flowmoe import _lib
+    n1, n2 = ctypes.c_size_t(), ctypes.c_size_t()
+    L = _layer()
+    _lib.call("fm_workspace_size", ctypes.byref(L), 16, ctypes.byref(n1))
+    _lib.call("fm_workspace_size", ctypes.byref(L), 8192, ctypes.byref(n2))
+    assert 0 < n1.value < n2.value
+
+
+@pytest.mark.parametrize("kw,code", [(dict(top_k=200), 1), (dict(hidden=100), 1), (dict(ffn=700), 1),
+                                     (dict(e_begin=100, e_local=64), 1), (dict(n_experts=4096), 1)])
+def test_bad_geometry_is_rejected(kw, code):
+    from flowmoe import _lib
+    n = ctypes.c_size_t()
+    rc = _lib.lib.fm_workspace_size(ctypes.byref(_layer(**kw)), 16, ctypes.byref(n))
+    assert rc == code
+    assert _lib.last_error()
+
+
+def test_topk_past_experts_raises_like_reference():
+    from flowmoe import _lib
+    with pytest.raises(_lib.FlowMoeError, match="topk"):
+        _lib.call("fm_workspace_size", ctypes.byref(_layer(n_experts=4, top_k=5)), 1, ctypes.byref(ctypes.c_size_t()))
+
+
+def test_small_workspace_is_rejected():
+    from flowmoe import _lib
+    rc = _lib.lib.fm_moe_block(ctypes.byref(_layer()), None, 0, None, None, None, None, 16, 16, None, None, 16, None)
+    assert rc == _lib.FM_EWORKSPACE
+
+
+def test_tile_geometry_checked():
+    from flowmoe import _lib
+    assert _lib.lib.fm_q4_1_to_tiles(None, 100, 2048, None, None) == _lib.FM_EINVAL_SHAPE

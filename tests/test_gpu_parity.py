@@ -1,0 +1,161 @@
+"""Parity of the CUDA path (through the C ABI) against the CPU oracle on identical seeded inputs.
+
+Bars: expert ids, counts and permutations bit-exact wherever the router margin
+(k-th minus (k+1)-th probability) exceeds 1e-3; block outputs within max relative error 2e-2 of an
+fp64 accumulation of the same dequantised weights, measured as max|got - ref| / max|ref - res| (the
+expert contribution, so the residual cannot hide an error).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import cases, moe as OM, q4_1 as OQ
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    return torch.device("cuda:0")
+
+
+def _layer(c, dev):
+    import flowmoe
+    cfg = flowmoe.MoEConfig(hidden=c["H"], n_experts=c["E"], top_k=c["k"], ffn=c["F"], shared_ffn=c["FS"])
+    return flowmoe.MoELayer.from_q4_1(cfg, c["gate"], c["up"], c["down"], c["Wr"], shared=c["shared"], device=dev)
+
+
+def _rel(got, ref, res):
+    return float(np.abs(got - ref).max() / max(np.abs(ref - res).max(), 1e-30))
+
+
+def test_tiles_round_trip_bit_exact(dev):
+    import flowmoe
+    rng = np.random.default_rng(5)
+    blocks = OQ.random_q4_1_blocks(256, 512, rng)
+    t = flowmoe.q4_1_to_tiles(blocks, 256, 512, dev)
+    back = flowmoe.tiles_to_q4_1(t, 256, 512).cpu().numpy()
+    assert np.array_equal(back.reshape(blocks.shape), blocks)
+    assert not np.array_equal(t.cpu().numpy(), blocks.reshape(-1))   # it is a real permutation
+
+
+def _check_router(c, probs, idx, w):
+    xb = c["x"]
+    p_ref, idx_ref, w_ref = OM.router_block(xb, c["Wr"], c["k"])
+    margin = OM.router_margins(xb, c["Wr"], c["k"])
+    sure = margin > 1e-3
+    assert sure.mean() > 0.5
+    np.testing.assert_array_equal(np.sort(idx[sure], 1), np.sort(idx_ref[sure], 1))
+    np.testing.assert_array_equal(idx[sure], idx_ref[sure])
+    np.testing.assert_allclose(w, w_ref, rtol=1e-3, atol=1e-5)
+    if probs is not None:
+        np.testing.assert_allclose(probs, p_ref, rtol=1e-3, atol=1e-6)
+
+
+@pytest.mark.parametrize("T,E,H", [(16, 128, 2048), (1, 128, 2048), (333, 256, 2048), (64, 8, 256)])
+def test_router_topk_parity(dev, T, E, H):
+    import flowmoe
+    c = cases.make_case(H=H, E=E, F=128, T=T, seed=T, weights=None)
+    x = torch.from_numpy(c["x"]).to(dev).to(torch.bfloat16)
+    Wr = torch.from_numpy(c["Wr"]).to(dev)
+    probs, idx, w = flowmoe.router_block(x, Wr, c["k"])
+    _check_router(c, probs.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy())
+
+
+def test_router_reference_fixture_and_tie(dev, golden):
+    import flowmoe
+    r = golden["router"]
+    x = torch.tensor(r["rc_xm"], dtype=torch.float32, device=dev)
+    W = torch.tensor(r["rc_Wr"], dtype=torch.float32, device=dev)
+    # the device rounds xm and Wr to bf16 (the reference's NPU router does too); compare with the
+    # oracle on the same rounded operands, ids exact where the margin allows
+    p, idx, w = flowmoe.router_block(x, W, int(r["rc_topk"]))
+    xb, Wb = OM.bf16_round(r["rc_xm"]), OM.bf16_round(r["rc_Wr"])
+    p_ref, idx_ref, w_ref = OM.router_block(xb, Wb, int(r["rc_topk"]))
+    sure = OM.router_margins(xb, Wb, int(r["rc_topk"])) > 1e-3
+    np.testing.assert_array_equal(idx.cpu().numpy()[sure], idx_ref[sure])
+    np.testing.assert_allclose(w.cpu().numpy(), w_ref, rtol=1e-3)
+    # tie KAT (test_prefill_batch.py:363-369): experts 0, 1, 3 tie -> [0, 1], weights 0.5 / 0.5
+    tx = torch.tensor(r["tie_x"], dtype=torch.float32, device=dev)
+    tW = torch.tensor(r["tie_W"], dtype=torch.float32, device=dev)
+    p, idx, w = flowmoe.router_block(tx, tW, 2)
+    assert idx.cpu().tolist() == [[0, 1]]
+    np.testing.assert_allclose(w.cpu().numpy(), [[0.5, 0.5]], rtol=1e-6)
+
+
+@pytest.mark.parametrize("T,E,k", [(16, 128, 8), (4096, 256, 8), (3, 8, 3), (700, 64, 6)])
+def test_dispatch_bit_exact(dev, T, E, k):
+    import flowmoe
+    rng = np.random.default_rng(T)
+    idx = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    if T > 100:   # skew: a hot expert (duplicates within a token are legal owed-list entries)
+        idx[: T // 2, 0] = 3
+    cfg = flowmoe.MoEConfig(hidden=256, n_experts=E, top_k=k, ffn=128)
+    dummy = torch.zeros(256, dtype=torch.uint8, device=dev)
+    layer = flowmoe.MoELayer(cfg, dummy, dummy, torch.zeros(E + 1, 256, dtype=torch.bfloat16, device=dev))
+    t_real = T - 1 if T > 3 else T
+    counts, offsets, pos, pair = layer.dispatch(torch.from_numpy(idx).to(dev), t_real)
+    c_ref, o_ref, pos_ref, pair_ref = OM.dispatch(idx, E, t_real)
+    np.testing.assert_array_equal(counts.cpu().numpy(), c_ref)
+    np.testing.assert_array_equal(offsets.cpu().numpy(), o_ref)
+    np.testing.assert_array_equal(pos.cpu().numpy(), pos_ref[:t_real])
+    np.testing.assert_array_equal(pair.cpu().numpy(), pair_ref)
+
+
+def _run_block(c, dev, t_real=None):
+    layer = _layer(c, dev)
+    x = torch.from_numpy(c["x"]).to(dev).to(torch.bfloat16)
+    res = torch.from_numpy(c["res"]).to(dev)
+    probs, idx, w = layer.router_block(x)
+    sg = layer.shared_gate_buf if c["FS"] else None
+    out = layer.moe_block(x, res, idx, w, t_real=t_real, shared_gate=sg)
+    return layer, x, res, idx.cpu().numpy(), w.cpu().numpy(), out.cpu().numpy()
+
+
+@pytest.mark.parametrize("T", [16, 1, 32])
+def test_moe_block_config1(dev, T):
+    """BASELINE config 1 geometry (C30: H 2048, E 128, F 768, top-8, no shared)."""
+    c = cases.make_case(T=T, seed=0)
+    layer, x, res, idx, w, out = _run_block(c, dev)
+    ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"])
+    assert _rel(out, ref, c["res"]) < TOL
+
+
+def test_moe_block_shared_expert_and_padding(dev):
+    """C36-shaped (shared expert + sigmoid gate) at small E, with rows past t_real carried."""
+    c = cases.make_case(H=2048, E=16, F=512, FS=512, k=8, T=24, seed=1)
+    layer, x, res, idx, w, out = _run_block(c, dev, t_real=21)
+    ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], t_real=21, shared=c["shared"])
+    assert _rel(out, ref, c["res"]) < TOL
+    np.testing.assert_array_equal(out[21:], c["res"][21:])
+
+
+def test_moe_layer_fused_matches_staged(dev):
+    c = cases.make_case(H=2048, E=32, F=256, FS=256, k=8, T=40, seed=2)
+    layer, x, res, idx, w, out = _run_block(c, dev)
+    fused = layer.forward(x, res).cpu().numpy()
+    np.testing.assert_allclose(fused, out, rtol=0, atol=0)
+
+
+def test_moe_block_prefill_sized(dev):
+    """T=512 pairs over several dispatch chunks (C30 prefill shape, fewer experts to keep the oracle fast)."""
+    c = cases.make_case(H=2048, E=32, F=768, k=8, T=512, seed=3)
+    layer, x, res, idx, w, out = _run_block(c, dev)
+    ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"])
+    assert _rel(out, ref, c["res"]) < TOL
+
+
+def test_bad_expert_id_raises(dev):
+    import flowmoe
+    c = cases.make_case(H=256, E=8, F=128, k=2, T=4, seed=4)
+    layer = _layer(c, dev)
+    x = torch.from_numpy(c["x"]).to(dev)
+    res = torch.from_numpy(c["res"]).to(dev)
+    idx = torch.tensor([[0, 1], [2, 9], [3, 4], [5, 6]], dtype=torch.int32, device=dev)
+    w = torch.full((4, 2), 0.5, device=dev)
+    with pytest.raises(flowmoe._lib.FlowMoeError, match="FM_EINVAL_EXPERT"):
+        layer.moe_block(x, res, idx, w)
