@@ -12,8 +12,10 @@
  * tile (band b, slab s) sits at byte ((b * K/64) + s) * 5120 and holds
  *     [0, 4096)    row r (0..127): 32 nibble bytes = the 16 nibble bytes of block 2s, then of block 2s+1
  *     [4096, 5120) row r: 8 bytes = d(2s) m(2s) d(2s+1) m(2s+1), fp16
- * Per expert, the gate and up matrices [F, H] are stored back to back (gate tiles, then up tiles) in
- * the "gate_up" array and the down matrix [H, F] in the "down" array.
+ * The down matrix [H, F] of each expert uses these 128-row bands ("down" array). Its gate and up
+ * matrices [F, H] are interleaved by fm_gate_up_to_tiles() into 128-row bands of 64 features: band c
+ * holds gate rows 64c..64c+63 as tile rows 0-63 and up rows 64c..64c+63 as tile rows 64-127
+ * ("gate_up" array), so one tile feeds both operands of the SwiGLU.
  */
 #ifndef FLOWMOE_H
 #define FLOWMOE_H
@@ -51,11 +53,11 @@ typedef struct fm_layer {
     int32_t hidden;     /* H (% 128 == 0) */
     int32_t n_experts;  /* E, the router width (all experts, all ranks) */
     int32_t top_k;      /* k <= E, k <= 16 */
-    int32_t ffn;        /* F, routed expert intermediate (% 128 == 0) */
-    int32_t shared_ffn; /* F_s of the always-on shared expert; 0 = none */
+    int32_t ffn;        /* F, routed expert intermediate (% 64 == 0) */
+    int32_t shared_ffn; /* F_s of the always-on shared expert (% 64 == 0); 0 = none */
     int32_t e_begin;    /* first expert held by this rank (expert parallel); 0 on one GPU */
     int32_t e_local;    /* experts held by this rank; E on one GPU */
-    int32_t flags;      /* reserved, 0 */
+    int32_t flags;      /* 0 = pick the kernels by size; 1 = force the mma.sync path, 2 = force tcgen05 */
     const uint8_t* gate_up;   /* tiles, e_local x (2 x F x H x 5/8 B): gate then up, per expert */
     const uint8_t* down;      /* tiles, e_local x (H x F x 5/8 B) */
     const uint8_t* shared_gate_up; /* tiles of the shared expert, or NULL */
@@ -74,6 +76,11 @@ FM_API int fm_version(char* buf, size_t n);
  * Replaces the reference's pool packer open_kernels/q4_1_pack.py:124-142 (pack_q4_1_pool) /
  * gguf_pool/gguf_pool.py:191-213 (pack_q4_pool) for this device. rows % 128 == 0, k % 64 == 0. */
 FM_API int fm_q4_1_to_tiles(const uint8_t* blocks, int32_t rows, int32_t k, uint8_t* tiles, void* stream);
+
+/* GGUF Q4_1 gate and up blocks, each uint8[F, k/32, 20] (device) -> the interleaved gate_up tiles of
+ * one expert (device, 2 x F x k x 5/8 bytes). F % 64 == 0, k % 64 == 0. */
+FM_API int fm_gate_up_to_tiles(const uint8_t* gate, const uint8_t* up, int32_t F, int32_t k, uint8_t* tiles,
+                               void* stream);
 
 /* Tile layout -> GGUF Q4_1 blocks (the inverse; used to prove the repack is a permutation). */
 FM_API int fm_tiles_to_q4_1(const uint8_t* tiles, int32_t rows, int32_t k, uint8_t* blocks, void* stream);
@@ -120,8 +127,9 @@ FM_API int fm_moe_dispatch(const fm_layer* L, const int32_t* idx, int32_t T, int
                            int32_t* offsets, int32_t* pos, int32_t* pair, void* workspace, size_t workspace_bytes,
                            void* stream);
 
-/* Synchronises `stream` and returns FM_EINVAL_EXPERT if the last fm_moe_block on this workspace met
- * an expert id outside the range the block accepts (the check core.cpp:5159-5160 throws on). */
+/* Synchronises `stream` and returns FM_ETIMEOUT if a bounded device wait of the last call on this
+ * workspace gave up, else FM_EINVAL_EXPERT if it met an expert id outside the range the block accepts
+ * (the check core.cpp:5159-5160 throws on). */
 FM_API int fm_moe_check(void* workspace, void* stream);
 
 /* Kernel launches this library has made in this process (the driver-visible proof that the device

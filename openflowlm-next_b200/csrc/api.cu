@@ -57,6 +57,9 @@ int cuda_status(cudaError_t e, const char* what) {
 // kernels: see kernels.cuh
 
 constexpr int kBN = 64;        // rows per expert work item (expert_mma)
+constexpr int kBNTc = 256;     // rows per expert work item (expert_tc)
+constexpr int kTcMinTokens = 64;   // the tcgen05 path from this many tokens (below: the mma.sync path)
+constexpr int kFlagLegacy = 1, kFlagTc = 2;
 constexpr int kChunk = 2048;   // dispatch chunk (dispatch.cu)
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -73,9 +76,8 @@ static int validate(const fm_layer* L, int T) {
         return FM_EINVAL_SHAPE;
     }
     const int H = L->hidden, E = L->n_experts, k = L->top_k, F = L->ffn, FS = L->shared_ffn;
-    if (H <= 0 || H % kTileRows || E <= 0 || E > 1024 || F <= 0 || F % kTileRows || FS < 0 || FS % kTileRows ||
-        T < 0) {
-        set_error("bad geometry H=%d E=%d F=%d F_s=%d T=%d (H, F, F_s %% 128 == 0, E <= 1024)", H, E, F, FS, T);
+    if (H <= 0 || H % kTileRows || E <= 0 || E > 1024 || F <= 0 || F % 64 || FS < 0 || FS % 64 || T < 0) {
+        set_error("bad geometry H=%d E=%d F=%d F_s=%d T=%d (H %% 128, F and F_s %% 64 == 0, E <= 1024)", H, E, F, FS, T);
         return FM_EINVAL_SHAPE;
     }
     if (k <= 0 || k > E || k > kMaxTopK) {
@@ -99,7 +101,7 @@ static Layout make_layout(const fm_layer* L, int T) {
     const int G = L->e_local + 1;
     const int rt_routed = o.P / kBN + L->e_local;       // >= sum over routed groups of ceil(cnt / kBN)
     const int rt_shared = (T + kBN - 1) / kBN;
-    o.max_gu = rt_routed * (L->ffn / kTileRows) + rt_shared * (L->shared_ffn / kTileRows);
+    o.max_gu = rt_routed * (L->ffn / 64) + rt_shared * (L->shared_ffn / 64);
     o.max_dn = (rt_routed + (L->shared_ffn ? rt_shared : 0)) * (H / kTileRows);
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t at = off; off = align256(off + bytes); return at; };
@@ -155,11 +157,19 @@ static int xm_to_bf16(const fm_layer* L, const void* xm, int dtype, int T, void*
     return rc;
 }
 
+static bool use_tc(const fm_layer* L, int T) {
+    if (L->flags & kFlagLegacy) return false;
+    if (L->flags & kFlagTc) return true;
+    return T >= kTcMinTokens;
+}
+
 static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, const int32_t* idx, const float* w,
                      const float* sgate, int T, int t_real, float* out, void* ws, const Layout& lo, cudaStream_t st) {
     const int H = L->hidden, k = L->top_k, E = L->n_experts;
     const bool shared_on = L->shared_ffn > 0 && sgate && L->shared_gate_up && L->shared_down && t_real > 0;
     const int P = t_real * k;
+    const bool tc = use_tc(L, T);
+    const int bn = tc ? kBNTc : kBN;
     if (cudaMemsetAsync(at<int>(ws, lo.err), 0, 16, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
     const int nblk = (P + kChunk - 1) / kChunk;
     // rows of the sorted space: routed [0, P), shared [P_cap, P_cap + t_real) with P_cap = T * k
@@ -167,9 +177,8 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     prof_begin(kStageDispatch, st);
     int rc = launch_dispatch(idx, P, L->e_begin, L->e_local, E, Pcap, shared_on ? t_real : 0, at<int>(ws, lo.blk_hist), nblk,
                              at<int>(ws, lo.counts), at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
-                             at<int>(ws, lo.gu_list), L->ffn / kTileRows,
-                             shared_on ? L->shared_ffn / kTileRows : 0, at<int>(ws, lo.dn_list), H / kTileRows, kBN,
-                             at<int>(ws, lo.err), st);
+                             at<int>(ws, lo.gu_list), L->ffn / 64, shared_on ? L->shared_ffn / 64 : 0,
+                             at<int>(ws, lo.dn_list), H / kTileRows, bn, at<int>(ws, lo.err), st);
     if (rc) return rc;
     prof_end(kStageDispatch, st);
     prof_begin(kStageGather, st);
@@ -177,6 +186,55 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
                             k, H, lo.rows, at<uint16_t>(ws, lo.xperm), st)))
         return rc;
     prof_end(kStageGather, st);
+    if (tc) {
+        // out = res first (rows past t_real stay res); the down GEMM then adds w * y into it
+        if (cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            return cuda_status(cudaGetLastError(), "out = res");
+        TcLaunch g{};
+        g.max_items = lo.max_gu;
+        g.list = at<int>(ws, lo.gu_list);
+        g.act = at<uint16_t>(ws, lo.xperm);
+        g.act_rows = lo.rows;
+        g.act_cols = H;
+        g.act_ld = H;
+        g.w_routed = L->gate_up;
+        g.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
+        g.w_shared = L->shared_gate_up;
+        g.shared_group = L->e_local;
+        g.K_routed = H;
+        g.K_shared = H;
+        g.h_out = at<uint16_t>(ws, lo.hperm);
+        g.h_ld = lo.fmax;
+        g.err = at<int>(ws, lo.err) + 1;
+        prof_begin(kStageGateUp, st);
+        if ((rc = launch_expert_tc(true, g, st))) return rc;
+        prof_end(kStageGateUp, st);
+        TcLaunch d{};
+        d.max_items = lo.max_dn;
+        d.list = at<int>(ws, lo.dn_list);
+        d.act = at<uint16_t>(ws, lo.hperm);
+        d.act_rows = lo.rows;
+        d.act_cols = lo.fmax;
+        d.act_ld = lo.fmax;
+        d.w_routed = L->down;
+        d.w_routed_stride = (size_t)H * L->ffn / 32 * 20;
+        d.w_shared = L->shared_down;
+        d.shared_group = L->e_local;
+        d.K_routed = L->ffn;
+        d.K_shared = L->shared_ffn;
+        d.out = out;
+        d.H = H;
+        d.pair = at<int>(ws, lo.pair);
+        d.wpair = w;
+        d.k = k;
+        d.shared_base = Pcap;
+        d.sgate = sgate;
+        d.err = at<int>(ws, lo.err) + 1;
+        prof_begin(kStageDown, st);
+        if ((rc = launch_expert_tc(false, d, st))) return rc;
+        prof_end(kStageDown, st);
+        return FM_OK;
+    }
     GroupedArgs a{};
     a.list = at<int>(ws, lo.gu_list);
     a.act = at<uint16_t>(ws, lo.xperm);
@@ -187,8 +245,6 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     a.shared_group = L->e_local;
     a.K_routed = H;
     a.K_shared = H;
-    a.N_routed = L->ffn;
-    a.N_shared = L->shared_ffn;
     a.out = at<uint16_t>(ws, lo.hperm);
     a.out_ld = lo.fmax;
     prof_begin(kStageGateUp, st);
@@ -204,8 +260,6 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     d.shared_group = L->e_local;
     d.K_routed = L->ffn;
     d.K_shared = L->shared_ffn;
-    d.N_routed = H;
-    d.N_shared = H;
     d.out = at<float>(ws, lo.yperm);
     d.out_ld = H;
     prof_begin(kStageDown, st);
@@ -367,13 +421,17 @@ extern "C" FM_API int fm_profile_read(double* ms, int32_t n_stages) {
 
 extern "C" FM_API int fm_moe_check(void* workspace, void* stream) {
     g_err[0] = 0;
-    int bad = 0;   // the error counter sits at the start of every workspace layout
+    int word[2] = {0, 0};   // the error words sit at the start of every workspace layout
     cudaStream_t st = (cudaStream_t)stream;
     if (cudaStreamSynchronize(st) != cudaSuccess) return cuda_status(cudaGetLastError(), "stream sync");
-    if (cudaMemcpy(&bad, workspace, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
-        return cuda_status(cudaGetLastError(), "read error counter");
-    if (bad) {
-        set_error("router produced %d expert index(es) outside the experts this block holds", bad);
+    if (cudaMemcpy(word, workspace, sizeof(word), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "read error words");
+    if (word[1]) {
+        set_error("a device wait gave up (status %d): the block's output is incomplete", word[1]);
+        return word[1];
+    }
+    if (word[0]) {
+        set_error("router produced %d expert index(es) outside the experts this block holds", word[0]);
         return FM_EINVAL_EXPERT;
     }
     return FM_OK;

@@ -62,11 +62,12 @@ __device__ int block_exclusive_scan(int v, int* sh, int* total) {
     return base + x - v;
 }
 
-// Work list entry: (group, band, row0, nrows). list[0] = number of entries.
+// Work list entry: (group, band, row0, nrows). list[0] = number of entries. Row tiles outer, bands
+// inner, so consecutive items share their activation rows in L2.
 __device__ void emit_tiles(int* list, int first, int g, int bands, int row0, int cnt, int bn) {
     int i = first;
-    for (int b = 0; b < bands; ++b)
-        for (int r = 0; r < cnt; r += bn, ++i) {
+    for (int r = 0; r < cnt; r += bn)
+        for (int b = 0; b < bands; ++b, ++i) {
             int4 t = make_int4(g, b, row0 + r, min(bn, cnt - r));
             reinterpret_cast<int4*>(list + 4)[i] = t;
         }

@@ -23,11 +23,32 @@ struct GroupedArgs {
     const uint8_t* w_shared;
     int shared_group;
     int K_routed, K_shared;
-    int N_routed, N_shared;
     void* out;
     int out_ld;
 };
 int launch_expert_mma(bool gate_up, const GroupedArgs& a, int max_items, cudaStream_t st);
+struct TcLaunch {
+    int max_items;
+    const int* list;
+    const uint16_t* act;      // sorted bf16 activations (TMA source)
+    int act_rows, act_cols, act_ld;
+    const uint8_t* w_routed;
+    size_t w_routed_stride;
+    const uint8_t* w_shared;
+    int shared_group;
+    int K_routed, K_shared;
+    uint16_t* h_out;          // GATE_UP
+    int h_ld;
+    float* out;               // DOWN
+    int H;
+    const int* pair;
+    const float* wpair;
+    int k;
+    int shared_base;
+    const float* sgate;
+    int* err;
+};
+int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st);
 int launch_combine(const float* res, const float* y, const int* pos, const int32_t* idx, const float* w,
                    const float* sgate, int shared_on, int T, int t_real, int k, int H, int P, float* out, cudaStream_t st);
 

@@ -30,6 +30,28 @@ __global__ void q4_1_to_tiles_kernel(const uint32_t* __restrict__ blocks, int ro
     }
 }
 
+// gate_up layout: band c of a [F, K] pair holds gate rows 64c..64c+63 as tile rows 0-63 and up rows
+// 64c..64c+63 as tile rows 64-127, so one 128-row tile feeds the SwiGLU pair of 64 features.
+__global__ void gate_up_to_tiles_kernel(const uint32_t* __restrict__ gate, const uint32_t* __restrict__ up, int F, int k,
+                                        uint32_t* __restrict__ tiles) {
+    const int slabs = k / kTileK;
+    const long long n = (long long)2 * F * slabs;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / slabs), s = (int)(i % slabs);   // r in [0, 2F): tile row order
+        const int band = r / kTileRows, rr = r % kTileRows;
+        const int src_row = band * 64 + (rr & 63);
+        const uint32_t* b0 = (rr < 64 ? gate : up) + ((long long)src_row * (k / 32) + 2 * s) * 5;
+        uint32_t w[10];
+#pragma unroll
+        for (int j = 0; j < 10; ++j) w[j] = __ldg(b0 + j);
+        const long long tile = (long long)band * slabs + s;
+        uint4* nib4 = reinterpret_cast<uint4*>(tiles + tile * (kTileBytes / 4) + rr * 8);
+        nib4[0] = make_uint4(w[1], w[2], w[3], w[4]);
+        nib4[1] = make_uint4(w[6], w[7], w[8], w[9]);
+        *reinterpret_cast<uint2*>(tiles + tile * (kTileBytes / 4) + kTileNibBytes / 4 + rr * 2) = make_uint2(w[0], w[5]);
+    }
+}
+
 __global__ void tiles_to_q4_1_kernel(const uint32_t* __restrict__ tiles, int rows, int k, uint32_t* __restrict__ blocks) {
     const int slabs = k / kTileK;
     const long long n = (long long)rows * slabs;
@@ -89,6 +111,24 @@ extern "C" FM_API int fm_q4_1_to_tiles(const uint8_t* blocks, int32_t rows, int3
     const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
     q4_1_to_tiles_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint32_t*)blocks, rows, k, (uint32_t*)tiles);
     FM_LAUNCH_CHECK("q4_1_to_tiles");
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_gate_up_to_tiles(const uint8_t* gate, const uint8_t* up, int32_t F, int32_t k, uint8_t* tiles,
+                                           void* stream) {
+    if (F <= 0 || k <= 0 || F % 64 || k % kTileK) {
+        set_error("gate_up tiles need F %% 64 == 0 and k %% 64 == 0 (got F=%d k=%d)", F, k);
+        return FM_EINVAL_SHAPE;
+    }
+    if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(tiles)) & 15) {
+        set_error("fm_gate_up_to_tiles: pointers must be 16-byte aligned");
+        return FM_EINVAL_SHAPE;
+    }
+    const long long n = (long long)2 * F * (k / kTileK);
+    const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    gate_up_to_tiles_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint32_t*)gate, (const uint32_t*)up, F, k,
+                                                                    (uint32_t*)tiles);
+    FM_LAUNCH_CHECK("gate_up_to_tiles");
     return FM_OK;
 }
 

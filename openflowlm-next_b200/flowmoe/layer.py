@@ -80,6 +80,21 @@ def q4_1_to_tiles(blocks, rows: int, k: int, device="cuda", out: torch.Tensor | 
     return dst
 
 
+def gate_up_to_tiles(gate_blocks, up_blocks, F: int, k: int, device="cuda") -> torch.Tensor:
+    """Per expert GGUF gate and up blocks [E, F, k/32, 20] -> the interleaved gate_up tiles [E, 2*F*k*5/8]."""
+    g = _as_dev_u8(gate_blocks, device).reshape(-1)
+    u = _as_dev_u8(up_blocks, device).reshape(-1)
+    per = F * k // 32 * Q4_1_BYTES
+    if g.numel() != u.numel() or g.numel() % per:
+        raise ValueError(f"gate/up blocks are not whole [{F}, {k}] matrices of equal count")
+    E = g.numel() // per
+    out = torch.empty(E, 2 * per, dtype=torch.uint8, device=device)
+    st = _stream(out.device)
+    for e in range(E):
+        call("fm_gate_up_to_tiles", g[e * per:].data_ptr(), u[e * per:].data_ptr(), F, k, out[e].data_ptr(), st)
+    return out
+
+
 def tiles_to_q4_1(tiles: torch.Tensor, rows: int, k: int) -> torch.Tensor:
     """The inverse permutation (tile layout -> GGUF blocks), per matrix."""
     src = tiles.reshape(-1)
@@ -115,6 +130,17 @@ class MoELayer:
                           router.data_ptr(), _ptr(self.router_bias))
         self._ws: torch.Tensor | None = None
 
+    PATHS = {"auto": 0, "mma": 1, "tc": 2}
+
+    @property
+    def path(self) -> str:
+        """Kernel choice: "auto" (tcgen05 from 64 tokens, mma.sync below), "mma" or "tc" (forced)."""
+        return {v: k for k, v in self.PATHS.items()}[self._L.flags]
+
+    @path.setter
+    def path(self, name: str) -> None:
+        self._L.flags = self.PATHS[name]
+
     # ---- construction from the reference's block layout
     @classmethod
     def from_q4_1(cls, cfg: MoEConfig, gate_blocks, up_blocks, down_blocks, router_w, shared=None, device="cuda",
@@ -127,12 +153,7 @@ class MoELayer:
         u = _as_dev_u8(up_blocks, device).reshape(E, -1)
         if g.shape[1] != cfg.q4_bytes(F, H) or u.shape[1] != cfg.q4_bytes(F, H):
             raise ValueError("gate/up blocks do not match [E_local, F, H/32, 20]")
-        gate_up = torch.empty(E, cfg.gate_up_bytes, dtype=torch.uint8, device=device)
-        half = cfg.q4_bytes(F, H)
-        tg = q4_1_to_tiles(g, F, H, device).reshape(E, half)
-        tu = q4_1_to_tiles(u, F, H, device).reshape(E, half)
-        gate_up[:, :half] = tg
-        gate_up[:, half:] = tu
+        gate_up = gate_up_to_tiles(g, u, F, H, device)
         down = q4_1_to_tiles(_as_dev_u8(down_blocks, device), H, F, device).reshape(E, -1)
         if down.shape[1] != cfg.down_bytes:
             raise ValueError("down blocks do not match [E_local, H, F/32, 20]")
@@ -143,7 +164,7 @@ class MoELayer:
                 raise ValueError("shared expert weights given but cfg.shared_ffn == 0")
             sg, su, sd, sgw = shared
             FS = cfg.shared_ffn
-            sgu = torch.cat([q4_1_to_tiles(sg, FS, H, device), q4_1_to_tiles(su, FS, H, device)])
+            sgu = gate_up_to_tiles(sg, su, FS, H, device).reshape(-1)
             sdn = q4_1_to_tiles(sd, H, FS, device)
         wr = _bf16(router_w, device)
         if tuple(wr.shape) != (H, cfg.n_experts):

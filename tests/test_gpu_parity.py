@@ -23,10 +23,13 @@ def dev():
     return torch.device("cuda:0")
 
 
-def _layer(c, dev):
+def _layer(c, dev, path="auto"):
     import flowmoe
     cfg = flowmoe.MoEConfig(hidden=c["H"], n_experts=c["E"], top_k=c["k"], ffn=c["F"], shared_ffn=c["FS"])
-    return flowmoe.MoELayer.from_q4_1(cfg, c["gate"], c["up"], c["down"], c["Wr"], shared=c["shared"], device=dev)
+    layer = flowmoe.MoELayer.from_q4_1(cfg, c["gate"], c["up"], c["down"], c["Wr"], shared=c["shared"], device=dev,
+                                       router_bias=c.get("bias"))
+    layer.path = path
+    return layer
 
 
 def _rel(got, ref, res):
@@ -106,8 +109,8 @@ def test_dispatch_bit_exact(dev, T, E, k):
     np.testing.assert_array_equal(pair.cpu().numpy(), pair_ref)
 
 
-def _run_block(c, dev, t_real=None):
-    layer = _layer(c, dev)
+def _run_block(c, dev, t_real=None, path="auto"):
+    layer = _layer(c, dev, path)
     x = torch.from_numpy(c["x"]).to(dev).to(torch.bfloat16)
     res = torch.from_numpy(c["res"]).to(dev)
     probs, idx, w = layer.router_block(x)
@@ -116,19 +119,20 @@ def _run_block(c, dev, t_real=None):
     return layer, x, res, idx.cpu().numpy(), w.cpu().numpy(), out.cpu().numpy()
 
 
-@pytest.mark.parametrize("T", [16, 1, 32])
-def test_moe_block_config1(dev, T):
-    """BASELINE config 1 geometry (C30: H 2048, E 128, F 768, top-8, no shared)."""
+@pytest.mark.parametrize("T,path", [(16, "auto"), (1, "auto"), (32, "auto"), (16, "tc"), (1, "tc")])
+def test_moe_block_config1(dev, T, path):
+    """BASELINE config 1 geometry (C30: H 2048, E 128, F 768, top-8, no shared), both kernel paths."""
     c = cases.make_case(T=T, seed=0)
-    layer, x, res, idx, w, out = _run_block(c, dev)
+    layer, x, res, idx, w, out = _run_block(c, dev, path=path)
     ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"])
     assert _rel(out, ref, c["res"]) < TOL
 
 
-def test_moe_block_shared_expert_and_padding(dev):
+@pytest.mark.parametrize("path", ["mma", "tc"])
+def test_moe_block_shared_expert_and_padding(dev, path):
     """C36-shaped (shared expert + sigmoid gate) at small E, with rows past t_real carried."""
     c = cases.make_case(H=2048, E=16, F=512, FS=512, k=8, T=24, seed=1)
-    layer, x, res, idx, w, out = _run_block(c, dev, t_real=21)
+    layer, x, res, idx, w, out = _run_block(c, dev, t_real=21, path=path)
     ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], t_real=21, shared=c["shared"])
     assert _rel(out, ref, c["res"]) < TOL
     np.testing.assert_array_equal(out[21:], c["res"][21:])
@@ -136,17 +140,40 @@ def test_moe_block_shared_expert_and_padding(dev):
 
 def test_moe_layer_fused_matches_staged(dev):
     c = cases.make_case(H=2048, E=32, F=256, FS=256, k=8, T=40, seed=2)
-    layer, x, res, idx, w, out = _run_block(c, dev)
+    layer, x, res, idx, w, out = _run_block(c, dev, path="mma")
     fused = layer.forward(x, res).cpu().numpy()
     np.testing.assert_allclose(fused, out, rtol=0, atol=0)
 
 
-def test_moe_block_prefill_sized(dev):
-    """T=512 pairs over several dispatch chunks (C30 prefill shape, fewer experts to keep the oracle fast)."""
+@pytest.mark.parametrize("path", ["mma", "tc"])
+def test_moe_block_prefill_sized(dev, path):
+    """T=512 over several dispatch chunks and 256-row work items (C30 prefill shape, fewer experts to
+    keep the oracle fast)."""
     c = cases.make_case(H=2048, E=32, F=768, k=8, T=512, seed=3)
-    layer, x, res, idx, w, out = _run_block(c, dev)
+    layer, x, res, idx, w, out = _run_block(c, dev, path=path)
     ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"])
     assert _rel(out, ref, c["res"]) < TOL
+
+
+def test_moe_block_skewed_prefill_tc(dev):
+    """Zipf-skewed routing (BASELINE config 3's bias): hot experts span many 256-row items, others
+    get a handful of rows or none; shared expert on; tcgen05 path."""
+    c = cases.make_case(H=2048, E=16, F=256, FS=256, k=4, T=1000, seed=6, zipf=1.1)
+    layer, x, res, idx, w, out = _run_block(c, dev, path="tc")
+    counts = np.bincount(idx.reshape(-1), minlength=16)
+    assert counts.max() > 256 and counts.min() < 256
+    ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
+    assert _rel(out, ref, c["res"]) < TOL
+
+
+def test_tc_matches_mma_path(dev):
+    """The two kernel paths agree with each other far inside the oracle tolerance."""
+    c = cases.make_case(H=2048, E=8, F=128, FS=128, k=2, T=300, seed=7)
+    outs = []
+    for path in ("mma", "tc"):
+        layer, x, res, idx, w, out = _run_block(c, dev, path=path)
+        outs.append(out)
+    assert _rel(outs[1], outs[0], c["res"]) < 2e-3
 
 
 def test_bad_expert_id_raises(dev):
