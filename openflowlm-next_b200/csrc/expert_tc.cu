@@ -34,7 +34,10 @@ constexpr int TC_SA = 2;                   // dequantised A tile ring
 constexpr int TC_A_BYTES = 128 * 128;      // 128 rows x 64 bf16
 constexpr int TC_B_BYTES = TC_BN * 128;    // 256 rows x 64 bf16
 constexpr int TC_BOX_ROWS = 32;
-constexpr int TC_EPI_BYTES = 32 * 64 * 4;  // up-value staging (GATE_UP) / token + weight lists (DOWN)
+constexpr int TC_EPI_LD = 132;             // padded f32 row of the DOWN staging tile
+// epilogue staging: GATE_UP gate/up exchange (2 x 16 x 64 f32) + h tile (32 x 64 bf16);
+// DOWN weighted y tile (32 x 132 f32) + token / weight lists (2 x 256)
+constexpr int TC_EPI_BYTES = 32 * TC_EPI_LD * 4 + 2 * 256 * 4;
 
 struct TcSmem {
     // offsets from the 1024-aligned dynamic smem base
@@ -71,28 +74,31 @@ struct TcArgs {
 
 __device__ __forceinline__ void fail(int* err, int code) { atomicCAS(err, 0, code); }
 
-// q (0..15, one byte of t) as an exact float: 2^23 + q built by a byte permute, then minus 2^23.
-__device__ __forceinline__ float byte_to_f32(uint32_t t, uint32_t sel) {
-    return __uint_as_float(__byte_perm(t, 0x4B000000u, sel)) - 8388608.0f;
-}
+// Code q (0..15, byte b of t) as the float 0.5 + q/256: a byte permute places q in mantissa bits
+// 16-19 under the exponent byte 0x3F. Then q*d + m = f * (256 d) + (m - 128 d): the product is exact
+// (8 x 11 significant bits) and the single rounding of the add is the only one besides the fp32
+// rounding of the per-block constant m - 128 d (relative 2^-24), far below the bf16 rounding that
+// follows.
+__device__ __forceinline__ float code_f(uint32_t t, uint32_t sel) { return __uint_as_float(__byte_perm(t, 0x3F000000u, sel)); }
 
-// Four codes (bytes of t) -> two bf16x2 words of q*d + m.
-__device__ __forceinline__ uint2 deq4(uint32_t t, float d, float m) {
-    const float a = fmaf(byte_to_f32(t, 0x7540), d, m);
-    const float b = fmaf(byte_to_f32(t, 0x7541), d, m);
-    const float c = fmaf(byte_to_f32(t, 0x7542), d, m);
-    const float e = fmaf(byte_to_f32(t, 0x7543), d, m);
+// Four codes (bytes of t) -> two bf16x2 words of q*d + m, with D = 256 d and C = m - 128 d.
+__device__ __forceinline__ uint2 deq4(uint32_t t, float D, float C) {
+    const float a = fmaf(code_f(t, 0x7044), D, C);
+    const float b = fmaf(code_f(t, 0x7144), D, C);
+    const float c = fmaf(code_f(t, 0x7244), D, C);
+    const float e = fmaf(code_f(t, 0x7344), D, C);
     return make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, e));
 }
 
 // One GGUF block's 16 nibble bytes (4 words) -> 4 chunks of 8 bf16 (K = 0-7, 8-15, 16-23, 24-31).
 __device__ __forceinline__ void deq_block(uint4 n, float d, float m, uint4* ch) {
+    const float D = 256.0f * d, C = fmaf(-128.0f, d, m);
     const uint32_t w[4] = {n.x, n.y, n.z, n.w};
     uint2 lo[4], hi[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        lo[i] = deq4(w[i] & 0x0F0F0F0Fu, d, m);
-        hi[i] = deq4((w[i] >> 4) & 0x0F0F0F0Fu, d, m);
+        lo[i] = deq4(w[i] & 0x0F0F0F0Fu, D, C);
+        hi[i] = deq4((w[i] >> 4) & 0x0F0F0F0Fu, D, C);
     }
     ch[0] = make_uint4(lo[0].x, lo[0].y, lo[1].x, lo[1].y);   // values 0-7: low nibbles of bytes 0-7
     ch[1] = make_uint4(lo[2].x, lo[2].y, lo[3].x, lo[3].y);   // values 8-15
@@ -278,12 +284,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
         const int lg = warp & 3;                 // TMEM lane group this warp may access
         const int row = lg * 32 + lane;          // accumulator row = TMEM lane
         const int et = threadIdx.x - 192;        // 0..127
-        float* upbuf = reinterpret_cast<float*>(smem + TcSmem::epi);            // [32][64]
-        int* tok = reinterpret_cast<int*>(smem + TcSmem::epi);                  // [256]
-        float* wgt = reinterpret_cast<float*>(smem + TcSmem::epi + TC_BN * 4);  // [256]
-        bool ok = true;
+        uint8_t* epi = smem + TcSmem::epi;
+        float* xg = reinterpret_cast<float*>(epi);                   // GATE_UP: gate, cols 16-31 [16][64]
+        float* xu = xg + 16 * 64;                                    //          up, cols 0-15 [16][64]
+        uint16_t* hst = reinterpret_cast<uint16_t*>(xu + 16 * 64);   //          h tile [32][64] bf16
+        float* ys = reinterpret_cast<float*>(epi);                   // DOWN: weighted y [32][TC_EPI_LD]
+        int* tok = reinterpret_cast<int*>(epi + 32 * TC_EPI_LD * 4); //       token per row [256]
+        float* wgt = reinterpret_cast<float*>(tok + 256);            //       weight per row [256]
+        __shared__ int epi_abort;
+        if (et == 0) epi_abort = 0;
+        named_bar(1, 128);
         int local = 0;
-        for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++local) {
+        for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++local) {
             const Item it = decode_item<GATE_UP>(a, i);
             const int acc = local & 1;
             const uint32_t accph = (local >> 1) & 1;
@@ -304,49 +316,65 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
                     wgt[j] = wv;
                 }
             }
-            if (!mbar_wait(&acc_full[acc], accph)) { ok = false; }
+            if (!mbar_wait(&acc_full[acc], accph)) epi_abort = 1;
             named_bar(1, 128);
-            if (!ok) break;
+            if (epi_abort) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(lg * 32) << 16) + acc * 256;
             for (int c0 = 0; c0 < it.n; c0 += 32) {
                 uint32_t v[32];
+                tmem_ld32(taddr + c0, v);
+                tmem_ld_wait();
                 if (GATE_UP) {
-                    if (lg >= 2) {
-                        tmem_ld32(taddr + c0, v);
-                        tmem_ld_wait();
+                    // gate warps (rows 0-63) finish columns 0-15, up warps (rows 64-127) columns 16-31
+                    if (lg < 2) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) upbuf[j * 64 + (row - 64)] = __uint_as_float(v[j]);
+                        for (int j = 0; j < 16; ++j) xg[j * 64 + row] = __uint_as_float(v[16 + j]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) xu[j * 64 + row - 64] = __uint_as_float(v[j]);
                     }
                     named_bar(1, 128);
-                    if (lg < 2) {
-                        tmem_ld32(taddr + c0, v);
-                        tmem_ld_wait();
-                        const int f = it.band * 64 + row;
-                        uint16_t* dst = a.h_out + (size_t)(it.row0 + c0) * a.h_ld + f;
+                    const int f = row & 63;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if (c0 + j < it.n) {
-                                const float h = silu_f(__uint_as_float(v[j])) * upbuf[j * 64 + row];
-                                dst[(size_t)j * a.h_ld] = f32_to_bf16_bits(h);
-                            }
-                        }
+                    for (int j = 0; j < 16; ++j) {
+                        const float g = lg < 2 ? __uint_as_float(v[j]) : xg[j * 64 + f];
+                        const float u = lg < 2 ? xu[j * 64 + f] : __uint_as_float(v[16 + j]);
+                        const float h = __fdividef(g, 1.0f + __expf(-g)) * u;
+                        hst[(lg < 2 ? j : 16 + j) * 64 + f] = f32_to_bf16_bits(h);
+                    }
+                    named_bar(1, 128);
+                    // 32 token rows x 128 B: 4 threads per row, 2 x 16 B each
+                    const int j = et >> 2, part = et & 3;
+                    if (c0 + j < it.n) {
+                        const uint4* src = reinterpret_cast<const uint4*>(hst + j * 64 + part * 16);
+                        uint4* dst = reinterpret_cast<uint4*>(a.h_out + (size_t)(it.row0 + c0 + j) * a.h_ld +
+                                                              it.band * 64 + part * 16);
+                        dst[0] = src[0];
+                        dst[1] = src[1];
                     }
                     named_bar(1, 128);
                 } else {
-                    tmem_ld32(taddr + c0, v);
-                    tmem_ld_wait();
-                    float* col = a.out + it.band * 128 + row;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (c0 + j < it.n) red_add_f32(col + (size_t)tok[c0 + j] * a.H, wgt[c0 + j] * __uint_as_float(v[j]));
+                    for (int j = 0; j < 32; ++j) ys[j * TC_EPI_LD + row] = __uint_as_float(v[j]) * wgt[c0 + j];
+                    named_bar(1, 128);
+                    // warp w scatters tokens 8w..8w+7 of the chunk: 32 lanes x 4 floats = the 128 rows
+                    const int ew = et >> 5;
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        const int j = ew * 8 + jj;
+                        if (c0 + j < it.n) {
+                            const float4 y = *reinterpret_cast<const float4*>(ys + j * TC_EPI_LD + lane * 4);
+                            red_add_v4(a.out + (size_t)tok[c0 + j] * a.H + it.band * 128 + lane * 4, y);
+                        }
+                    }
+                    named_bar(1, 128);
                 }
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
-            named_bar(1, 128);   // tok/wgt and upbuf are rewritten by the next item
         }
-        if (!ok) {
+        if (epi_abort) {
             fail(a.err, FM_ETIMEOUT);
             atomicExch(&abort_flag, 1);
         }
