@@ -127,6 +127,16 @@ FM_API int fm_moe_dispatch(const fm_layer* L, const int32_t* idx, int32_t T, int
                            int32_t* offsets, int32_t* pos, int32_t* pair, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* fm_moe_layer for callers that cannot allocate device memory -- a decode loop being captured into a
+ * CUDA graph, or a host engine that plans every device buffer up front -- so it takes no workspace.
+ * No counterpart in the reference. The scratch space is a static 16 MiB device array in this library,
+ * held on every GPU that loads it until exit; calls needing more (fm_workspace_size > 16 MiB, about
+ * 128 tokens for the BASELINE layers) return FM_EWORKSPACE. All calls on a device share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller. The first call on each
+ * device looks the array's address up; make it before any stream capture. */
+FM_API int fm_moe_layer_noalloc(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, int32_t T,
+                                int32_t t_real, float* out, int32_t* idx, float* w, void* stream);
+
 /* Synchronises `stream` and returns FM_ETIMEOUT if a bounded device wait of the last call on this
  * workspace gave up, else FM_EINVAL_EXPERT if it met an expert id outside the range the block accepts
  * (the check core.cpp:5159-5160 throws on). */

@@ -52,6 +52,7 @@ SIGNATURES = {
     "fm_moe_block": [LP, P, I32, P, P, P, P, I32, I32, P, P, SZ, P],
     "fm_moe_layer": [LP, P, I32, P, I32, I32, P, P, P, P, SZ, P],
     "fm_moe_dispatch": [LP, P, I32, I32, P, P, P, P, P, SZ, P],
+    "fm_moe_layer_noalloc": [LP, P, I32, P, I32, I32, P, P, P, P],
     "fm_moe_check": [P, P],
     "fm_launch_count": [ctypes.POINTER(ctypes.c_ulonglong)],
     "fm_profile": [I32],
