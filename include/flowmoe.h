@@ -10,7 +10,9 @@
  * bytes, 32 values along K). The tile layout is a byte permutation of the same blocks (nothing is
  * re-quantised): a matrix W[N, K] (N % 128 == 0, K % 64 == 0) is cut into tiles of 128 rows x 64 K;
  * tile (band b, slab s) sits at byte ((b * K/64) + s) * 5120 and holds
- *     [0, 4096)    row r (0..127): 32 nibble bytes = the 16 nibble bytes of block 2s, then of block 2s+1
+ *     [0, 4096)    row r (0..127): 32 nibble bytes = the 16 nibble bytes of block 2s, then of block 2s+1,
+ *                  each block's bytes b0..b15 stored as the four words [b(2c) b(2c+1) b(2c+8) b(2c+9)],
+ *                  c = 0..3 (one mma.sync A fragment per word)
  *     [4096, 5120) row r: 8 bytes = d(2s) m(2s) d(2s+1) m(2s+1), fp16
  * The down matrix [H, F] of each expert uses these 128-row bands ("down" array). Its gate and up
  * matrices [F, H] are interleaved by fm_gate_up_to_tiles() into 128-row bands of 64 features: band c
@@ -57,7 +59,8 @@ typedef struct fm_layer {
     int32_t shared_ffn; /* F_s of the always-on shared expert (% 64 == 0); 0 = none */
     int32_t e_begin;    /* first expert held by this rank (expert parallel); 0 on one GPU */
     int32_t e_local;    /* experts held by this rank; E on one GPU */
-    int32_t flags;      /* 0 = pick the kernels by size; 1 = force the mma.sync path, 2 = force tcgen05 */
+    int32_t flags;      /* 0 = pick kernels by size (GEMV up to 32 tokens, tcgen05 from 64, mma.sync between);
+                           1 = force mma.sync, 2 = force tcgen05, 3 = force the GEMV (when T <= 32) */
     const uint8_t* gate_up;   /* tiles, e_local x (2 x F x H x 5/8 B): gate then up, per expert */
     const uint8_t* down;      /* tiles, e_local x (H x F x 5/8 B) */
     const uint8_t* shared_gate_up; /* tiles of the shared expert, or NULL */

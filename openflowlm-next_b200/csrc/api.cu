@@ -20,16 +20,20 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 // summed per stage) by fm_profile_read. Events are created when profiling is first enabled.
 struct Profiler {
     bool on = false;
-    static constexpr int kPairs = 256;
+    static constexpr int kPairs = 1024;
     cudaEvent_t ev[kPairs][2] = {};
     int stage[kPairs] = {};
     int n = 0;
-    int open[kStageCount] = {};
+    int open[kStageCount] = {};   // pair index of the stage's open event, -1 when none
 };
 static thread_local Profiler g_prof;
 
 void prof_begin(int stage, cudaStream_t st) {
-    if (!g_prof.on || g_prof.n >= Profiler::kPairs) return;
+    if (!g_prof.on) return;
+    if (g_prof.n >= Profiler::kPairs) {   // table full: this stage goes unrecorded
+        g_prof.open[stage] = -1;
+        return;
+    }
     const int i = g_prof.n++;
     g_prof.stage[i] = stage;
     g_prof.open[stage] = i;
@@ -39,7 +43,8 @@ void prof_begin(int stage, cudaStream_t st) {
 void prof_end(int stage, cudaStream_t st) {
     if (!g_prof.on) return;
     const int i = g_prof.open[stage];
-    if (i < g_prof.n && g_prof.stage[i] == stage) cudaEventRecord(g_prof.ev[i][1], st);
+    if (i >= 0 && i < g_prof.n && g_prof.stage[i] == stage) cudaEventRecord(g_prof.ev[i][1], st);
+    g_prof.open[stage] = -1;
 }
 
 void set_error(const char* fmt, ...) {
@@ -59,15 +64,18 @@ int cuda_status(cudaError_t e, const char* what) {
 constexpr int kBN = 64;        // rows per expert work item (expert_mma)
 constexpr int kBNTc = 256;     // rows per expert work item (expert_tc)
 constexpr int kTcMinTokens = 64;   // the tcgen05 path from this many tokens (below: the mma.sync path)
-constexpr int kFlagLegacy = 1, kFlagTc = 2;
+constexpr int kFlagLegacy = 1, kFlagTc = 2, kFlagGemv = 3;
+constexpr int kDecodeMaxT = 32;    // the GEMV path up to this many tokens
+constexpr int kGemvRowsApi = 8;    // sorted rows per GEMV item (decode.cu)
 constexpr int kChunk = 2048;   // dispatch chunk (dispatch.cu)
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
     size_t err, xb, logits, counts, offsets, blk_hist, pos, pair, gu_list, dn_list, xperm, hperm, yperm, sgate, idx, w;
+    size_t part, done;
     size_t total;
-    int nblk, max_gu, max_dn, P, rows, fmax;
+    int nblk, max_gu, max_dn, P, rows, fmax, max_slots, part_cols;
 };
 
 static int validate(const fm_layer* L, int T) {
@@ -103,6 +111,16 @@ static Layout make_layout(const fm_layer* L, int T) {
     const int rt_shared = (T + kBN - 1) / kBN;
     o.max_gu = rt_routed * (L->ffn / 64) + rt_shared * (L->shared_ffn / 64);
     o.max_dn = (rt_routed + (L->shared_ffn ? rt_shared : 0)) * (H / kTileRows);
+    const bool decode = T <= kDecodeMaxT;
+    if (decode) {
+        // GEMV items: 16-row tiles, up to 4 K chunks each
+        const int tt = o.P / kGemvRowsApi + L->e_local + (T + kGemvRowsApi - 1) / kGemvRowsApi;
+        const int bands = (L->ffn > L->shared_ffn ? L->ffn : L->shared_ffn) / 64;
+        o.max_slots = tt * (bands > H / kTileRows ? bands : H / kTileRows);
+        if (4 * o.max_slots > o.max_gu) o.max_gu = 4 * o.max_slots;
+        if (4 * o.max_slots > o.max_dn) o.max_dn = 4 * o.max_slots;
+        o.part_cols = 2 * o.fmax > H ? 2 * o.fmax : H;
+    }
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t at = off; off = align256(off + bytes); return at; };
     o.err = take(16);   // first: fm_moe_check reads the counter at the workspace start
@@ -121,6 +139,10 @@ static Layout make_layout(const fm_layer* L, int T) {
     o.sgate = take((size_t)T * 4);
     o.idx = take((size_t)o.P * 4);
     o.w = take((size_t)o.P * 4);
+    if (decode) {
+        o.part = take((size_t)4 * o.rows * o.part_cols * 4);
+        o.done = take((size_t)2 * o.max_slots * 4);
+    }
     o.total = off;
     return o;
 }
@@ -157,18 +179,93 @@ static int xm_to_bf16(const fm_layer* L, const void* xm, int dtype, int T, void*
     return rc;
 }
 
-static bool use_tc(const fm_layer* L, int T) {
-    if (L->flags & kFlagLegacy) return false;
-    if (L->flags & kFlagTc) return true;
-    return T >= kTcMinTokens;
+enum class Path { Mma, Tc, Gemv };
+
+static Path pick_path(const fm_layer* L, int T) {
+    const bool gemv_ok = T <= kDecodeMaxT && L->e_local < 1024 && T * L->top_k <= 1024;
+    switch (L->flags) {
+        case kFlagLegacy: return Path::Mma;
+        case kFlagTc: return Path::Tc;
+        case kFlagGemv: return gemv_ok ? Path::Gemv : Path::Mma;
+        default: break;
+    }
+    if (gemv_ok) return Path::Gemv;
+    return T >= kTcMinTokens ? Path::Tc : Path::Mma;
+}
+
+static int run_block_gemv(const fm_layer* L, const uint16_t* xb, const float* res, const int32_t* idx, const float* w,
+                          const float* sgate, int T, int t_real, float* out, void* ws, const Layout& lo,
+                          cudaStream_t st) {
+    const int H = L->hidden, k = L->top_k;
+    const bool shared_on = L->shared_ffn > 0 && sgate && L->shared_gate_up && L->shared_down && t_real > 0;
+    const int P = t_real * k, Pcap = lo.P;
+    if (cudaMemsetAsync(at<int>(ws, lo.err), 0, 16, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
+    if (cudaMemsetAsync(at<int>(ws, lo.done), 0, (size_t)2 * lo.max_slots * 4, st) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "memset");
+    prof_begin(kStageDispatch, st);
+    int rc = launch_dispatch_small(idx, P, L->e_begin, L->e_local, Pcap, shared_on ? t_real : 0, at<int>(ws, lo.counts),
+                                   at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
+                                   at<int>(ws, lo.gu_list), L->ffn / 64, shared_on ? L->shared_ffn / 64 : 0,
+                                   H / kTileK, at<int>(ws, lo.dn_list), H / kTileRows, L->ffn / kTileK,
+                                   shared_on ? L->shared_ffn / kTileK : L->ffn / kTileK, at<int>(ws, lo.err), st);
+    if (rc) return rc;
+    prof_end(kStageDispatch, st);
+    GemvLaunch g{};
+    g.max_items = lo.max_gu;
+    g.list = at<int>(ws, lo.gu_list);
+    g.w_routed = L->gate_up;
+    g.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
+    g.w_shared = L->shared_gate_up;
+    g.shared_group = L->e_local;
+    g.K_routed = H;
+    g.K_shared = H;
+    g.act = xb;
+    g.act_ld = H;
+    g.pair = at<int>(ws, lo.pair);
+    g.k = k;
+    g.shared_base = Pcap;
+    g.part = at<float>(ws, lo.part);
+    g.part_rows = lo.rows;
+    g.done = at<int>(ws, lo.done);
+    g.h_out = at<uint16_t>(ws, lo.hperm);
+    g.h_ld = lo.fmax;
+    g.F_routed = L->ffn;
+    g.F_shared = L->shared_ffn;
+    g.err = at<int>(ws, lo.err) + 1;
+    prof_begin(kStageGateUp, st);
+    if ((rc = launch_gemv(true, g, st))) return rc;
+    prof_end(kStageGateUp, st);
+    GemvLaunch d = g;
+    d.max_items = lo.max_dn;
+    d.list = at<int>(ws, lo.dn_list);
+    d.w_routed = L->down;
+    d.w_routed_stride = (size_t)H * L->ffn / 32 * 20;
+    d.w_shared = L->shared_down;
+    d.K_routed = L->ffn;
+    d.K_shared = L->shared_ffn;
+    d.act = at<uint16_t>(ws, lo.hperm);
+    d.act_ld = lo.fmax;
+    d.done = at<int>(ws, lo.done) + lo.max_slots;
+    d.y_out = at<float>(ws, lo.yperm);
+    d.H = H;
+    prof_begin(kStageDown, st);
+    if ((rc = launch_gemv(false, d, st))) return rc;
+    prof_end(kStageDown, st);
+    prof_begin(kStageCombine, st);
+    rc = launch_combine(res, at<float>(ws, lo.yperm), at<int>(ws, lo.pos), idx, w, sgate, shared_on ? 1 : 0, T, t_real,
+                        k, H, Pcap, out, st);
+    prof_end(kStageCombine, st);
+    return rc;
 }
 
 static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, const int32_t* idx, const float* w,
                      const float* sgate, int T, int t_real, float* out, void* ws, const Layout& lo, cudaStream_t st) {
     const int H = L->hidden, k = L->top_k, E = L->n_experts;
     const bool shared_on = L->shared_ffn > 0 && sgate && L->shared_gate_up && L->shared_down && t_real > 0;
+    const Path path = pick_path(L, T);
+    if (path == Path::Gemv) return run_block_gemv(L, xb, res, idx, w, sgate, T, t_real, out, ws, lo, st);
     const int P = t_real * k;
-    const bool tc = use_tc(L, T);
+    const bool tc = path == Path::Tc;
     const int bn = tc ? kBNTc : kBN;
     if (cudaMemsetAsync(at<int>(ws, lo.err), 0, 16, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
     const int nblk = (P + kChunk - 1) / kChunk;
@@ -348,9 +445,16 @@ extern "C" FM_API int fm_moe_layer(const fm_layer* L, const void* xm, int32_t xm
     float* ws_w = w ? w : at<float>(workspace, lo.w);
     float* sg = at<float>(workspace, lo.sgate);
     prof_begin(kStageRouter, st);
-    if (int rc = launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k, at<float>(workspace, lo.logits),
-                               nullptr, ids, ws_w, sg, st))
+    if (pick_path(L, T) == Path::Gemv) {
+        if (int rc = launch_router_small(xb, L->router, T, L->hidden, L->n_experts, at<float>(workspace, lo.logits), st))
+            return rc;
+        if (int rc = launch_router_topk(at<float>(workspace, lo.logits), L->router_bias, T, L->n_experts, L->top_k,
+                                        nullptr, ids, ws_w, sg, st))
+            return rc;
+    } else if (int rc = launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k,
+                                      at<float>(workspace, lo.logits), nullptr, ids, ws_w, sg, st)) {
         return rc;
+    }
     prof_end(kStageRouter, st);
     return run_block(L, xb, res, ids, ws_w, sg, T, t_real, out, workspace, lo, st);
 }
@@ -402,6 +506,7 @@ extern "C" FM_API int fm_profile(int32_t enable) {
     }
     g_prof.on = enable != 0;
     g_prof.n = 0;
+    for (int& o : g_prof.open) o = -1;
     return FM_OK;
 }
 

@@ -25,35 +25,28 @@ __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Two adjacent K values of one row from a 16-bit nibble word u (bytes j, j+1 of a block's 16
-// nibble bytes): hi == 0 -> values j, j+1 (low nibbles), hi == 1 -> values j+16, j+17.
-__device__ __forceinline__ uint32_t deq_pair(uint32_t u, int hi, float d, float m) {
-    const int sh = hi ? 4 : 0;
-    const float q0 = (float)((u >> sh) & 0xF), q1 = (float)((u >> (8 + sh)) & 0xF);
+// Two K values of one row from two code bytes (bits 0-3 and 8-11 of u): w = q * d + m, bf16x2.
+__device__ __forceinline__ uint32_t deq_pair(uint32_t u, float d, float m) {
+    const float q0 = (float)(u & 0xF), q1 = (float)((u >> 8) & 0xF);
     return pack_bf16x2(fmaf(q0, d, m), fmaf(q1, d, m));
 }
 
 // A fragments (m16n8k16 row-major), k16 step kk of the slab; fragment rows g and g+8 come from tile
-// rows rA and rB. Slab k = kk*16 + {2c, 2c+1, 2c+8, 2c+9}: block kk/2, values j = k % 32 -> byte
-// j % 16, high nibble when j >= 16 (kk odd).
+// rows rA and rB. Step kk covers block kk/2, values 16*(kk&1) + {2c, 2c+1, 2c+8, 2c+9}: in the tile's
+// fragment order those are the low (kk even) or high (kk odd) nibbles of word c of the block.
 __device__ __forceinline__ void load_a_frag(const uint8_t* tile, int rA, int rB, int c, int kk, uint32_t* a) {
-    const int blk = kk >> 1, hi = kk & 1;
-    const uint8_t* nibA = tile + rA * 32 + blk * 16;
-    const uint8_t* nibB = tile + rB * 32 + blk * 16;
+    const int blk = kk >> 1, sh = (kk & 1) * 4;
+    const uint32_t ua = *reinterpret_cast<const uint32_t*>(tile + rA * 32 + blk * 16 + c * 4) >> sh;
+    const uint32_t ub = *reinterpret_cast<const uint32_t*>(tile + rB * 32 + blk * 16 + c * 4) >> sh;
     const __half2 scA = *reinterpret_cast<const __half2*>(tile + kTileNibBytes + rA * 8 + blk * 4);
     const __half2 scB = *reinterpret_cast<const __half2*>(tile + kTileNibBytes + rB * 8 + blk * 4);
     const float dA = __low2float(scA), mA = __high2float(scA);
     const float dB = __low2float(scB), mB = __high2float(scB);
-    const uint32_t uA0 = *reinterpret_cast<const uint16_t*>(nibA + 2 * c);
-    const uint32_t uA1 = *reinterpret_cast<const uint16_t*>(nibA + 2 * c + 8);
-    const uint32_t uB0 = *reinterpret_cast<const uint16_t*>(nibB + 2 * c);
-    const uint32_t uB1 = *reinterpret_cast<const uint16_t*>(nibB + 2 * c + 8);
-    a[0] = deq_pair(uA0, hi, dA, mA);
-    a[1] = deq_pair(uB0, hi, dB, mB);
-    a[2] = deq_pair(uA1, hi, dA, mA);
-    a[3] = deq_pair(uB1, hi, dB, mB);
+    a[0] = deq_pair(ua, dA, mA);          // values 2c, 2c+1
+    a[1] = deq_pair(ub, dB, mB);
+    a[2] = deq_pair(ua >> 16, dA, mA);    // values 2c+8, 2c+9
+    a[3] = deq_pair(ub >> 16, dB, mB);
 }
-
 
 template <bool GATE_UP>
 __global__ void __launch_bounds__(256) expert_mma_kernel(GroupedArgs a) {

@@ -106,6 +106,12 @@ __device__ __forceinline__ void deq_block(uint4 n, float d, float m, uint4* ch) 
     ch[3] = make_uint4(hi[2].x, hi[2].y, hi[3].x, hi[3].y);   // values 24-31
 }
 
+// A tile block's 4 words in fragment order (see repack.cu) -> GGUF byte order b0..b15.
+__device__ __forceinline__ uint4 gguf_order(uint4 t) {
+    return make_uint4(__byte_perm(t.x, t.y, 0x5410), __byte_perm(t.z, t.w, 0x5410), __byte_perm(t.x, t.y, 0x7632),
+                      __byte_perm(t.z, t.w, 0x7632));
+}
+
 struct Item {
     int g, band, row0, n, slabs;
     const uint8_t* w;
@@ -254,8 +260,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
             for (int s = 0; s < it.slabs; ++s) {
                 if (!mbar_wait(&raw_full[rs], rph)) { ok = false; break; }
                 const uint8_t* raw = smem + TcSmem::raw + rs * kTileBytes;
-                const uint4 n0 = *reinterpret_cast<const uint4*>(raw + r * 32);
-                const uint4 n1 = *reinterpret_cast<const uint4*>(raw + r * 32 + 16);
+                const uint4 n0 = gguf_order(*reinterpret_cast<const uint4*>(raw + r * 32));
+                const uint4 n1 = gguf_order(*reinterpret_cast<const uint4*>(raw + r * 32 + 16));
                 const uint2 sc = *reinterpret_cast<const uint2*>(raw + kTileNibBytes + r * 8);
                 mbar_arrive(&raw_empty[rs]);
                 const float d0 = __half2float(__ushort_as_half((unsigned short)(sc.x & 0xFFFF)));

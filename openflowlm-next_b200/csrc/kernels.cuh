@@ -49,6 +49,37 @@ struct TcLaunch {
     int* err;
 };
 int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st);
+struct GemvLaunch {
+    int max_items;
+    const int* list;
+    const uint8_t* w_routed;
+    size_t w_routed_stride;
+    const uint8_t* w_shared;
+    int shared_group;
+    int K_routed, K_shared;
+    const uint16_t* act;
+    int act_ld;
+    const int* pair;
+    int k;
+    int shared_base;
+    float* part;
+    int part_rows;
+    int* done;
+    uint16_t* h_out;
+    int h_ld;
+    int F_routed, F_shared;
+    float* y_out;
+    int H;
+    int* err;
+};
+int launch_router_small(const uint16_t* xb, const uint16_t* router, int T, int H, int E, float* logits, cudaStream_t st);
+int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
+                          int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
+                          int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int* err,
+                          cudaStream_t st);
+int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st);
+int launch_router_topk(float* logits, const float* bias, int T, int E, int k, float* probs, int32_t* idx, float* w,
+                       float* sgate, cudaStream_t st);
 int launch_combine(const float* res, const float* y, const int* pos, const int32_t* idx, const float* w,
                    const float* sgate, int shared_on, int T, int t_real, int k, int H, int P, float* out, cudaStream_t st);
 

@@ -8,6 +8,19 @@
 
 namespace fm {
 
+// Within each block's 16 nibble bytes the tile stores, for c = 0..3, the word
+// [b(2c), b(2c+1), b(2c+8), b(2c+9)]: exactly the codes one mma.sync A-fragment thread needs (values
+// 2c, 2c+1, 2c+8, 2c+9 in the low nibbles, +16 in the high ones), so a fragment is one 32-bit load.
+__device__ __forceinline__ uint4 to_frag_order(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+    return make_uint4(__byte_perm(w0, w2, 0x5410), __byte_perm(w0, w2, 0x7632), __byte_perm(w1, w3, 0x5410),
+                      __byte_perm(w1, w3, 0x7632));
+}
+
+__device__ __forceinline__ uint4 from_frag_order(uint4 t) {
+    return make_uint4(__byte_perm(t.x, t.y, 0x5410), __byte_perm(t.z, t.w, 0x5410), __byte_perm(t.x, t.y, 0x7632),
+                      __byte_perm(t.z, t.w, 0x7632));
+}
+
 // One thread per (row, slab): blocks 2s and 2s+1 of row r (40 bytes) -> 32 nibble bytes + 8 scale
 // bytes of tile (r / 128, s). Blocks are 20 bytes = 5 words, so every block starts 4-byte aligned.
 __global__ void q4_1_to_tiles_kernel(const uint32_t* __restrict__ blocks, int rows, int k, uint32_t* __restrict__ tiles) {
@@ -23,8 +36,8 @@ __global__ void q4_1_to_tiles_kernel(const uint32_t* __restrict__ blocks, int ro
         const int rr = r % kTileRows;
         uint32_t* nib = tiles + tile * (kTileBytes / 4) + rr * 8;
         uint4* nib4 = reinterpret_cast<uint4*>(nib);
-        nib4[0] = make_uint4(w[1], w[2], w[3], w[4]);
-        nib4[1] = make_uint4(w[6], w[7], w[8], w[9]);
+        nib4[0] = to_frag_order(w[1], w[2], w[3], w[4]);
+        nib4[1] = to_frag_order(w[6], w[7], w[8], w[9]);
         uint2* sc = reinterpret_cast<uint2*>(tiles + tile * (kTileBytes / 4) + kTileNibBytes / 4 + rr * 2);
         *sc = make_uint2(w[0], w[5]);   // d0 m0 | d1 m1
     }
@@ -46,8 +59,8 @@ __global__ void gate_up_to_tiles_kernel(const uint32_t* __restrict__ gate, const
         for (int j = 0; j < 10; ++j) w[j] = __ldg(b0 + j);
         const long long tile = (long long)band * slabs + s;
         uint4* nib4 = reinterpret_cast<uint4*>(tiles + tile * (kTileBytes / 4) + rr * 8);
-        nib4[0] = make_uint4(w[1], w[2], w[3], w[4]);
-        nib4[1] = make_uint4(w[6], w[7], w[8], w[9]);
+        nib4[0] = to_frag_order(w[1], w[2], w[3], w[4]);
+        nib4[1] = to_frag_order(w[6], w[7], w[8], w[9]);
         *reinterpret_cast<uint2*>(tiles + tile * (kTileBytes / 4) + kTileNibBytes / 4 + rr * 2) = make_uint2(w[0], w[5]);
     }
 }
@@ -61,7 +74,7 @@ __global__ void tiles_to_q4_1_kernel(const uint32_t* __restrict__ tiles, int row
         const int rr = r % kTileRows;
         const uint4* nib4 = reinterpret_cast<const uint4*>(tiles + tile * (kTileBytes / 4) + rr * 8);
         const uint2 sc = *reinterpret_cast<const uint2*>(tiles + tile * (kTileBytes / 4) + kTileNibBytes / 4 + rr * 2);
-        const uint4 a = nib4[0], b = nib4[1];
+        const uint4 a = from_frag_order(nib4[0]), b = from_frag_order(nib4[1]);
         uint32_t* o = blocks + ((long long)r * (k / 32) + 2 * s) * 5;
         o[0] = sc.x; o[1] = a.x; o[2] = a.y; o[3] = a.z; o[4] = a.w;
         o[5] = sc.y; o[6] = b.x; o[7] = b.y; o[8] = b.z; o[9] = b.w;

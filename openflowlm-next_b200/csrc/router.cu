@@ -155,6 +155,13 @@ int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st) {
     return FM_OK;
 }
 
+int launch_router_topk(float* logits, const float* bias, int T, int E, int k, float* probs, int32_t* idx, float* w,
+                       float* sgate, cudaStream_t st) {
+    router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, E, k, probs, idx, w, sgate);
+    FM_LAUNCH_CHECK("router_topk");
+    return FM_OK;
+}
+
 int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
                   float* logits, float* probs, int32_t* idx, float* w, float* sgate, cudaStream_t st) {
     dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM);

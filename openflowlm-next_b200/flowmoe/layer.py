@@ -130,11 +130,12 @@ class MoELayer:
                           router.data_ptr(), _ptr(self.router_bias))
         self._ws: torch.Tensor | None = None
 
-    PATHS = {"auto": 0, "mma": 1, "tc": 2}
+    PATHS = {"auto": 0, "mma": 1, "tc": 2, "gemv": 3}
 
     @property
     def path(self) -> str:
-        """Kernel choice: "auto" (tcgen05 from 64 tokens, mma.sync below), "mma" or "tc" (forced)."""
+        """Kernel choice: "auto" (GEMV up to 32 tokens, tcgen05 from 64, mma.sync between), or forced
+        "mma", "tc", "gemv" (the GEMV only applies up to 32 tokens)."""
         return {v: k for k, v in self.PATHS.items()}[self._L.flags]
 
     @path.setter

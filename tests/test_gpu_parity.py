@@ -128,7 +128,7 @@ def test_moe_block_config1(dev, T, path):
     assert _rel(out, ref, c["res"]) < TOL
 
 
-@pytest.mark.parametrize("path", ["mma", "tc"])
+@pytest.mark.parametrize("path", ["mma", "tc", "gemv"])
 def test_moe_block_shared_expert_and_padding(dev, path):
     """C36-shaped (shared expert + sigmoid gate) at small E, with rows past t_real carried."""
     c = cases.make_case(H=2048, E=16, F=512, FS=512, k=8, T=24, seed=1)
@@ -163,6 +163,39 @@ def test_moe_block_skewed_prefill_tc(dev):
     counts = np.bincount(idx.reshape(-1), minlength=16)
     assert counts.max() > 256 and counts.min() < 256
     ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
+    assert _rel(out, ref, c["res"]) < TOL
+
+
+@pytest.mark.parametrize("T", [1, 3, 32])
+def test_gemv_decode_c36(dev, T):
+    """Decode sizes on the C36 geometry (256 experts, shared expert): the GEMV path, split-K chosen
+    by the number of active experts (T=1: 4 chunks, T=32: 1)."""
+    c = cases.make_case(H=2048, E=256, F=512, FS=512, k=8, T=T, seed=20 + T)
+    layer, x, res, idx, w, out = _run_block(c, dev, path="gemv")
+    ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
+    assert _rel(out, ref, c["res"]) < TOL
+
+
+def test_gemv_split_k_small_layer(dev):
+    """Few active bands: the GEMV splits K (4 chunks for gate/up, 2 for down) and the last chunk in
+    reduces them; shared expert on."""
+    c = cases.make_case(H=256, E=8, F=128, FS=128, k=2, T=2, seed=12)
+    layer, x, res, idx, w, out = _run_block(c, dev, path="gemv")
+    ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
+    assert _rel(out, ref, c["res"]) < TOL
+
+
+def test_gemv_hot_expert_many_rows(dev):
+    """All 32 tokens on the same two experts: GEMV items of 16 rows, several per expert."""
+    import flowmoe
+    c = cases.make_case(H=2048, E=8, F=768, k=2, T=32, seed=9)
+    layer = _layer(c, dev, "gemv")
+    x = torch.from_numpy(c["x"]).to(dev).to(torch.bfloat16)
+    res = torch.from_numpy(c["res"]).to(dev)
+    idx = torch.tensor([[3, 5]] * 32, dtype=torch.int32, device=dev)
+    w = torch.tensor([[0.75, 0.25]] * 32, dtype=torch.float32, device=dev)
+    out = layer.moe_block(x, res, idx, w).cpu().numpy()
+    ref = OM.moe_block_f64(c["x"], c["res"], idx.cpu().numpy(), w.cpu().numpy(), c["gate"], c["up"], c["down"])
     assert _rel(out, ref, c["res"]) < TOL
 
 
