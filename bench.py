@@ -166,6 +166,39 @@ def cpu_baseline(layer_blocks, cfg, x, res, budget_s=20.0, threads=None):
 
 
 # ------------------------------------------------------------------ sweep (configs 2 and 3)
+def graph_time(fn, reps=30):
+    """Capture fn in a CUDA graph and replay it: ms per replay of the plain graph, and the stage
+    durations from a second capture with the stage events inside it (its last replay)."""
+    from flowmoe import _lib
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    gp = torch.cuda.CUDAGraph()
+    _lib.profile(True)
+    with torch.cuda.graph(gp):
+        fn()
+    for _ in range(3):
+        gp.replay()
+    torch.cuda.synchronize()
+    stages = _lib.profile_read()
+    _lib.profile(False)
+    del g, gp
+    return ms, {k: round(v, 4) for k, v in stages.items() if v}
+
+
 def sweep(hbm, tfl_burst):
     import flowmoe
     from flowmoe.synth import C30, synth_layer, synth_tokens
@@ -173,18 +206,21 @@ def sweep(hbm, tfl_burst):
     out = {"decode": [], "prefill_zipf": []}
     layer = synth_layer(cfg, seed=0)
     expert_bytes = 3 * cfg.hidden * cfg.ffn * 5 // 8
-    st = torch.cuda.current_stream()
+    gu_bytes = 2 * cfg.hidden * cfg.ffn * 5 // 8
     for T in (1, 4, 8, 16, 32):
         x, res = synth_tokens(T, cfg.hidden, seed=T)
         o = torch.empty_like(res)
         idx = torch.empty(T, cfg.top_k, dtype=torch.int32, device="cuda")
         w = torch.empty(T, cfg.top_k, device="cuda")
-        ms = time_steps(lambda: layer.forward(x, res, out=o, idx=idx, w=w), 50, 10, 1, st)
+        ms, st = graph_time(lambda: layer.forward(x, res, out=o, idx=idx, w=w))
         U = int(torch.unique(idx).numel())
         nbytes = U * expert_bytes + (cfg.n_experts + 1) * cfg.hidden * 2 + T * cfg.hidden * (2 + 4 + 4)
         gbs = nbytes / (ms * 1e-3) / 1e9
+        gu = U * gu_bytes / (st["gate_up"] * 1e-3) / 1e9 if st.get("gate_up") else None
         out["decode"].append({"T": T, "experts_touched": U, "ms": round(ms, 4), "tokens_per_s": round(T / ms * 1e3, 1),
-                              "GB_s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4)})
+                              "GB_s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4), "stages_ms": st,
+                              "gemv_gate_up_GB_s": round(gu, 1) if gu else None,
+                              "gemv_gate_up_hbm_frac": round(gu / hbm, 4) if gu else None})
     del layer
     layer = synth_layer(cfg, seed=0, zipf=1.1)
     for T in (512, 2048, 8192):
@@ -192,12 +228,14 @@ def sweep(hbm, tfl_burst):
         o = torch.empty_like(res)
         idx = torch.empty(T, cfg.top_k, dtype=torch.int32, device="cuda")
         w = torch.empty(T, cfg.top_k, device="cuda")
-        ms = time_steps(lambda: layer.forward(x, res, out=o, idx=idx, w=w), 10, 3, 1, st)
+        ms, st = graph_time(lambda: layer.forward(x, res, out=o, idx=idx, w=w), reps=10)
         cnt = torch.bincount(idx.reshape(-1).long(), minlength=cfg.n_experts)
-        fl = routed_flops(cfg, T * cfg.top_k, T) + 2.0 * T * cfg.hidden * cfg.n_experts
+        fl = routed_flops(cfg, T * cfg.top_k, 0) + 2.0 * T * cfg.hidden * cfg.n_experts
         tf = fl / (ms * 1e-3) / 1e12
+        gu_tf = gate_up_flops(cfg, T * cfg.top_k, 0) / (st["gate_up"] * 1e-3) / 1e12 if st.get("gate_up") else None
         out["prefill_zipf"].append({"T": T, "ms": round(ms, 4), "tokens_per_s": round(T / ms * 1e3, 1),
-                                    "TFLOP_s": round(tf, 2), "tensor_frac": round(tf / tfl_burst, 4),
+                                    "TFLOP_s": round(tf, 2), "tensor_frac": round(tf / tfl_burst, 4), "stages_ms": st,
+                                    "gate_up_TFLOP_s": round(gu_tf, 1) if gu_tf else None,
                                     "max_expert_rows": int(cnt.max()), "empty_experts": int((cnt == 0).sum())})
     return out
 

@@ -152,7 +152,8 @@ FM_API int fm_launch_count(unsigned long long* n);
 /* Stage profiler (the reference's OFLM_OPEN_PROFILE stage timings, core.cpp:592-600, :850-935, on
  * CUDA events): while enabled, each call records a timing event pair around every stage on its
  * stream. Stages: 0 to_bf16, 1 router, 2 dispatch, 3 gather, 4 gate_up, 5 down, 6 combine.
- * fm_profile(1) creates the events on first use; do not enable it during stream capture. */
+ * fm_profile(1) creates the events on first use; call it before any stream capture. Inside a captured
+ * graph the records become event-record nodes, so fm_profile_read then reports the last replay. */
 FM_API int fm_profile(int32_t enable);
 
 /* Waits for the recorded events and writes the summed milliseconds per stage into ms[0..n_stages),

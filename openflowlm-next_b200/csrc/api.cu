@@ -28,6 +28,14 @@ struct Profiler {
 };
 static thread_local Profiler g_prof;
 
+// An event record that is a graph node inside a stream capture and a plain record outside it.
+static void prof_record(cudaEvent_t ev, cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    if (cs == cudaStreamCaptureStatusActive) cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal);
+    else cudaEventRecord(ev, st);
+}
+
 void prof_begin(int stage, cudaStream_t st) {
     if (!g_prof.on) return;
     if (g_prof.n >= Profiler::kPairs) {   // table full: this stage goes unrecorded
@@ -37,13 +45,13 @@ void prof_begin(int stage, cudaStream_t st) {
     const int i = g_prof.n++;
     g_prof.stage[i] = stage;
     g_prof.open[stage] = i;
-    cudaEventRecord(g_prof.ev[i][0], st);
+    prof_record(g_prof.ev[i][0], st);
 }
 
 void prof_end(int stage, cudaStream_t st) {
     if (!g_prof.on) return;
     const int i = g_prof.open[stage];
-    if (i >= 0 && i < g_prof.n && g_prof.stage[i] == stage) cudaEventRecord(g_prof.ev[i][1], st);
+    if (i >= 0 && i < g_prof.n && g_prof.stage[i] == stage) prof_record(g_prof.ev[i][1], st);
     g_prof.open[stage] = -1;
 }
 
@@ -125,7 +133,7 @@ static Layout make_layout(const fm_layer* L, int T) {
     auto take = [&](size_t bytes) { size_t at = off; off = align256(off + bytes); return at; };
     o.err = take(16);   // first: fm_moe_check reads the counter at the workspace start
     o.xb = take((size_t)T * H * 2);
-    o.logits = take((size_t)T * (E + 1) * 4);
+    o.logits = take((size_t)router_ksplit(T, H, E) * T * (E + 1) * 4);
     o.counts = take((size_t)G * 4);
     o.offsets = take((size_t)(G + 1) * 4);
     o.blk_hist = take((size_t)o.nblk * L->e_local * 4);
@@ -445,16 +453,9 @@ extern "C" FM_API int fm_moe_layer(const fm_layer* L, const void* xm, int32_t xm
     float* ws_w = w ? w : at<float>(workspace, lo.w);
     float* sg = at<float>(workspace, lo.sgate);
     prof_begin(kStageRouter, st);
-    if (pick_path(L, T) == Path::Gemv) {
-        if (int rc = launch_router_small(xb, L->router, T, L->hidden, L->n_experts, at<float>(workspace, lo.logits), st))
-            return rc;
-        if (int rc = launch_router_topk(at<float>(workspace, lo.logits), L->router_bias, T, L->n_experts, L->top_k,
-                                        nullptr, ids, ws_w, sg, st))
-            return rc;
-    } else if (int rc = launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k,
-                                      at<float>(workspace, lo.logits), nullptr, ids, ws_w, sg, st)) {
+    if (int rc = launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k,
+                               at<float>(workspace, lo.logits), nullptr, ids, ws_w, sg, st))
         return rc;
-    }
     prof_end(kStageRouter, st);
     return run_block(L, xb, res, ids, ws_w, sg, T, t_real, out, workspace, lo, st);
 }

@@ -20,35 +20,6 @@
 
 namespace fm {
 
-// ------------------------------------------------------------------ router logits for few tokens
-// One warp per router row (expert, or the shared-gate row E), all T tokens; the CTA stages x in smem.
-__global__ void __launch_bounds__(256) router_small_kernel(const uint16_t* __restrict__ xb, const uint16_t* __restrict__ router,
-                                                           int T, int H, int rows, float* __restrict__ logits) {
-    extern __shared__ __align__(16) uint16_t xs[];   // [T][H]
-    for (int i = threadIdx.x; i < T * H / 8; i += blockDim.x)
-        reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(xb)[i];
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x * 8 + warp;
-    if (e >= rows) return;
-    const uint16_t* w = router + (size_t)e * H;
-    for (int t = 0; t < T; ++t) {
-        float acc = 0.f;
-        for (int h = lane * 8; h < H; h += 256) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(w + h);
-            const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)t * H + h);
-            const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                acc = fmaf(__uint_as_float(ww[q] << 16), __uint_as_float(xx[q] << 16), acc);
-                acc = fmaf(__uint_as_float(ww[q] & 0xFFFF0000u), __uint_as_float(xx[q] & 0xFFFF0000u), acc);
-            }
-        }
-        acc = warp_sum(acc);
-        if (lane == 0) logits[(size_t)t * rows + e] = acc;
-    }
-}
-
 // ------------------------------------------------------------------ single-CTA dispatch + GEMV lists
 // Pairs P <= 1024. Same results as dispatch_{hist,scan,scatter} (stable, token-then-slot order within an
 // expert), plus the GEMV work lists: items (g | band << 16, row0, n | kc << 16, slot), list[0] = count,
@@ -528,23 +499,6 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_kernel(GemvArgs a) {
 }
 
 // ------------------------------------------------------------------ launchers
-int launch_router_small(const uint16_t* xb, const uint16_t* router, int T, int H, int E, float* logits, cudaStream_t st) {
-    const int rows = E + 1;
-    const size_t sm = (size_t)T * H * 2;
-    if (sm > 48 * 1024) {
-        static bool attr = false;
-        if (!attr) {
-            cudaFuncSetAttribute(router_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-            attr = true;
-        }
-    }
-    router_small_kernel<<<(rows + 7) / 8, 256, sm, st>>>(xb, router, T, H, rows, logits);
-    FM_LAUNCH_CHECK("router_small");
-    return FM_OK;
-}
-
-
-
 int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
                           int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
                           int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int* err,

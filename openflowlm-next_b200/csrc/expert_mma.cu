@@ -123,7 +123,8 @@ int launch_expert_mma(bool gate_up, const GroupedArgs& a, int max_items, cudaStr
 }
 
 // out[t] = res[t] + sgate[t] * y[P + t] + sum over t's pairs in ascending expert order of w * y[pos].
-// Rows t >= t_real: out = res. One block per token, 256 threads x float4.
+// Rows t >= t_real: out = res. Grid (T, H / 1024): each thread one float4 column group; every load of a
+// thread is issued before the ordered accumulation.
 __global__ void combine_kernel(const float* __restrict__ res, const float* __restrict__ y, const int* __restrict__ pos,
                                const int32_t* __restrict__ idx, const float* __restrict__ w,
                                const float* __restrict__ sgate, int shared_on, int T, int t_real, int k, int H, int P,
@@ -156,28 +157,34 @@ __global__ void combine_kernel(const float* __restrict__ res, const float* __res
     }
     __syncthreads();
     const int n = n_sel;
-    const float g = (t < t_real && shared_on) ? sgate[t] : 0.0f;
-    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
-        float4 o = reinterpret_cast<const float4*>(res + (size_t)t * H)[i];
-        if (t < t_real) {
-            if (shared_on) {
-                const float4 v = reinterpret_cast<const float4*>(y + (size_t)(P + t) * H)[i];
-                o.x += g * v.x; o.y += g * v.y; o.z += g * v.z; o.w += g * v.w;
-            }
-            for (int j = 0; j < n; ++j) {
-                const float4 v = reinterpret_cast<const float4*>(y + (size_t)srow[j] * H)[i];
-                const float ww = sw[j];
-                o.x += ww * v.x; o.y += ww * v.y; o.z += ww * v.z; o.w += ww * v.w;
-            }
+    const int i = blockIdx.y * blockDim.x + threadIdx.x;   // float4 column group
+    if (i >= H / 4) return;
+    float4 o = reinterpret_cast<const float4*>(res + (size_t)t * H)[i];
+    if (t < t_real) {
+        float4 v[kMaxTopK + 1];
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j)
+            if (j < n) v[j] = reinterpret_cast<const float4*>(y + (size_t)srow[j] * H)[i];
+        if (shared_on) v[kMaxTopK] = reinterpret_cast<const float4*>(y + (size_t)(P + t) * H)[i];
+        if (shared_on) {
+            const float g = sgate[t];
+            o.x += g * v[kMaxTopK].x; o.y += g * v[kMaxTopK].y; o.z += g * v[kMaxTopK].z; o.w += g * v[kMaxTopK].w;
         }
-        reinterpret_cast<float4*>(out + (size_t)t * H)[i] = o;
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j)
+            if (j < n) {
+                const float ww = sw[j];
+                o.x += ww * v[j].x; o.y += ww * v[j].y; o.z += ww * v[j].z; o.w += ww * v[j].w;
+            }
     }
+    reinterpret_cast<float4*>(out + (size_t)t * H)[i] = o;
 }
 
 int launch_combine(const float* res, const float* y, const int* pos, const int32_t* idx, const float* w,
                    const float* sgate, int shared_on, int T, int t_real, int k, int H, int P, float* out, cudaStream_t st) {
     if (T <= 0) return FM_OK;
-    combine_kernel<<<T, 256, 0, st>>>(res, y, pos, idx, w, sgate, shared_on, T, t_real, k, H, P, out);
+    dim3 grid(T, (H / 4 + 255) / 256);
+    combine_kernel<<<grid, 256, 0, st>>>(res, y, pos, idx, w, sgate, shared_on, T, t_real, k, H, P, out);
     FM_LAUNCH_CHECK("combine");
     return FM_OK;
 }

@@ -72,14 +72,12 @@ struct GemvLaunch {
     int H;
     int* err;
 };
-int launch_router_small(const uint16_t* xb, const uint16_t* router, int T, int H, int E, float* logits, cudaStream_t st);
+int router_ksplit(int T, int H, int E);
 int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
                           int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
                           int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int* err,
                           cudaStream_t st);
 int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st);
-int launch_router_topk(float* logits, const float* bias, int T, int E, int k, float* probs, int32_t* idx, float* w,
-                       float* sgate, cudaStream_t st);
 int launch_combine(const float* res, const float* y, const int* pos, const int32_t* idx, const float* w,
                    const float* sgate, int shared_on, int T, int t_real, int k, int H, int P, float* out, cudaStream_t st);
 

@@ -27,81 +27,112 @@ __device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, cons
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-// C[M, N] (ldc) = A[M, K] . B[N, K]^T, bf16 in, f32 out. 64x64 CTA tile, 4 warps of 32x32, K step 32.
-// K % 32 == 0. A plain tensor-core GEMM: the router is ~2% of the block's FLOPs.
+// Partial logits: part[z][M][N] = A[M, kz] . B[N, kz]^T over the z-th K chunk (kz = K / gridDim.z),
+// bf16 in, f32 out. 64x64 CTA tile, 4 warps of 32x32, K step 32 with the next step's operands fetched
+// into registers while the current one is multiplied. The top-k kernel sums the chunks in order.
 constexpr int RG_BM = 64, RG_BN = 64, RG_BK = 32, RG_LD = RG_BK + 8;
+constexpr int kMaxKSplit = 16;
 
 __global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __restrict__ A, const uint16_t* __restrict__ B,
-                                                            float* __restrict__ C, int M, int N, int K, int ldc) {
-    __shared__ __align__(16) uint16_t sa[RG_BM][RG_LD];
-    __shared__ __align__(16) uint16_t sb[RG_BN][RG_LD];
+                                                            float* __restrict__ part, int M, int N, int K) {
+    __shared__ __align__(16) uint16_t sa[2][RG_BM][RG_LD];
+    __shared__ __align__(16) uint16_t sb[2][RG_BN][RG_LD];
     const int m0 = blockIdx.y * RG_BM, n0 = blockIdx.x * RG_BN;
+    const int kc = K / gridDim.z, kbeg = blockIdx.z * kc;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
     const int g = lane >> 2, c = lane & 3;
     float acc[2][4][4] = {};
-    for (int k0 = 0; k0 < K; k0 += RG_BK) {
-        // 64 rows x 32 K bf16 = 64 x 4 uint4 per operand; 128 threads -> 2 each
-        for (int i = threadIdx.x; i < RG_BM * 4; i += 128) {
-            const int r = i >> 2, q = i & 3;
-            uint4 va = make_uint4(0, 0, 0, 0), vb = make_uint4(0, 0, 0, 0);
-            if (m0 + r < M) va = *reinterpret_cast<const uint4*>(A + (size_t)(m0 + r) * K + k0 + q * 8);
-            if (n0 + r < N) vb = *reinterpret_cast<const uint4*>(B + (size_t)(n0 + r) * K + k0 + q * 8);
-            *reinterpret_cast<uint4*>(&sa[r][q * 8]) = va;
-            *reinterpret_cast<uint4*>(&sb[r][q * 8]) = vb;
+    uint4 ra[2], rb[2];
+    auto fetch = [&](int k0) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int i = threadIdx.x + j * 128, r = i >> 2, q = i & 3;
+            ra[j] = m0 + r < M ? *reinterpret_cast<const uint4*>(A + (size_t)(m0 + r) * K + k0 + q * 8) : make_uint4(0, 0, 0, 0);
+            rb[j] = n0 + r < N ? *reinterpret_cast<const uint4*>(B + (size_t)(n0 + r) * K + k0 + q * 8) : make_uint4(0, 0, 0, 0);
         }
-        __syncthreads();
+    };
+    auto stash = [&](int buf) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int i = threadIdx.x + j * 128, r = i >> 2, q = i & 3;
+            *reinterpret_cast<uint4*>(&sa[buf][r][q * 8]) = ra[j];
+            *reinterpret_cast<uint4*>(&sb[buf][r][q * 8]) = rb[j];
+        }
+    };
+    fetch(kbeg);
+    stash(0);
+    __syncthreads();
+    int buf = 0;
+    for (int k0 = kbeg; k0 < kbeg + kc; k0 += RG_BK) {
+        const bool more = k0 + RG_BK < kbeg + kc;
+        if (more) fetch(k0 + RG_BK);
 #pragma unroll
         for (int kk = 0; kk < RG_BK; kk += 16) {
             uint32_t af[2][4], bf[4][2];
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 const int r = wm + i * 16 + g;
-                af[i][0] = *reinterpret_cast<const uint32_t*>(&sa[r][kk + 2 * c]);
-                af[i][1] = *reinterpret_cast<const uint32_t*>(&sa[r + 8][kk + 2 * c]);
-                af[i][2] = *reinterpret_cast<const uint32_t*>(&sa[r][kk + 2 * c + 8]);
-                af[i][3] = *reinterpret_cast<const uint32_t*>(&sa[r + 8][kk + 2 * c + 8]);
+                af[i][0] = *reinterpret_cast<const uint32_t*>(&sa[buf][r][kk + 2 * c]);
+                af[i][1] = *reinterpret_cast<const uint32_t*>(&sa[buf][r + 8][kk + 2 * c]);
+                af[i][2] = *reinterpret_cast<const uint32_t*>(&sa[buf][r][kk + 2 * c + 8]);
+                af[i][3] = *reinterpret_cast<const uint32_t*>(&sa[buf][r + 8][kk + 2 * c + 8]);
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int n = wn + j * 8 + g;
-                bf[j][0] = *reinterpret_cast<const uint32_t*>(&sb[n][kk + 2 * c]);
-                bf[j][1] = *reinterpret_cast<const uint32_t*>(&sb[n][kk + 2 * c + 8]);
+                bf[j][0] = *reinterpret_cast<const uint32_t*>(&sb[buf][n][kk + 2 * c]);
+                bf[j][1] = *reinterpret_cast<const uint32_t*>(&sb[buf][n][kk + 2 * c + 8]);
             }
 #pragma unroll
             for (int i = 0; i < 2; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) mma_bf16_16816(acc[i][j], af[i], bf[j]);
         }
-        __syncthreads();
+        if (more) {
+            stash(buf ^ 1);
+            __syncthreads();
+            buf ^= 1;
+        }
     }
+    float* C = part + (size_t)blockIdx.z * M * N;
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int r = m0 + wm + i * 16 + g, n = n0 + wn + j * 8 + 2 * c;
             if (r < M) {
-                if (n < N) C[(size_t)r * ldc + n] = acc[i][j][0];
-                if (n + 1 < N) C[(size_t)r * ldc + n + 1] = acc[i][j][1];
+                if (n < N) C[(size_t)r * N + n] = acc[i][j][0];
+                if (n + 1 < N) C[(size_t)r * N + n + 1] = acc[i][j][1];
             }
             if (r + 8 < M) {
-                if (n < N) C[(size_t)(r + 8) * ldc + n] = acc[i][j][2];
-                if (n + 1 < N) C[(size_t)(r + 8) * ldc + n + 1] = acc[i][j][3];
+                if (n < N) C[(size_t)(r + 8) * N + n] = acc[i][j][2];
+                if (n + 1 < N) C[(size_t)(r + 8) * N + n + 1] = acc[i][j][3];
             }
         }
 }
 
 // One warp per token. logits row has E + 1 entries (the last is the shared-gate logit).
+// The K chunks of the logits (ks of them, [ks][T][E + 1]) are summed in chunk order into chunk 0.
 __global__ void router_topk_kernel(float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
-                                   float* __restrict__ probs, int32_t* __restrict__ idx, float* __restrict__ w,
+                                   int ks, float* __restrict__ probs, int32_t* __restrict__ idx, float* __restrict__ w,
                                    float* __restrict__ sgate) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
     float* lg = logits + (size_t)warp * (E + 1);
-    if (bias) {
-        for (int e = lane; e < E; e += 32) lg[e] += bias[e];
-        __syncwarp();
+    for (int e = lane; e <= E; e += 32) {
+        float part[kMaxKSplit];   // all chunk loads in flight at once, then summed in chunk order
+#pragma unroll
+        for (int z = 0; z < kMaxKSplit; ++z)
+            part[z] = z < ks ? logits[(size_t)z * T * (E + 1) + (size_t)warp * (E + 1) + e] : 0.f;
+        float v = part[0];
+#pragma unroll
+        for (int z = 1; z < kMaxKSplit; ++z)
+            if (z < ks) v += part[z];
+        if (bias && e < E) v += bias[e];
+        lg[e] = v;
     }
+    __syncwarp();
     float mx = -1e30f;
     for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
 #pragma unroll
@@ -155,19 +186,21 @@ int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st) {
     return FM_OK;
 }
 
-int launch_router_topk(float* logits, const float* bias, int T, int E, int k, float* probs, int32_t* idx, float* w,
-                       float* sgate, cudaStream_t st) {
-    router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, E, k, probs, idx, w, sgate);
-    FM_LAUNCH_CHECK("router_topk");
-    return FM_OK;
+// K chunks of the router GEMM: enough CTAs to cover the SMs when few tokens give few tiles.
+int router_ksplit(int T, int H, int E) {
+    const int tiles = ((E + 1 + RG_BN - 1) / RG_BN) * ((T + RG_BM - 1) / RG_BM);
+    int ks = 1;
+    while (ks < kMaxKSplit && tiles * ks < 148 && H % (2 * ks * RG_BK) == 0) ks *= 2;
+    return ks;
 }
 
 int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
                   float* logits, float* probs, int32_t* idx, float* w, float* sgate, cudaStream_t st) {
-    dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM);
-    router_logits_kernel<<<grid, 128, 0, st>>>(xb, router, logits, T, E + 1, H, E + 1);
+    const int ks = router_ksplit(T, H, E);
+    dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM, ks);
+    router_logits_kernel<<<grid, 128, 0, st>>>(xb, router, logits, T, E + 1, H);
     FM_LAUNCH_CHECK("router_logits");
-    router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, E, k, probs, idx, w, sgate);
+    router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, E, k, ks, probs, idx, w, sgate);
     FM_LAUNCH_CHECK("router_topk");
     return FM_OK;
 }
