@@ -7,7 +7,10 @@ Headline workload (the metric's 1/2/4/8-GPU line): the Qwen3.
 (H 2048, 256 experts, top-8, F 512, shared expert F 512 with sigmoid gate, Q4_1 weights) over T=8192
 bf16 tokens per GPU. A step is one fm_moe_layer call (router, dispatch, shared + routed experts,
 combine) over the step's tokens. Weights (503 MB of Q4_1) exceed the 126 MB L2, so every step
-streams them from HBM.
+streams them from HBM. With N > 1 GPUs (torchrun, one rank per GPU) the layer is expert parallel:
+rank r holds experts [r * 256 / N, (r + 1) * 256 / N), router and shared expert replicated, its own
+8192 tokens; a step is flowmoe.ep's dispatch -> NCCL all-to-all -> local experts -> all-to-all back
+-> combine (weak scaling: the tokens per GPU stay fixed).
   value   tokens/s of the whole job, inputs resident on the device, CUDA events, max over ranks;
   e2e     the same through the public API with pinned host buffers: x (bf16) and res (f32) copied
           in and out (f32) copied back inside each timed step;
@@ -279,16 +282,37 @@ def run_flowmoe(args):
     torch.cuda.set_device(local)
     hbm, tfl_burst, tfl_sus, peak_kind = peaks()
     cfg = flowmoe.MoEConfig(**C36)
-    blocks = synth_blocks(cfg, seed=0)
-    gate, up, down, wr, shared = blocks
-    layer = flowmoe.MoELayer.from_q4_1(cfg, gate, up, down, wr, shared=shared)
     T = T_HEADLINE
     x, res = synth_tokens(T, cfg.hidden, seed=rank)
-    out = torch.empty_like(res)
-    idx = torch.empty(T, cfg.top_k, dtype=torch.int32, device="cuda")
-    w = torch.empty(T, cfg.top_k, device="cuda")
     st = torch.cuda.current_stream()
-    step = lambda: layer.forward(x, res, out=out, idx=idx, w=w)  # noqa: E731
+    ep_info = {}
+    if world > 1:
+        # expert parallel: this rank's 256 / N experts, the replicated router and shared expert, its
+        # own T tokens; two all-to-all exchanges per step over NCCL
+        from flowmoe.ep import EPMoELayer, expert_range
+        eb, el = expert_range(cfg.n_experts, rank, world)
+        cfg = flowmoe.MoEConfig(**C36, e_begin=eb, e_local=el)
+        blocks = synth_blocks(cfg, seed=0)
+        gate, up, down, wr, shared = blocks
+        layer = EPMoELayer(flowmoe.MoELayer.from_q4_1(cfg, gate, up, down, wr, shared=shared), max_tokens=T)
+        out_box = [None]
+
+        def step():
+            out_box[0] = layer(x, res, timings=ep_info)
+
+        def forward_into(xd, rd):
+            return layer(xd, rd)
+    else:
+        blocks = synth_blocks(cfg, seed=0)
+        gate, up, down, wr, shared = blocks
+        layer = flowmoe.MoELayer.from_q4_1(cfg, gate, up, down, wr, shared=shared)
+        out = torch.empty_like(res)
+        idx = torch.empty(T, cfg.top_k, dtype=torch.int32, device="cuda")
+        w = torch.empty(T, cfg.top_k, device="cuda")
+        step = lambda: layer.forward(x, res, out=out, idx=idx, w=w)  # noqa: E731
+
+        def forward_into(xd, rd):
+            return layer.forward(xd, rd, out=out, idx=idx, w=w)
 
     # device-resident timing, with the stage events recorded live in the timed region
     for _ in range(args.warmup):
@@ -305,7 +329,10 @@ def run_flowmoe(args):
     ms_max = max_over_ranks(ms, world)
     value = T * world / (ms_max * 1e-3)
     stage_ms = {k: round(v / args.steps, 4) for k, v in stages.items()}
-    pairs = T * cfg.top_k
+    if world > 1:
+        # the rest of the step: the count exchange, its device->host read and the two row exchanges
+        stage_ms["exchange"] = round(ms - sum(stages.values()) / args.steps, 4)
+    pairs = ep_info.get("recv_rows", T * cfg.top_k)
     gu_ms = stages["gate_up"] / args.steps
     gu_tflops = gate_up_flops(cfg, pairs, T) / (gu_ms * 1e-3) / 1e12
 
@@ -318,12 +345,11 @@ def run_flowmoe(args):
     def e2e_step():
         xd.copy_(xh, non_blocking=True)
         rd.copy_(rh, non_blocking=True)
-        layer.forward(xd, rd, out=out, idx=idx, w=w)
-        oh.copy_(out, non_blocking=True)
+        oh.copy_(forward_into(xd, rd), non_blocking=True)
 
     e2e_ms = max_over_ranks(time_steps(e2e_step, args.steps, 2, world, st), world)
     e2e = {"value": round(T * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
-           "h2d_bytes_per_step": x.numel() * 2 + res.numel() * 4, "d2h_bytes_per_step": out.numel() * 4}
+           "h2d_bytes_per_step": x.numel() * 2 + res.numel() * 4, "d2h_bytes_per_step": oh.numel() * 4}
 
     line = None
     if rank == 0:
@@ -342,8 +368,9 @@ def run_flowmoe(args):
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": WORKLOAD, "hidden": cfg.hidden, "experts": cfg.n_experts, "top_k": cfg.top_k,
                            "ffn": cfg.ffn, "shared_ffn": cfg.shared_ffn, "tokens_per_gpu": T, "weights": "q4_1",
-                           "parallelism": "replica" if world > 1 else "single",
-                           "l2": "expert weights 503 MB > 126 MB L2 streamed every step"},
+                           "parallelism": f"ep{world}" if world > 1 else "single",
+                           "l2": "expert weights 503 MB > 126 MB L2 streamed every step",
+                           **({"experts_per_gpu": cfg.local, "recv_rows_rank0": pairs} if world > 1 else {})},
                 "roofline": {"bound": "tensor", "kernel": "expert_gemm<gate_up>",
                              "achieved": round(gu_tflops, 2), "peak": tfl_sus, "unit": "TFLOP/s",
                              "frac": round(gu_tflops / tfl_sus, 4), "traffic": traffic,

@@ -140,6 +140,40 @@ FM_API int fm_moe_dispatch(const fm_layer* L, const int32_t* idx, int32_t T, int
 FM_API int fm_moe_layer_noalloc(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, int32_t T,
                                 int32_t t_real, float* out, int32_t* idx, float* w, void* stream);
 
+/* Expert parallel (EP) over G ranks, one process per GPU. No counterpart in the reference, which runs
+ * every expert on one NPU (Core::moe_block, core.cpp:5150-5259); these three stages split that call
+ * around the two all-to-all exchanges the host makes (flowmoe/ep.py, NCCL over NVLink):
+ *   rank r owns experts [e_begin, e_begin + e_local) = [r * E / G, (r + 1) * E / G); the router
+ *   ([E + 1, H], replicated) and the shared expert (replicated) run on each rank's own tokens.
+ * Scratch needs: fm_ep_workspace_size for T own tokens and R received rows (the largest R the call
+ * will see; R <= G * T * k). */
+FM_API int fm_ep_workspace_size(const fm_layer* L, int32_t T, int32_t R, int32_t n_ranks, size_t* bytes);
+
+/* Stage 1: router over all E experts (idx, w, shared_gate as fm_router_topk), then the stable
+ * expert sort over ALL experts: counts [E] per expert, pos [t_real, k] = each pair's row in the sorted
+ * order, and xsend [t_real * k, H] bf16 = the sorted rows. The rows for rank g are the contiguous
+ * range of experts [g * e_local, (g + 1) * e_local). xb_out [T, H] receives xm as bf16 when
+ * xm_dtype is FM_F32 (fm_ep_experts needs it); it may be NULL for FM_BF16 input. */
+FM_API int fm_ep_dispatch(const fm_layer* L, const void* xm, int32_t xm_dtype, int32_t T, int32_t t_real,
+                          uint16_t* xb_out, int32_t* idx, float* w, float* shared_gate, int32_t* counts, int32_t* pos,
+                          uint16_t* xsend, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stage 2 (after the dispatch exchange): xrecv [R, H] bf16 = the rows every rank sent here, source
+ * rank major and local expert ascending within a source; recv_counts [n_ranks, e_local] (device) =
+ * rows per (source, local expert). Writes out [T, H] = res + shared_gate * shared_expert(xb) for this
+ * rank's own tokens (rows >= t_real: res), and yrecv [R, H] bf16 = each received row's unweighted
+ * expert output, in the received order (the rows the combine exchange sends back). */
+FM_API int fm_ep_experts(const fm_layer* L, const uint16_t* xrecv, int32_t R, const int32_t* recv_counts,
+                         int32_t n_ranks, const uint16_t* xb, const float* shared_gate, const float* res, int32_t T,
+                         int32_t t_real, float* out, uint16_t* yrecv, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* Stage 3 (after the combine exchange): ysorted [t_real * k, H] bf16 = the expert outputs in the
+ * sorted order of stage 1; out[t] += sum of w * y over t's pairs in ascending expert order, t < t_real
+ * (the weighted scatter of core.cpp:5244-5252). */
+FM_API int fm_ep_combine(const fm_layer* L, float* out, const uint16_t* ysorted, const int32_t* pos, const int32_t* idx,
+                         const float* w, int32_t T, int32_t t_real, void* stream);
+
 /* Synchronises `stream` and returns FM_ETIMEOUT if a bounded device wait of the last call on this
  * workspace gave up, else FM_EINVAL_EXPERT if it met an expert id outside the range the block accepts
  * (the check core.cpp:5159-5160 throws on). */

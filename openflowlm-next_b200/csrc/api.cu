@@ -532,6 +532,10 @@ extern "C" FM_API int fm_moe_check(void* workspace, void* stream) {
     if (cudaStreamSynchronize(st) != cudaSuccess) return cuda_status(cudaGetLastError(), "stream sync");
     if (cudaMemcpy(word, workspace, sizeof(word), cudaMemcpyDeviceToHost) != cudaSuccess)
         return cuda_status(cudaGetLastError(), "read error words");
+    if (word[1] == FM_EINVAL_SHAPE) {
+        set_error("expert parallel: the received row counts are negative or do not add up to R; no rows were computed");
+        return word[1];
+    }
     if (word[1]) {
         set_error("a device wait gave up (status %d): the block's output is incomplete", word[1]);
         return word[1];
@@ -541,4 +545,248 @@ extern "C" FM_API int fm_moe_check(void* workspace, void* stream) {
         return FM_EINVAL_EXPERT;
     }
     return FM_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Expert parallel: three device stages around the host's two all-to-all exchanges (see flowmoe/ep.py).
+//   fm_ep_dispatch  router + stable sort over ALL experts + gather: the rows bound for rank g are the
+//                   contiguous expert range [g * e_local, (g + 1) * e_local) of the sorted matrix;
+//   fm_ep_experts   the rows received from every rank regrouped expert-major, this rank's experts
+//                   (tcgen05 grouped GEMMs) written back as unweighted bf16 rows in the received order,
+//                   and the replicated shared expert of this rank's own tokens added into out = res;
+//   fm_ep_combine   out[t] += w * y for t's pairs, y the rows the expert ranks returned.
+namespace fm {
+
+struct EpDispatchLayout {
+    size_t err, logits, counts, offsets, blk_hist, pair, gu_list, dn_list, total;
+    int P, nblk;
+};
+
+static EpDispatchLayout ep_dispatch_layout(const fm_layer* L, int T) {
+    EpDispatchLayout o{};
+    const int H = L->hidden, E = L->n_experts, k = L->top_k;
+    o.P = T * k;
+    o.nblk = (o.P + kChunk - 1) / kChunk;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t a = off; off = align256(off + bytes); return a; };
+    o.err = take(16);
+    o.logits = take((size_t)router_ksplit(T, H, E) * T * (E + 1) * 4);
+    o.counts = take((size_t)(E + 1) * 4);
+    o.offsets = take((size_t)(E + 2) * 4);
+    o.blk_hist = take((size_t)o.nblk * E * 4);
+    o.pair = take((size_t)o.P * 4);
+    o.gu_list = take(16);
+    o.dn_list = take(16);
+    o.total = off;
+    return o;
+}
+
+struct EpExpertsLayout {
+    size_t err, seg, src_off, dst_off, rowmap, gu_list, dn_list, xexp, hexp, total;
+    int rows, fmax, max_gu, max_dn;
+};
+
+static EpExpertsLayout ep_experts_layout(const fm_layer* L, int T, int R, int G) {
+    EpExpertsLayout o{};
+    const int H = L->hidden, El = L->e_local;
+    o.rows = R + T;
+    o.fmax = L->ffn > L->shared_ffn ? L->ffn : L->shared_ffn;
+    const int rt_routed = R / kBNTc + El;
+    const int rt_shared = (T + kBNTc - 1) / kBNTc;
+    o.max_gu = rt_routed * (L->ffn / 64) + rt_shared * (L->shared_ffn / 64);
+    o.max_dn = (rt_routed + (L->shared_ffn ? rt_shared : 0)) * (H / kTileRows);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t a = off; off = align256(off + bytes); return a; };
+    o.err = take(16);
+    o.seg = take((size_t)El * 3 * 4);
+    o.src_off = take((size_t)G * El * 4);
+    o.dst_off = take((size_t)G * El * 4);
+    o.rowmap = take((size_t)(R > 0 ? R : 1) * 4);
+    o.gu_list = take((size_t)(4 + 4 * o.max_gu) * 4);
+    o.dn_list = take((size_t)(4 + 4 * o.max_dn) * 4);
+    o.xexp = take((size_t)o.rows * H * 2);
+    o.hexp = take((size_t)o.rows * o.fmax * 2);
+    o.total = off;
+    return o;
+}
+
+static int ep_check(const fm_layer* L, int T, int R, int G) {
+    if (int rc = validate(L, T)) return rc;
+    if (G <= 0 || R < 0 || L->e_local <= 0 || L->e_local > 1024 || (size_t)G * L->e_local > (1u << 20)) {
+        set_error("expert parallel: bad n_ranks %d / received rows %d / local experts %d (1..1024)", G, R, L->e_local);
+        return FM_EINVAL_SHAPE;
+    }
+    return FM_OK;
+}
+
+static int ws_ok(size_t need, void* ws, size_t bytes) {
+    if (!ws || bytes < need) {
+        set_error("workspace of %zu B is smaller than the %zu B needed", bytes, need);
+        return FM_EWORKSPACE;
+    }
+    if (reinterpret_cast<uintptr_t>(ws) & 255) {
+        set_error("workspace must be 256-byte aligned");
+        return FM_EWORKSPACE;
+    }
+    return FM_OK;
+}
+
+}  // namespace fm
+
+extern "C" FM_API int fm_ep_workspace_size(const fm_layer* L, int32_t T, int32_t R, int32_t n_ranks, size_t* bytes) {
+    g_err[0] = 0;
+    if (int rc = ep_check(L, T, R, n_ranks)) return rc;
+    const size_t a = ep_dispatch_layout(L, T).total, b = ep_experts_layout(L, T, R, n_ranks).total;
+    *bytes = a > b ? a : b;
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_ep_dispatch(const fm_layer* L, const void* xm, int32_t xm_dtype, int32_t T, int32_t t_real,
+                                     uint16_t* xb_out, int32_t* idx, float* w, float* shared_gate, int32_t* counts,
+                                     int32_t* pos, uint16_t* xsend, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+    g_err[0] = 0;
+    if (int rc = validate(L, T)) return rc;
+    if (t_real < 0 || t_real > T) {
+        set_error("t_real %d outside [0, T=%d]", t_real, T);
+        return FM_EINVAL_SHAPE;
+    }
+    const int H = L->hidden, E = L->n_experts, k = L->top_k;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (T == 0) {
+        if (cudaMemsetAsync(counts, 0, (size_t)E * 4, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
+        return FM_OK;
+    }
+    const EpDispatchLayout lo = ep_dispatch_layout(L, T);
+    if (int rc = ws_ok(lo.total, workspace, workspace_bytes)) return rc;
+    const uint16_t* xb = static_cast<const uint16_t*>(xm);
+    if (xm_dtype == FM_F32) {
+        if (!xb_out) {
+            set_error("fm_ep_dispatch: f32 activations need xb_out for their bf16 copy");
+            return FM_EINVAL_SHAPE;
+        }
+        prof_begin(kStageToBf16, st);
+        if (int rc = launch_to_bf16(static_cast<const float*>(xm), xb_out, (long long)T * H, st)) return rc;
+        prof_end(kStageToBf16, st);
+        xb = xb_out;
+    } else if (xm_dtype != FM_BF16) {
+        set_error("xm dtype %d is neither FM_F32 nor FM_BF16", xm_dtype);
+        return FM_EINVAL_SHAPE;
+    }
+    if (cudaMemsetAsync(at<int>(workspace, lo.err), 0, 16, st) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "memset");
+    prof_begin(kStageRouter, st);
+    if (int rc = launch_router(xb, L->router, L->router_bias, T, H, E, k, at<float>(workspace, lo.logits), nullptr, idx, w,
+                               shared_gate, st))
+        return rc;
+    prof_end(kStageRouter, st);
+    const int P = t_real * k;
+    prof_begin(kStageDispatch, st);
+    int rc = launch_dispatch(idx, P, 0, E, E, lo.P, 0, at<int>(workspace, lo.blk_hist), (P + kChunk - 1) / kChunk,
+                             at<int>(workspace, lo.counts), at<int>(workspace, lo.offsets), pos,
+                             at<int>(workspace, lo.pair), at<int>(workspace, lo.gu_list), 0, 0,
+                             at<int>(workspace, lo.dn_list), 0, kBNTc, at<int>(workspace, lo.err), st);
+    if (rc) return rc;
+    if (cudaMemcpyAsync(counts, at<int>(workspace, lo.counts), (size_t)E * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "counts copy");
+    prof_end(kStageDispatch, st);
+    prof_begin(kStageGather, st);
+    rc = launch_gather(xb, at<int>(workspace, lo.pair), at<int>(workspace, lo.counts), at<int>(workspace, lo.offsets), E,
+                       lo.P, k, H, P, xsend, st);
+    prof_end(kStageGather, st);
+    return rc;
+}
+
+extern "C" FM_API int fm_ep_experts(const fm_layer* L, const uint16_t* xrecv, int32_t R, const int32_t* recv_counts,
+                                    int32_t n_ranks, const uint16_t* xb, const float* shared_gate, const float* res,
+                                    int32_t T, int32_t t_real, float* out, uint16_t* yrecv, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    g_err[0] = 0;
+    if (int rc = ep_check(L, T, R, n_ranks)) return rc;
+    if (t_real < 0 || t_real > T) {
+        set_error("t_real %d outside [0, T=%d]", t_real, T);
+        return FM_EINVAL_SHAPE;
+    }
+    if (T == 0 && R == 0) return FM_OK;
+    const int H = L->hidden, El = L->e_local;
+    const EpExpertsLayout lo = ep_experts_layout(L, T, R, n_ranks);
+    if (int rc = ws_ok(lo.total, workspace, workspace_bytes)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool shared_on = L->shared_ffn > 0 && L->shared_gate_up && L->shared_down && shared_gate && t_real > 0;
+    const int srows = shared_on ? t_real : 0;
+    if (cudaMemsetAsync(at<int>(workspace, lo.err), 0, 16, st) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "memset");
+    if (T > 0 && cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "out = res");
+    prof_begin(kStageGather, st);
+    int rc = launch_ep_regroup(recv_counts, n_ranks, El, xrecv, R, xb, srows, H, at<int>(workspace, lo.seg),
+                               at<int>(workspace, lo.src_off), at<int>(workspace, lo.dst_off),
+                               at<uint16_t>(workspace, lo.xexp), at<int>(workspace, lo.rowmap),
+                               at<int>(workspace, lo.err), st);
+    if (rc) return rc;
+    prof_end(kStageGather, st);
+    prof_begin(kStageDispatch, st);
+    rc = launch_seg_lists(at<int>(workspace, lo.seg), El, El, R, srows, at<int>(workspace, lo.gu_list), L->ffn / 64,
+                          L->shared_ffn / 64, at<int>(workspace, lo.dn_list), H / kTileRows, kBNTc, st);
+    if (rc) return rc;
+    prof_end(kStageDispatch, st);
+    TcLaunch g{};
+    g.max_items = lo.max_gu;
+    g.list = at<int>(workspace, lo.gu_list);
+    g.act = at<uint16_t>(workspace, lo.xexp);
+    g.act_rows = lo.rows;
+    g.act_cols = H;
+    g.act_ld = H;
+    g.w_routed = L->gate_up;
+    g.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
+    g.w_shared = L->shared_gate_up;
+    g.shared_group = El;
+    g.K_routed = H;
+    g.K_shared = H;
+    g.h_out = at<uint16_t>(workspace, lo.hexp);
+    g.h_ld = lo.fmax;
+    g.err = at<int>(workspace, lo.err) + 1;
+    prof_begin(kStageGateUp, st);
+    if ((rc = launch_expert_tc(true, g, st))) return rc;
+    prof_end(kStageGateUp, st);
+    TcLaunch d{};
+    d.max_items = lo.max_dn;
+    d.list = at<int>(workspace, lo.dn_list);
+    d.act = at<uint16_t>(workspace, lo.hexp);
+    d.act_rows = lo.rows;
+    d.act_cols = lo.fmax;
+    d.act_ld = lo.fmax;
+    d.w_routed = L->down;
+    d.w_routed_stride = (size_t)H * L->ffn / 32 * 20;
+    d.w_shared = L->shared_down;
+    d.shared_group = El;
+    d.K_routed = L->ffn;
+    d.K_shared = L->shared_ffn;
+    d.out = out;
+    d.H = H;
+    d.pair = at<int>(workspace, lo.rowmap);
+    d.k = L->top_k;
+    d.shared_base = R;
+    d.sgate = shared_gate;
+    d.y_rows = yrecv;
+    d.err = at<int>(workspace, lo.err) + 1;
+    prof_begin(kStageDown, st);
+    if ((rc = launch_expert_tc(false, d, st))) return rc;
+    prof_end(kStageDown, st);
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_ep_combine(const fm_layer* L, float* out, const uint16_t* ysorted, const int32_t* pos,
+                                    const int32_t* idx, const float* w, int32_t T, int32_t t_real, void* stream) {
+    g_err[0] = 0;
+    if (int rc = validate(L, T)) return rc;
+    if (t_real < 0 || t_real > T) {
+        set_error("t_real %d outside [0, T=%d]", t_real, T);
+        return FM_EINVAL_SHAPE;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    prof_begin(kStageCombine, st);
+    const int rc = launch_combine_bf16(out, ysorted, pos, idx, w, T, t_real, L->top_k, L->hidden, st);
+    prof_end(kStageCombine, st);
+    return rc;
 }

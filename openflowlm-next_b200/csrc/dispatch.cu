@@ -204,6 +204,145 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ xb, const int* _
     for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
 }
 
+// Work lists from a segment table seg[i] = (local expert, first row, rows) (expert parallel: the rows
+// one source rank sent for one expert), plus the shared expert's rows [shared_base, +shared_rows) as
+// group G = e_local. One block of 1024 threads; segments in table order.
+__global__ void __launch_bounds__(1024) seg_lists_kernel(const int* __restrict__ seg, int nseg, int shared_group,
+                                                         int shared_base, int shared_rows, int* __restrict__ gu_list,
+                                                         int gu_bands, int gu_bands_shared, int* __restrict__ dn_list,
+                                                         int dn_bands, int bn) {
+    __shared__ int sh[32];
+    int gu_carry = 0, dn_carry = 0;
+    const int nall = nseg + (shared_rows > 0 ? 1 : 0);
+    for (int i0 = 0; i0 < nall; i0 += 1024) {
+        const int i = i0 + threadIdx.x;
+        int g = 0, row0 = 0, cnt = 0, gub = 0;
+        if (i < nseg) {
+            g = seg[3 * i];
+            row0 = seg[3 * i + 1];
+            cnt = seg[3 * i + 2];
+            gub = gu_bands;
+        } else if (i < nall) {
+            g = shared_group;
+            row0 = shared_base;
+            cnt = shared_rows;
+            gub = gu_bands_shared;
+        }
+        const int rt = (cnt + bn - 1) / bn;
+        int tgu = 0, tdn = 0;
+        const int egu = block_exclusive_scan(rt * gub, sh, &tgu);
+        const int edn = block_exclusive_scan(rt * dn_bands, sh, &tdn);
+        if (i < nall && cnt > 0) {
+            emit_tiles(gu_list, gu_carry + egu, g, gub, row0, cnt, bn);
+            emit_tiles(dn_list, dn_carry + edn, g, dn_bands, row0, cnt, bn);
+        }
+        gu_carry += tgu;
+        dn_carry += tdn;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        gu_list[0] = gu_carry;
+        dn_list[0] = dn_carry;
+    }
+}
+
+// Expert parallel receive side. rc[s * El + j] = rows of local expert j sent by source rank s; the rows
+// arrive source-major (all of source 0's rows, local experts ascending, then source 1's, ...).
+// ep_plan: seg[j] = (j, first expert-major row, rows), and per (s, j) the first source-major row
+// src_off and the first expert-major row dst_off (sources ascending within an expert). One block of
+// 1024 threads, El <= 1024. Counts that are negative or do not add up to R set err[1] =
+// FM_EINVAL_SHAPE and leave every segment empty, so no later kernel touches a row past R.
+__global__ void __launch_bounds__(1024) ep_plan_kernel(const int* __restrict__ rc, int G, int El, int R,
+                                                       int* __restrict__ seg, int* __restrict__ src_off,
+                                                       int* __restrict__ dst_off, int* __restrict__ err) {
+    __shared__ int sh[32];
+    __shared__ int bad;
+    const int j = threadIdx.x;
+    if (j == 0) bad = 0;
+    __syncthreads();
+    int tot = 0;
+    if (j < El)
+        for (int s = 0; s < G; ++s) {
+            const int c = rc[s * El + j];
+            if (c < 0) bad = 1;
+            tot += c;
+        }
+    int all = 0;
+    const int base = block_exclusive_scan(j < El ? tot : 0, sh, &all);
+    const bool ok = !bad && all == R;
+    if (!ok && j == 0) atomicExch(err + 1, FM_EINVAL_SHAPE);
+    if (j < El) {
+        seg[3 * j] = j;
+        seg[3 * j + 1] = ok ? base : 0;
+        seg[3 * j + 2] = ok ? tot : 0;
+        int run = base;
+        for (int s = 0; s < G; ++s) {
+            dst_off[s * El + j] = run;
+            run += rc[s * El + j];
+        }
+    }
+    int carry = 0;
+    for (int s = 0; s < G; ++s) {
+        int t = 0;
+        const int ex = block_exclusive_scan(j < El ? rc[s * El + j] : 0, sh, &t);
+        if (j < El) src_off[s * El + j] = carry + ex;
+        carry += t;
+    }
+}
+
+// One warp per expert-major row: rows [0, R) come from the received rows (the (s, j) segment holding
+// source row r is the last with src_off <= r, found by binary search), rows [R, R + t_real) are this
+// rank's own tokens for the shared expert. rowmap[dst] = source-major row r.
+__global__ void ep_regroup_kernel(const uint16_t* __restrict__ xrecv, int R, const int* __restrict__ src_off,
+                                  const int* __restrict__ dst_off, int nseg, const uint16_t* __restrict__ xb, int t_real,
+                                  int H, uint16_t* __restrict__ xexp, int* __restrict__ rowmap,
+                                  const int* __restrict__ err) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const uint4* src;
+    int dst;
+    if (row < R) {
+        int lo = 0, hi = nseg - 1;   // last i with src_off[i] <= row
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (src_off[mid] <= row) lo = mid;
+            else hi = mid - 1;
+        }
+        if (err[1]) return;   // the plan found counts that do not add up to R
+        dst = dst_off[lo] + (row - src_off[lo]);
+        if (dst < 0 || dst >= R) return;
+        src = reinterpret_cast<const uint4*>(xrecv + (size_t)row * H);
+        if (lane == 0) rowmap[dst] = row;
+    } else if (row < R + t_real) {
+        dst = row;
+        src = reinterpret_cast<const uint4*>(xb + (size_t)(row - R) * H);
+    } else {
+        return;
+    }
+    uint4* d = reinterpret_cast<uint4*>(xexp + (size_t)dst * H);
+    for (int i = lane; i < H / 8; i += 32) d[i] = src[i];
+}
+
+int launch_ep_regroup(const int* rc, int G, int El, const uint16_t* xrecv, int R, const uint16_t* xb, int t_real, int H,
+                      int* seg, int* src_off, int* dst_off, uint16_t* xexp, int* rowmap, int* err, cudaStream_t st) {
+    ep_plan_kernel<<<1, 1024, 0, st>>>(rc, G, El, R, seg, src_off, dst_off, err);
+    FM_LAUNCH_CHECK("ep_plan");
+    const int rows = R + t_real;
+    if (rows > 0) {
+        ep_regroup_kernel<<<(rows + 7) / 8, 256, 0, st>>>(xrecv, R, src_off, dst_off, G * El, xb, t_real, H, xexp, rowmap,
+                                                          err);
+        FM_LAUNCH_CHECK("ep_regroup");
+    }
+    return FM_OK;
+}
+
+int launch_seg_lists(const int* seg, int nseg, int shared_group, int shared_base, int shared_rows, int* gu_list,
+                     int gu_bands, int gu_bands_shared, int* dn_list, int dn_bands, int bn, cudaStream_t st) {
+    seg_lists_kernel<<<1, 1024, 0, st>>>(seg, nseg, shared_group, shared_base, shared_rows, gu_list, gu_bands,
+                                        gu_bands_shared, dn_list, dn_bands, bn);
+    FM_LAUNCH_CHECK("seg_lists");
+    return FM_OK;
+}
+
 int launch_dispatch(const int32_t* idx, int P, int e_begin, int e_local, int E, int shared_base, int shared_rows,
                     int* blk_hist, int nblk,
                     int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,

@@ -189,4 +189,63 @@ int launch_combine(const float* res, const float* y, const int* pos, const int32
     return FM_OK;
 }
 
+// Expert-parallel combine: out[t] += sum over t's pairs in ascending expert order of w * y[pos], y the
+// bf16 rows returned by the expert ranks in the sender's sorted order; out already holds res plus the
+// gated shared expert. Rows t >= t_real are left as they are.
+__global__ void combine_bf16_kernel(float* __restrict__ out, const uint16_t* __restrict__ y, const int* __restrict__ pos,
+                                    const int32_t* __restrict__ idx, const float* __restrict__ w, int t_real, int k,
+                                    int H) {
+    const int t = blockIdx.x;
+    if (t >= t_real) return;
+    __shared__ int srow[kMaxTopK];
+    __shared__ float sw[kMaxTopK];
+    __shared__ int n_sel;
+    if (threadIdx.x == 0) {
+        int n = 0, ord[kMaxTopK], ids[kMaxTopK];
+        for (int s = 0; s < k; ++s) {
+            const int e = idx[(size_t)t * k + s];
+            int j = n;
+            while (j > 0 && ids[j - 1] > e) { ids[j] = ids[j - 1]; ord[j] = ord[j - 1]; --j; }
+            ids[j] = e;
+            ord[j] = s;
+            ++n;
+        }
+        int m = 0;
+        for (int j = 0; j < n; ++j) {
+            const int p = pos[(size_t)t * k + ord[j]];
+            if (p >= 0) { srow[m] = p; sw[m] = w[(size_t)t * k + ord[j]]; ++m; }
+        }
+        n_sel = m;
+    }
+    __syncthreads();
+    const int n = n_sel;
+    const int i = blockIdx.y * blockDim.x + threadIdx.x;   // 4-column group
+    if (i >= H / 4) return;
+    float4 o = reinterpret_cast<const float4*>(out + (size_t)t * H)[i];
+    uint2 v[kMaxTopK];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+        if (j < n) v[j] = reinterpret_cast<const uint2*>(y + (size_t)srow[j] * H)[i];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+        if (j < n) {
+            const float ww = sw[j];
+            o.x += ww * __uint_as_float(v[j].x << 16);
+            o.y += ww * __uint_as_float(v[j].x & 0xFFFF0000u);
+            o.z += ww * __uint_as_float(v[j].y << 16);
+            o.w += ww * __uint_as_float(v[j].y & 0xFFFF0000u);
+        }
+    reinterpret_cast<float4*>(out + (size_t)t * H)[i] = o;
+}
+
+int launch_combine_bf16(float* out, const uint16_t* y, const int* pos, const int32_t* idx, const float* w, int T,
+                        int t_real, int k, int H, cudaStream_t st) {
+    if (t_real <= 0) return FM_OK;
+    dim3 grid(t_real, (H / 4 + 255) / 256);
+    combine_bf16_kernel<<<grid, 256, 0, st>>>(out, y, pos, idx, w, t_real, k, H);
+    FM_LAUNCH_CHECK("combine_bf16");
+    (void)T;
+    return FM_OK;
+}
+
 }  // namespace fm

@@ -69,6 +69,7 @@ struct TcArgs {
     int k;
     int shared_base;
     const float* sgate;
+    uint16_t* y_rows;   // DOWN, expert-parallel mode: routed row r's y, unweighted bf16, goes to y_rows[pair[r]]
     int* err;
 };
 
@@ -313,6 +314,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
                     if (it.g == a.shared_group) {
                         t = rrow - a.shared_base;
                         wv = a.sgate[t];
+                    } else if (a.y_rows) {
+                        t = a.pair[rrow];   // expert-major row -> the received row it came from
+                        wv = 1.0f;
                     } else {
                         const int p = a.pair[rrow];
                         t = p / a.k;
@@ -371,6 +375,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
                         const int j = ew * 8 + jj;
                         if (c0 + j < it.n) {
                             const float4 y = *reinterpret_cast<const float4*>(ys + j * TC_EPI_LD + lane * 4);
+                            if (a.y_rows && it.g != a.shared_group) {
+                                *reinterpret_cast<uint2*>(a.y_rows + (size_t)tok[c0 + j] * a.H + it.band * 128 + lane * 4) =
+                                    make_uint2(pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
+                                continue;
+                            }
                             red_add_v4(a.out + (size_t)tok[c0 + j] * a.H + it.band * 128 + lane * 4, y);
                         }
                     }
@@ -462,6 +471,7 @@ int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
     a.k = L.k;
     a.shared_base = L.shared_base;
     a.sgate = L.sgate;
+    a.y_rows = L.y_rows;
     a.err = L.err;
     const int grid = L.max_items < sm_count() ? L.max_items : sm_count();
     const int sm = TcSmem::total;

@@ -46,6 +46,7 @@ struct TcLaunch {
     int k;
     int shared_base;
     const float* sgate;
+    uint16_t* y_rows;
     int* err;
 };
 int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st);
@@ -78,6 +79,12 @@ int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, i
                           int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int* err,
                           cudaStream_t st);
 int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st);
+int launch_seg_lists(const int* seg, int nseg, int shared_group, int shared_base, int shared_rows, int* gu_list,
+                     int gu_bands, int gu_bands_shared, int* dn_list, int dn_bands, int bn, cudaStream_t st);
+int launch_ep_regroup(const int* rc, int G, int El, const uint16_t* xrecv, int R, const uint16_t* xb, int t_real, int H,
+                      int* seg, int* src_off, int* dst_off, uint16_t* xexp, int* rowmap, int* err, cudaStream_t st);
+int launch_combine_bf16(float* out, const uint16_t* y, const int* pos, const int32_t* idx, const float* w, int T,
+                        int t_real, int k, int H, cudaStream_t st);
 int launch_combine(const float* res, const float* y, const int* pos, const int32_t* idx, const float* w,
                    const float* sgate, int shared_on, int T, int t_real, int k, int H, int P, float* out, cudaStream_t st);
 

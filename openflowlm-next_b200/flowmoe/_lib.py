@@ -53,6 +53,10 @@ SIGNATURES = {
     "fm_moe_layer": [LP, P, I32, P, I32, I32, P, P, P, P, SZ, P],
     "fm_moe_dispatch": [LP, P, I32, I32, P, P, P, P, P, SZ, P],
     "fm_moe_layer_noalloc": [LP, P, I32, P, I32, I32, P, P, P, P],
+    "fm_ep_workspace_size": [LP, I32, I32, I32, ctypes.POINTER(SZ)],
+    "fm_ep_dispatch": [LP, P, I32, I32, I32, P, P, P, P, P, P, P, P, SZ, P],
+    "fm_ep_experts": [LP, P, I32, P, I32, P, P, P, I32, I32, P, P, P, SZ, P],
+    "fm_ep_combine": [LP, P, P, P, P, P, I32, I32, P],
     "fm_moe_check": [P, P],
     "fm_launch_count": [ctypes.POINTER(ctypes.c_ulonglong)],
     "fm_profile": [I32],

@@ -3,7 +3,7 @@
 Expert weights fp32 N(0, 0.02) quantised to GGUF Q4_1 by the oracle's restatement of gguf.quantize;
 router weight and shared gate bf16 N(0, 0.02); activations bf16 N(0, 1); residual f32 N(0, 1);
 numpy ``default_rng(seed)``. Optional Zipf(s) router bias for the prefill configs: logits +=
-ln p_{pi(e)}, p_r ~ r^-s, pi a seeded permutation (the form SURVEY 8(d) fixes).
+ln p_{pi(e)}, p_r ~ r^-s, pi a seeded permutation (the skew form the prefill benchmark uses).
 """
 from __future__ import annotations
 
