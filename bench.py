@@ -26,9 +26,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import subprocess
 import sys
-import tempfile
 import time
 from pathlib import Path
 
@@ -79,35 +77,56 @@ def barrier(world):
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clocks and throttle reasons sampled DURING the timed region: an NVML thread polling every
+    ~2 ms (the timed region is tens of milliseconds, shorter than nvidia-smi's sampling period), the
+    same counters nvidia-smi's clocks.sm / clocks_event_reasons report."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, index: int):
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
+        import threading
+        self.samples, self.err = [], None
+        self.stop_ev = threading.Event()
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.p = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            try:   # the CUDA device's own GPU, whatever CUDA_VISIBLE_DEVICES maps it to
+                self.h = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(torch.cuda.get_device_properties(index).uuid))
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:   # no NVML: report why instead of clocks
+            self.nv, self.err = None, f"nvml unavailable: {type(e).__name__}"
+            return
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+        while not self.samples and self.t.is_alive():   # the sampler is live before timing starts
+            time.sleep(0.001)
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop_ev.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((sm, rs))
+            except Exception as e:
+                self.err = f"nvml sample failed: {type(e).__name__}"
+                return
+            time.sleep(0.002)
 
     def stop(self):
-        if self.p is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.p.terminate()
-        self.p.wait()
-        self.f.seek(0)
-        rows = [r.split(", ") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
-        os.unlink(self.f.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        if self.nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err], "samples": 0}
+        self.stop_ev.set()
+        self.t.join()
+        busy = self.samples[1:] or self.samples     # the first sample is taken before the region starts
+        if not busy:
+            return {"sm_mhz": None, "sm_max_mhz": self.max, "reasons": [self.err or "no samples"], "samples": 0}
+        reasons = sorted({n for _, r in busy for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": float(np.median([c for c, _ in busy])), "sm_max_mhz": float(self.max), "reasons": reasons,
+                "samples": len(busy), "source": "nvml"}
 
 
 def time_steps(fn, steps, warmup, world, stream):
@@ -289,19 +308,31 @@ def run_flowmoe(args):
     if world > 1:
         # expert parallel: this rank's 256 / N experts, the replicated router and shared expert, its
         # own T tokens; two all-to-all exchanges per step over NCCL
-        from flowmoe.ep import EPMoELayer, expert_range
+        from flowmoe.ep import EPMoELayer, PeerEPMoELayer, expert_range
         eb, el = expert_range(cfg.n_experts, rank, world)
         cfg = flowmoe.MoEConfig(**C36, e_begin=eb, e_local=el)
         blocks = synth_blocks(cfg, seed=0)
         gate, up, down, wr, shared = blocks
-        layer = EPMoELayer(flowmoe.MoELayer.from_q4_1(cfg, gate, up, down, wr, shared=shared), max_tokens=T)
-        out_box = [None]
+        base = flowmoe.MoELayer.from_q4_1(cfg, gate, up, down, wr, shared=shared)
+        if args.ep == "peer":
+            # one fm_ep_peer_layer call: rows and y rows stored into their owners' buffers over NVLink
+            layer = PeerEPMoELayer(base, t_cap=T)
+            out = torch.empty_like(res)
+            idx = torch.empty(T, cfg.top_k, dtype=torch.int32, device="cuda")
 
-        def step():
-            out_box[0] = layer(x, res, timings=ep_info)
+            def step():
+                layer(x, res, out=out, idx=idx)
 
-        def forward_into(xd, rd):
-            return layer(xd, rd)
+            def forward_into(xd, rd):
+                return layer(xd, rd, out=out, idx=idx)
+        else:
+            layer = EPMoELayer(base, max_tokens=T)
+
+            def step():
+                layer(x, res, timings=ep_info)
+
+            def forward_into(xd, rd):
+                return layer(xd, rd)
     else:
         blocks = synth_blocks(cfg, seed=0)
         gate, up, down, wr, shared = blocks
@@ -330,9 +361,18 @@ def run_flowmoe(args):
     value = T * world / (ms_max * 1e-3)
     stage_ms = {k: round(v / args.steps, 4) for k, v in stages.items()}
     if world > 1:
-        # the rest of the step: the count exchange, its device->host read and the two row exchanges
+        # the rest of the step, outside the library's stage events (NCCL exchange: the count exchange,
+        # its device->host read and the two row exchanges; peer exchange: host launch gaps only)
         stage_ms["exchange"] = round(ms - sum(stages.values()) / args.steps, 4)
     pairs = ep_info.get("recv_rows", T * cfg.top_k)
+    if world > 1 and args.ep == "peer":
+        # rows this rank's experts received: the counts of its expert range over all ranks' tokens
+        from flowmoe.ep import expert_range
+        eb, el = expert_range(cfg.n_experts, rank, world)
+        mine = ((idx >= eb) & (idx < eb + el)).sum().to(torch.float64)
+        import torch.distributed as dist
+        dist.all_reduce(mine)
+        pairs = int(mine.item())
     gu_ms = stages["gate_up"] / args.steps
     gu_tflops = gate_up_flops(cfg, pairs, T) / (gu_ms * 1e-3) / 1e12
 
@@ -369,6 +409,8 @@ def run_flowmoe(args):
                 "config": {"workload": WORKLOAD, "hidden": cfg.hidden, "experts": cfg.n_experts, "top_k": cfg.top_k,
                            "ffn": cfg.ffn, "shared_ffn": cfg.shared_ffn, "tokens_per_gpu": T, "weights": "q4_1",
                            "parallelism": f"ep{world}" if world > 1 else "single",
+                           **({"ep_exchange": "peer stores over NVLink" if args.ep == "peer" else "nccl all_to_all"}
+                              if world > 1 else {}),
                            "l2": "expert weights 503 MB > 126 MB L2 streamed every step",
                            **({"experts_per_gpu": cfg.local, "recv_rows_rank0": pairs} if world > 1 else {})},
                 "roofline": {"bound": "tensor", "kernel": "expert_gemm<gate_up>",
@@ -381,6 +423,8 @@ def run_flowmoe(args):
     barrier(world)
     if world > 1:
         import torch.distributed as dist
+        if hasattr(layer, "close"):
+            layer.close()
         dist.destroy_process_group()
     return 0
 
@@ -394,6 +438,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: the expert-parallel exchange (peer-memory stores, or NCCL all-to-all)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

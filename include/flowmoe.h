@@ -174,6 +174,42 @@ FM_API int fm_ep_experts(const fm_layer* L, const uint16_t* xrecv, int32_t R, co
 FM_API int fm_ep_combine(const fm_layer* L, float* out, const uint16_t* ysorted, const int32_t* pos, const int32_t* idx,
                          const float* w, int32_t T, int32_t t_real, void* stream);
 
+/* ---- Expert parallel over peer memory (NVLink), no host round trip. No counterpart in the reference.
+ * Every rank allocates one symmetric buffer (fm_ipc_alloc, the same size on every rank), exchanges
+ * the handles (the host's all-gather) and maps its peers' buffers (fm_ipc_open). One fm_ep_peer_layer
+ * call then does the whole layer: router and sort as fm_ep_dispatch; the per-expert counts stored into
+ * every peer's buffer; the rows stored straight into the owning rank's receive buffer, already grouped
+ * by expert; the tcgen05 expert GEMMs, whose DOWN epilogue stores each y row straight back into the
+ * sending rank's buffer; the ordered weighted combine. Ranks synchronise through monotonic flags in the
+ * symmetric buffers with bounded device waits: a peer that does not take its step within timeout_ms
+ * makes the call end with FM_ETIMEOUT (fm_moe_check) instead of waiting for good, and no further stores
+ * go to the peers. All ranks must make the same sequence of calls on one group. */
+#define FM_EP_MAX_RANKS 16
+
+typedef struct fm_ep_group {
+    int32_t rank, n_ranks;           /* this process's rank, the group size (<= FM_EP_MAX_RANKS) */
+    int32_t t_cap;                   /* the most tokens any rank passes to one call */
+    int32_t timeout_ms;              /* bound of each device wait on the peers (0: 2000) */
+    void* sym[FM_EP_MAX_RANKS];      /* each rank's symmetric buffer as mapped here; sym[rank] is our own */
+} fm_ep_group;
+
+/* Bytes of the symmetric buffer (identical on every rank) and of the per-call workspace. */
+FM_API int fm_ep_peer_sizes(const fm_layer* L, const fm_ep_group* g, size_t* sym_bytes, size_t* ws_bytes);
+
+/* The whole expert-parallel layer for this rank's T tokens (t_real real): out [T, H] f32 = res + shared
+ * + routed experts, as fm_moe_layer; idx/w (may be NULL) receive the routing. */
+FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, const void* xm, int32_t xm_dtype, const float* res,
+                            int32_t T, int32_t t_real, float* out, int32_t* idx, float* w, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* Device memory shareable with the other processes of the node: cudaMalloc'd, zeroed, and its
+ * cudaIpcMemHandle_t (64 bytes) written to handle_out. */
+FM_API int fm_ipc_alloc(size_t bytes, void** ptr, void* handle_out);
+/* Maps another process's fm_ipc_alloc buffer (peer access enabled on demand). */
+FM_API int fm_ipc_open(const void* handle, void** ptr);
+FM_API int fm_ipc_close(void* ptr);
+FM_API int fm_ipc_free(void* ptr);
+
 /* Synchronises `stream` and returns FM_ETIMEOUT if a bounded device wait of the last call on this
  * workspace gave up, else FM_EINVAL_EXPERT if it met an expert id outside the range the block accepts
  * (the check core.cpp:5159-5160 throws on). */

@@ -790,3 +790,292 @@ extern "C" FM_API int fm_ep_combine(const fm_layer* L, float* out, const uint16_
     prof_end(kStageCombine, st);
     return rc;
 }
+
+// ---------------------------------------------------------------------------------------------------------------
+// Expert parallel over peer memory (ep_peer.cu): fm_ep_peer_layer and the IPC helpers.
+namespace fm {
+
+struct EpSymLayout {
+    size_t state, flags, cnt, meta, x, y, total;
+    int r_cap;
+};
+
+static EpSymLayout ep_sym_layout(const fm_layer* L, const fm_ep_group* g) {
+    EpSymLayout o{};
+    const int H = L->hidden, E = L->n_experts, k = L->top_k, G = g->n_ranks;
+    o.r_cap = G * g->t_cap * k;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t a = off; off = align256(off + bytes); return a; };
+    o.state = take(256);
+    o.flags = take((size_t)3 * kMaxRanksPad * 4);
+    o.cnt = take((size_t)G * E * 4);
+    o.meta = take((size_t)o.r_cap * 4);
+    o.x = take(((size_t)o.r_cap + g->t_cap) * H * 2);
+    o.y = take((size_t)g->t_cap * k * H * 2 + 16);
+    o.total = off;
+    return o;
+}
+
+struct EpPeerLayout {
+    size_t err, xb, logits, counts, offsets, blk_hist, pos, pair, idx, w, sgate, send_base, seg, gu_list, dn_list, hexp;
+    size_t total;
+    int max_gu, max_dn, fmax;
+};
+
+static EpPeerLayout ep_peer_layout(const fm_layer* L, const fm_ep_group* g, int T) {
+    EpPeerLayout o{};
+    const int H = L->hidden, E = L->n_experts, k = L->top_k, El = L->e_local, tc = g->t_cap;
+    const int r_cap = g->n_ranks * tc * k;
+    const int P = T * k, nblk = (P + kChunk - 1) / kChunk;
+    o.fmax = L->ffn > L->shared_ffn ? L->ffn : L->shared_ffn;
+    const int rt_routed = r_cap / kBNTc + El, rt_shared = (tc + kBNTc - 1) / kBNTc;
+    o.max_gu = rt_routed * (L->ffn / 64) + rt_shared * (L->shared_ffn / 64);
+    o.max_dn = (rt_routed + (L->shared_ffn ? rt_shared : 0)) * (H / kTileRows);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t a = off; off = align256(off + bytes); return a; };
+    o.err = take(16);
+    o.xb = take((size_t)T * H * 2);
+    o.logits = take((size_t)router_ksplit(T, H, E) * T * (E + 1) * 4);
+    o.counts = take((size_t)(E + 1) * 4);
+    o.offsets = take((size_t)(E + 2) * 4);
+    o.blk_hist = take((size_t)nblk * E * 4);
+    o.pos = take((size_t)P * 4);
+    o.pair = take((size_t)P * 4);
+    o.idx = take((size_t)P * 4);
+    o.w = take((size_t)P * 4);
+    o.sgate = take((size_t)T * 4);
+    o.send_base = take((size_t)E * 4);
+    o.seg = take((size_t)El * 3 * 4);
+    o.gu_list = take((size_t)(4 + 4 * o.max_gu) * 4);
+    o.dn_list = take((size_t)(4 + 4 * o.max_dn) * 4);
+    o.hexp = take(((size_t)r_cap + tc) * o.fmax * 2);
+    o.total = off;
+    return o;
+}
+
+static int ep_group_check(const fm_layer* L, const fm_ep_group* g, bool need_sym = true) {
+    if (int rc = validate(L, 0)) return rc;
+    if (!g || g->n_ranks < 1 || g->n_ranks > FM_EP_MAX_RANKS || g->rank < 0 || g->rank >= g->n_ranks || g->t_cap < 1) {
+        set_error("bad expert-parallel group (rank/n_ranks/t_cap; at most %d ranks)", FM_EP_MAX_RANKS);
+        return FM_EINVAL_SHAPE;
+    }
+    const int G = g->n_ranks, E = L->n_experts;
+    if (E % G || L->e_local != E / G || L->e_begin != g->rank * (E / G)) {
+        set_error("expert-parallel layer must hold experts [%d, %d) of %d on rank %d of %d", g->rank * (E / G),
+                  (g->rank + 1) * (E / G), E, g->rank, G);
+        return FM_EINVAL_SHAPE;
+    }
+    if ((long long)g->t_cap * L->top_k >= (1ll << 24) || (long long)G * g->t_cap * L->top_k >= (1ll << 30)) {
+        set_error("t_cap %d too large for the row metadata (t_cap * top_k < 2^24)", g->t_cap);
+        return FM_EINVAL_SHAPE;
+    }
+    for (int i = 0; need_sym && i < G; ++i)
+        if (!g->sym[i]) {
+            set_error("expert-parallel group: rank %d's symmetric buffer is not mapped", i);
+            return FM_EINVAL_SHAPE;
+        }
+    return FM_OK;
+}
+
+static int sm_count_api() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+}  // namespace fm
+
+extern "C" FM_API int fm_ep_peer_sizes(const fm_layer* L, const fm_ep_group* g, size_t* sym_bytes, size_t* ws_bytes) {
+    g_err[0] = 0;
+    if (int rc = ep_group_check(L, g, false)) return rc;
+    if (sym_bytes) *sym_bytes = ep_sym_layout(L, g).total;
+    if (ws_bytes) {
+        size_t m = 0;   // the router's split-K scratch depends on T: the largest over 1..t_cap
+        for (int T = 1; T <= g->t_cap; ++T) {
+            const size_t t = ep_peer_layout(L, g, T).total;
+            if (t > m) m = t;
+        }
+        *ws_bytes = m;
+    }
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, const void* xm, int32_t xm_dtype,
+                                       const float* res, int32_t T, int32_t t_real, float* out, int32_t* idx, float* w,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+    g_err[0] = 0;
+    if (int rc = ep_group_check(L, g)) return rc;
+    if (int rc = validate(L, T)) return rc;
+    if (T > g->t_cap || t_real < 0 || t_real > T) {
+        set_error("T=%d / t_real=%d outside the group's t_cap %d", T, t_real, g->t_cap);
+        return FM_EINVAL_SHAPE;
+    }
+    const int H = L->hidden, E = L->n_experts, k = L->top_k, El = L->e_local, G = g->n_ranks;
+    const EpSymLayout sl = ep_sym_layout(L, g);
+    const EpPeerLayout lo = ep_peer_layout(L, g, T);
+    if (int rc = ws_ok(lo.total, workspace, workspace_bytes)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    EpPeerArgs a{};
+    for (int i = 0; i < G; ++i) a.sym[i] = static_cast<uint8_t*>(g->sym[i]);
+    a.off_flags = sl.flags;
+    a.off_cnt = sl.cnt;
+    a.off_meta = sl.meta;
+    a.off_x = sl.x;
+    a.off_y = sl.y;
+    a.state = reinterpret_cast<int*>(a.sym[g->rank] + sl.state);
+    a.err = at<int>(workspace, lo.err);
+    a.rank = g->rank;
+    a.G = G;
+    a.E = E;
+    a.El = El;
+    a.H = H;
+    a.k = k;
+    a.r_cap = sl.r_cap;
+    a.timeout_ns = (long long)(g->timeout_ms > 0 ? g->timeout_ms : 2000) * 1000000ll;
+    if (cudaMemsetAsync(a.err, 0, 16, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
+    const uint16_t* xb = static_cast<const uint16_t*>(xm);
+    if (xm_dtype == FM_F32) {
+        if (T > 0) {
+            prof_begin(kStageToBf16, st);
+            if (int rc = launch_to_bf16(static_cast<const float*>(xm), at<uint16_t>(workspace, lo.xb), (long long)T * H, st))
+                return rc;
+            prof_end(kStageToBf16, st);
+        }
+        xb = at<uint16_t>(workspace, lo.xb);
+    } else if (xm_dtype != FM_BF16) {
+        set_error("xm dtype %d is neither FM_F32 nor FM_BF16", xm_dtype);
+        return FM_EINVAL_SHAPE;
+    }
+    int32_t* ids = idx ? idx : at<int32_t>(workspace, lo.idx);
+    float* wts = w ? w : at<float>(workspace, lo.w);
+    float* sg = at<float>(workspace, lo.sgate);
+    const bool shared_on = L->shared_ffn > 0 && L->shared_gate_up && L->shared_down && t_real > 0;
+    const int P = t_real * k;
+    int rc = FM_OK;
+    prof_begin(kStageRouter, st);
+    if (T > 0 && (rc = launch_router(xb, L->router, L->router_bias, T, H, E, k, at<float>(workspace, lo.logits), nullptr,
+                                     ids, wts, sg, st)))
+        return rc;
+    prof_end(kStageRouter, st);
+    prof_begin(kStageDispatch, st);
+    int* counts = at<int>(workspace, lo.counts);
+    int* offsets = at<int>(workspace, lo.offsets);
+    if ((rc = launch_dispatch(ids, P, 0, E, E, T * k, 0, at<int>(workspace, lo.blk_hist), (P + kChunk - 1) / kChunk,
+                              counts, offsets, at<int>(workspace, lo.pos), at<int>(workspace, lo.pair),
+                              at<int>(workspace, lo.gu_list), 0, 0, at<int>(workspace, lo.dn_list), 0, kBNTc, a.err, st)))
+        return rc;
+    if ((rc = launch_ep_post_counts(a, counts, st))) return rc;
+    if ((rc = launch_ep_plan_peer(a, at<int>(workspace, lo.send_base), at<int>(workspace, lo.seg), st))) return rc;
+    if ((rc = launch_seg_lists(at<int>(workspace, lo.seg), El, El, sl.r_cap, shared_on ? t_real : 0,
+                               at<int>(workspace, lo.gu_list), L->ffn / 64, L->shared_ffn / 64,
+                               at<int>(workspace, lo.dn_list), H / kTileRows, kBNTc, st)))
+        return rc;
+    prof_end(kStageDispatch, st);
+    prof_begin(kStageGather, st);
+    if ((rc = launch_ep_scatter_rows(a, xb, at<int>(workspace, lo.pair), ids, offsets, at<int>(workspace, lo.send_base), P,
+                                     shared_on ? t_real : 0, sm_count_api(), st)))
+        return rc;
+    if ((rc = launch_ep_wait(a, 1, st))) return rc;
+    prof_end(kStageGather, st);
+    if (T > 0 && cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "out = res");
+    uint8_t* mine = a.sym[g->rank];
+    TcLaunch gu{};
+    gu.max_items = lo.max_gu;
+    gu.list = at<int>(workspace, lo.gu_list);
+    gu.act = reinterpret_cast<const uint16_t*>(mine + sl.x);
+    gu.act_rows = sl.r_cap + g->t_cap;
+    gu.act_cols = H;
+    gu.act_ld = H;
+    gu.w_routed = L->gate_up;
+    gu.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
+    gu.w_shared = L->shared_gate_up;
+    gu.shared_group = El;
+    gu.K_routed = H;
+    gu.K_shared = H;
+    gu.h_out = at<uint16_t>(workspace, lo.hexp);
+    gu.h_ld = lo.fmax;
+    gu.err = a.err + 1;
+    prof_begin(kStageGateUp, st);
+    if ((rc = launch_expert_tc(true, gu, st))) return rc;
+    prof_end(kStageGateUp, st);
+    TcLaunch d{};
+    d.max_items = lo.max_dn;
+    d.list = at<int>(workspace, lo.dn_list);
+    d.act = at<uint16_t>(workspace, lo.hexp);
+    d.act_rows = sl.r_cap + g->t_cap;
+    d.act_cols = lo.fmax;
+    d.act_ld = lo.fmax;
+    d.w_routed = L->down;
+    d.w_routed_stride = (size_t)H * L->ffn / 32 * 20;
+    d.w_shared = L->shared_down;
+    d.shared_group = El;
+    d.K_routed = L->ffn;
+    d.K_shared = L->shared_ffn;
+    d.out = out;
+    d.H = H;
+    d.k = k;
+    d.shared_base = sl.r_cap;
+    d.sgate = sg;
+    d.meta = reinterpret_cast<const int*>(mine + sl.meta);
+    for (int i = 0; i < G; ++i) d.yret[i] = reinterpret_cast<uint16_t*>(a.sym[i] + sl.y);
+    d.err = a.err + 1;
+    prof_begin(kStageDown, st);
+    if ((rc = launch_expert_tc(false, d, st))) return rc;
+    if ((rc = launch_ep_signal(a, 2, st))) return rc;
+    prof_end(kStageDown, st);
+    prof_begin(kStageCombine, st);
+    if ((rc = launch_ep_wait(a, 2, st))) return rc;
+    rc = launch_combine_bf16(out, reinterpret_cast<const uint16_t*>(mine + sl.y), at<int>(workspace, lo.pos), ids, wts, T,
+                             t_real, k, H, st);
+    prof_end(kStageCombine, st);
+    return rc;
+}
+
+extern "C" FM_API int fm_ipc_alloc(size_t bytes, void** ptr, void* handle_out) {
+    g_err[0] = 0;
+    if (!ptr || !handle_out || !bytes) {
+        set_error("fm_ipc_alloc: null argument or zero size");
+        return FM_EINVAL_SHAPE;
+    }
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return cuda_status(cudaGetLastError(), "cudaMalloc(symmetric buffer)");
+    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(cudaGetLastError(), "clear symmetric buffer");
+    }
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(cudaGetLastError(), "cudaIpcGetMemHandle");
+    }
+    std::memcpy(handle_out, &h, sizeof h);
+    *ptr = p;
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_ipc_open(const void* handle, void** ptr) {
+    g_err[0] = 0;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof h);
+    if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "cudaIpcOpenMemHandle");
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_ipc_close(void* ptr) {
+    g_err[0] = 0;
+    if (cudaIpcCloseMemHandle(ptr) != cudaSuccess) return cuda_status(cudaGetLastError(), "cudaIpcCloseMemHandle");
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_ipc_free(void* ptr) {
+    g_err[0] = 0;
+    if (cudaFree(ptr) != cudaSuccess) return cuda_status(cudaGetLastError(), "cudaFree(symmetric buffer)");
+    return FM_OK;
+}

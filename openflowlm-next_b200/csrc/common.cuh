@@ -15,6 +15,7 @@ constexpr int kTileK = 64;           // K of a weight tile (two Q4_1 blocks, one
 constexpr int kTileBytes = 5120;     // 128 rows x (32 nibble bytes + 8 scale bytes)
 constexpr int kTileNibBytes = 4096;  // nibble area of a tile
 constexpr int kMaxTopK = 16;
+constexpr int kMaxRanks = FM_EP_MAX_RANKS;   // expert-parallel group size limit
 
 // Status recorded by the host API for the calling thread.
 void set_error(const char* fmt, ...);
@@ -58,6 +59,34 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
+}
+
+// Block-wide exclusive scan of one int per thread (blockDim.x == 1024). Returns the total in *total.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* sh, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) sh[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int s = sh[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        sh[lane] = s;   // inclusive warp totals
+    }
+    __syncthreads();
+    const int base = warp ? sh[warp - 1] : 0;
+    const int t = sh[31];
+    __syncthreads();
+    if (total) *total = t;
+    return base + x - v;
 }
 
 // Workspace layout shared by the entry points (byte offsets, 256-aligned). Built on the host.

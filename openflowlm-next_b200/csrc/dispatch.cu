@@ -34,34 +34,6 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_hist_kernel(const int32
     for (int e = threadIdx.x; e < e_local; e += blockDim.x) blk_hist[(size_t)blockIdx.x * e_local + e] = hist[e];
 }
 
-// Block-wide exclusive scan of one int per thread (blockDim.x == 1024). Returns the total in *total.
-__device__ int block_exclusive_scan(int v, int* sh, int* total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) sh[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-        int s = sh[lane];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, s, o);
-            if (lane >= o) s += y;
-        }
-        sh[lane] = s;   // inclusive warp totals
-    }
-    __syncthreads();
-    const int base = warp ? sh[warp - 1] : 0;
-    const int t = sh[31];
-    __syncthreads();
-    if (total) *total = t;
-    return base + x - v;
-}
-
 // Work list entry: (group, band, row0, nrows). list[0] = number of entries. Row tiles outer, bands
 // inner, so consecutive items share their activation rows in L2.
 __device__ void emit_tiles(int* list, int first, int g, int bands, int row0, int cnt, int bn) {

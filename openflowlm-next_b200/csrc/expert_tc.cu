@@ -70,6 +70,11 @@ struct TcArgs {
     int shared_base;
     const float* sgate;
     uint16_t* y_rows;   // DOWN, expert-parallel mode: routed row r's y, unweighted bf16, goes to y_rows[pair[r]]
+    // DOWN, peer expert-parallel mode: routed row r's y, unweighted bf16, goes straight to the rank that
+    // sent the row: yret[meta[r] >> 24] + (meta[r] & 0xFFFFFF) rows, a store over NVLink; skipped once
+    // the status word *err is set (a failed exchange: the peers may be gone)
+    const int* meta;
+    uint16_t* yret[kMaxRanks];
     int* err;
 };
 
@@ -307,6 +312,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
             const int acc = local & 1;
             const uint32_t accph = (local >> 1) & 1;
             if (!GATE_UP) {
+                const bool peer_ok = a.meta && *reinterpret_cast<volatile const int*>(a.err) == 0;
                 for (int j = et; j < it.n; j += 128) {
                     const int rrow = it.row0 + j;
                     int t;
@@ -314,6 +320,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
                     if (it.g == a.shared_group) {
                         t = rrow - a.shared_base;
                         wv = a.sgate[t];
+                    } else if (a.meta) {
+                        t = peer_ok ? a.meta[rrow] : -1;
+                        wv = 1.0f;
                     } else if (a.y_rows) {
                         t = a.pair[rrow];   // expert-major row -> the received row it came from
                         wv = 1.0f;
@@ -375,6 +384,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
                         const int j = ew * 8 + jj;
                         if (c0 + j < it.n) {
                             const float4 y = *reinterpret_cast<const float4*>(ys + j * TC_EPI_LD + lane * 4);
+                            if (a.meta && it.g != a.shared_group) {
+                                const int m = tok[c0 + j];
+                                if (m >= 0)
+                                    *reinterpret_cast<uint2*>(a.yret[m >> 24] + (size_t)(m & 0xFFFFFF) * a.H +
+                                                              it.band * 128 + lane * 4) =
+                                        make_uint2(pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
+                                continue;
+                            }
                             if (a.y_rows && it.g != a.shared_group) {
                                 *reinterpret_cast<uint2*>(a.y_rows + (size_t)tok[c0 + j] * a.H + it.band * 128 + lane * 4) =
                                     make_uint2(pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
@@ -393,6 +410,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
             fail(a.err, FM_ETIMEOUT);
             atomicExch(&abort_flag, 1);
         }
+        if (!GATE_UP && a.meta) __threadfence_system();   // the peer stores land before the rank signals
     }
     tc_fence_before();
     __syncthreads();
@@ -472,6 +490,8 @@ int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
     a.shared_base = L.shared_base;
     a.sgate = L.sgate;
     a.y_rows = L.y_rows;
+    a.meta = L.meta;
+    for (int i = 0; i < kMaxRanks; ++i) a.yret[i] = L.yret[i];
     a.err = L.err;
     const int grid = L.max_items < sm_count() ? L.max_items : sm_count();
     const int sm = TcSmem::total;

@@ -47,6 +47,8 @@ struct TcLaunch {
     int shared_base;
     const float* sgate;
     uint16_t* y_rows;
+    const int* meta;                 // peer expert-parallel DOWN (see expert_tc.cu)
+    uint16_t* yret[kMaxRanks];
     int* err;
 };
 int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st);
@@ -85,6 +87,22 @@ int launch_ep_regroup(const int* rc, int G, int El, const uint16_t* xrecv, int R
                       int* seg, int* src_off, int* dst_off, uint16_t* xexp, int* rowmap, int* err, cudaStream_t st);
 int launch_combine_bf16(float* out, const uint16_t* y, const int* pos, const int32_t* idx, const float* w, int T,
                         int t_real, int k, int H, cudaStream_t st);
+// Peer-memory expert parallel (ep_peer.cu). sym[g] = rank g's symmetric buffer as mapped here.
+constexpr int kMaxRanksPad = 64;   // ints per flag array in the symmetric buffer
+struct EpPeerArgs {
+    uint8_t* sym[kMaxRanks];
+    size_t off_flags, off_cnt, off_meta, off_x, off_y;
+    int* state;          // this rank's [0] epoch, [1] scatter blocks finished (in its symmetric buffer)
+    int* err;            // the call's status words; err[1] != 0 stops every later exchange step
+    int rank, G, E, El, H, k, r_cap;
+    long long timeout_ns;
+};
+int launch_ep_post_counts(const EpPeerArgs& a, const int* counts, cudaStream_t st);
+int launch_ep_plan_peer(const EpPeerArgs& a, int* send_base, int* seg, cudaStream_t st);
+int launch_ep_scatter_rows(const EpPeerArgs& a, const uint16_t* xb, const int* pair, const int32_t* idx,
+                           const int* offsets, const int* send_base, int P, int t_real, int sms, cudaStream_t st);
+int launch_ep_wait(const EpPeerArgs& a, int which, cudaStream_t st);
+int launch_ep_signal(const EpPeerArgs& a, int which, cudaStream_t st);
 int launch_combine(const float* res, const float* y, const int* pos, const int32_t* idx, const float* w,
                    const float* sgate, int shared_on, int T, int t_real, int k, int H, int P, float* out, cudaStream_t st);
 

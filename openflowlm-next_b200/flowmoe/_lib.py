@@ -34,6 +34,15 @@ class FmLayer(ctypes.Structure):
                 ("shared_down", ctypes.c_void_p), ("router", ctypes.c_void_p), ("router_bias", ctypes.c_void_p)]
 
 
+FM_EP_MAX_RANKS = 16
+
+
+class FmEpGroup(ctypes.Structure):
+    """``fm_ep_group`` (include/flowmoe.h)."""
+    _fields_ = [("rank", ctypes.c_int32), ("n_ranks", ctypes.c_int32), ("t_cap", ctypes.c_int32),
+                ("timeout_ms", ctypes.c_int32), ("sym", ctypes.c_void_p * FM_EP_MAX_RANKS)]
+
+
 P = ctypes.c_void_p
 I32 = ctypes.c_int32
 SZ = ctypes.c_size_t
@@ -57,6 +66,12 @@ SIGNATURES = {
     "fm_ep_dispatch": [LP, P, I32, I32, I32, P, P, P, P, P, P, P, P, SZ, P],
     "fm_ep_experts": [LP, P, I32, P, I32, P, P, P, I32, I32, P, P, P, SZ, P],
     "fm_ep_combine": [LP, P, P, P, P, P, I32, I32, P],
+    "fm_ep_peer_sizes": [LP, ctypes.c_void_p, ctypes.POINTER(SZ), ctypes.POINTER(SZ)],
+    "fm_ep_peer_layer": [LP, ctypes.c_void_p, P, I32, P, I32, I32, P, P, P, P, SZ, P],
+    "fm_ipc_alloc": [SZ, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p],
+    "fm_ipc_open": [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)],
+    "fm_ipc_close": [P],
+    "fm_ipc_free": [P],
     "fm_moe_check": [P, P],
     "fm_launch_count": [ctypes.POINTER(ctypes.c_ulonglong)],
     "fm_profile": [I32],

@@ -27,7 +27,7 @@ from datetime import timedelta
 import torch
 import torch.distributed as dist
 
-from ._lib import FM_BF16, FM_F32, call
+from ._lib import FM_BF16, FM_EP_MAX_RANKS, FM_F32, FmEpGroup, call
 from .layer import MoEConfig, MoELayer, _stream
 
 
@@ -158,6 +158,90 @@ class DeviceStages:
             call("fm_moe_check", self._ws.data_ptr(), _stream(self.device))
 
 
+class PeerGroup:
+    """The symmetric buffers of a peer-memory expert-parallel group: each rank allocates one
+    (fm_ipc_alloc), the IPC handles are all-gathered over ``group`` (host objects only), each rank maps
+    the others' (fm_ipc_open). ``layer`` must hold this rank's expert range."""
+
+    def __init__(self, layer: MoELayer, t_cap: int, group=None, timeout_ms: int = 2000):
+        self.layer = layer
+        self.group = group
+        G, r = dist.get_world_size(group), dist.get_rank(group)
+        if G > FM_EP_MAX_RANKS:
+            raise ValueError(f"at most {FM_EP_MAX_RANKS} ranks")
+        self.g = FmEpGroup(r, G, t_cap, timeout_ms)
+        sym_b, ws_b = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        call("fm_ep_peer_sizes", ctypes.byref(layer._L), ctypes.byref(self.g), ctypes.byref(sym_b), ctypes.byref(ws_b))
+        self.sym_bytes = sym_b.value
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        call("fm_ipc_alloc", self.sym_bytes, ctypes.byref(own), handle)
+        self._own = own.value
+        handles = [None] * G
+        dist.all_gather_object(handles, (handle.raw, t_cap, self.sym_bytes), group=group)
+        if len({h[1:] for h in handles}) != 1:
+            call("fm_ipc_free", self._own)
+            raise ValueError(f"ranks disagree on (t_cap, buffer bytes): {[h[1:] for h in handles]}")
+        handles = [h[0] for h in handles]
+        self._opened = []
+        for i in range(G):
+            if i == r:
+                self.g.sym[i] = self._own
+                continue
+            p = ctypes.c_void_p()
+            call("fm_ipc_open", handles[i], ctypes.byref(p))
+            self.g.sym[i] = p.value
+            self._opened.append(p.value)
+        self.ws = torch.empty(max(ws_b.value, 256), dtype=torch.uint8, device=layer.device)
+        torch.cuda.synchronize(layer.device)
+        dist.barrier(group=group)
+
+    def close(self):
+        """Unmap the peers' buffers and free our own, after every rank has finished with them."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.layer.device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            call("fm_ipc_close", p)
+        self._opened = []
+        dist.barrier(group=self.group)
+        call("fm_ipc_free", self._own)
+        self._own = None
+
+
+class PeerEPMoELayer:
+    """The MoE block of one rank over peer memory: one fm_ep_peer_layer call per layer, rows and y rows
+    stored straight into their owners' buffers over NVLink, no NCCL and no host round trip."""
+
+    def __init__(self, layer: MoELayer, t_cap: int, group=None, timeout_ms: int = 2000):
+        self.cfg = layer.cfg
+        self.layer = layer
+        self.peers = PeerGroup(layer, t_cap, group, timeout_ms)
+
+    def forward(self, x: torch.Tensor, res: torch.Tensor, t_real: int | None = None, out: torch.Tensor | None = None,
+                idx: torch.Tensor | None = None, w: torch.Tensor | None = None) -> torch.Tensor:
+        layer = self.layer
+        layer._check_x(x)
+        T = x.shape[0]
+        t_real = T if t_real is None else t_real
+        out = torch.empty(T, self.cfg.hidden, dtype=torch.float32, device=layer.device) if out is None else out
+        ws = self.peers.ws
+        call("fm_ep_peer_layer", ctypes.byref(layer._L), ctypes.byref(self.peers.g), x.data_ptr(), layer._dtype(x),
+             res.data_ptr(), T, t_real, out.data_ptr(), None if idx is None else idx.data_ptr(),
+             None if w is None else w.data_ptr(), ws.data_ptr(), ws.numel(), _stream(layer.device))
+        return out
+
+    __call__ = forward
+
+    def check(self):
+        """Synchronise; raise FM_ETIMEOUT if a peer did not take its step in time, or on a bad expert id."""
+        call("fm_moe_check", self.peers.ws.data_ptr(), _stream(self.layer.device))
+
+    def close(self):
+        self.peers.close()
+
+
 class EPMoELayer:
     """The MoE block of one rank in an expert-parallel group (``torch.distributed`` initialised, NCCL on
     the GPU). Holds only this rank's experts; ``forward(x, res)`` takes this rank's tokens."""
@@ -195,4 +279,5 @@ def init_process_group(backend: str = "nccl", timeout_s: float = 120.0):
     return dist.get_rank(), dist.get_world_size()
 
 
-__all__ = ["EPMoELayer", "DeviceStages", "ep_forward", "expert_range", "ExchangeError", "init_process_group"]
+__all__ = ["EPMoELayer", "PeerEPMoELayer", "PeerGroup", "DeviceStages", "ep_forward", "expert_range", "ExchangeError",
+           "init_process_group"]

@@ -197,3 +197,83 @@ def test_ep_counts_that_do_not_add_up_are_rejected(dev):
     st.experts(xrecv, R, rc, 2, x, sg, res, c["T"], c["T"])
     with pytest.raises(FlowMoeError, match="do not add up"):
         st.check()
+
+
+# ---- peer-memory expert parallel (fm_ep_peer_layer), two processes
+
+def _peer_worker(rank, world, port, outdir, mode):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    sys.path[:0] = [str(ROOT), str(ROOT / "openflowlm-next_b200")]
+    result = {"rank": rank}
+    import torch.distributed as dist
+    layer = None
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        from flowmoe.ep import PeerEPMoELayer
+        c = cases.make_case(H=512, E=32, F=256, FS=256, k=8, T=192, seed=321)
+        st = _rank_layer(c, rank, world, dev)
+        layer = PeerEPMoELayer(st.layer, t_cap=c["T"], timeout_ms=1000 if mode == "absent" else 5000)
+        n = c["T"] // world
+        shards = [(0, 120), (120, 192)] if mode == "uneven" else [(i * n, (i + 1) * n) for i in range(world)]
+        lo, hi = shards[rank]
+        x = torch.from_numpy(c["x"][lo:hi]).reshape(hi - lo, c["H"]).to(dev).to(torch.bfloat16).contiguous()
+        res = torch.from_numpy(c["res"][lo:hi]).reshape(hi - lo, c["H"]).to(dev).contiguous()
+        if mode == "absent":
+            # rank 1 maps the buffers, then skips the layer call: rank 0's waits must run out
+            if rank == 0:
+                layer(x, res)
+                try:
+                    layer.check()
+                    result.update(ok=False, error="no timeout reported")
+                except Exception as e:
+                    result.update(ok=True, error=str(e))
+            else:
+                result.update(ok=True)
+            dist.barrier()
+        else:
+            errs = []
+            for _ in range(3):     # the epochs advance; every buffer is reused
+                out = layer(x, res)
+                layer.check()
+                errs.append(_rel(out.cpu().numpy(), _want(c, lo, hi), c["res"][lo:hi]))
+            result.update(ok=True, errs=errs)
+    except Exception as e:
+        result.update(ok=False, error=f"{type(e).__name__}: {e}", tb=traceback.format_exc()[-3000:])
+    finally:
+        Path(outdir, f"rank{rank}.json").write_text(json.dumps(result))
+        try:
+            if layer is not None:
+                layer.close()
+        finally:
+            if dist.is_initialized():
+                dist.destroy_process_group()
+
+
+def _run_peer(mode, tmp_path):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.start_processes(_peer_worker, args=(2, _free_port(), str(tmp_path), mode), nprocs=2, join=False,
+                             start_method="spawn")
+    deadline = time.monotonic() + 240
+    while not ctx.join(timeout=1):
+        if time.monotonic() > deadline:
+            for p in ctx.processes:
+                p.kill()
+            pytest.fail("peer ranks did not finish within 240 s")
+    return [json.loads(Path(tmp_path, f"rank{r}.json").read_text()) for r in range(2)]
+
+
+@pytest.mark.parametrize("mode", ["even", "uneven"])
+def test_ep_peer_two_ranks(tmp_path, mode):
+    for r in _run_peer(mode, tmp_path):
+        assert r["ok"], r.get("tb")
+        assert max(r["errs"]) < TOL, r
+
+
+def test_ep_peer_absent_rank_times_out(tmp_path):
+    res = _run_peer("absent", tmp_path)
+    assert res[0]["ok"], res[0]
+    assert "FM_ETIMEOUT" in res[0]["error"], res[0]
