@@ -764,7 +764,7 @@ extern "C" FM_API int fm_ep_experts(const fm_layer* L, const uint16_t* xrecv, in
     d.K_shared = L->shared_ffn;
     d.out = out;
     d.H = H;
-    d.pair = at<int>(workspace, lo.rowmap);
+    d.ymap = at<int>(workspace, lo.rowmap);
     d.k = L->top_k;
     d.shared_base = R;
     d.sgate = shared_gate;

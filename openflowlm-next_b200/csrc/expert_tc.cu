@@ -2,7 +2,7 @@
 //
 // One persistent CTA per SM walks the work list (group, band, first sorted row, rows). A work item
 // is D[128 weight rows x n tokens] = W_band[128 x K] . X[n x K]^T with n <= 256, K walked in 64-wide
-// slabs. Warp roles (320 threads):
+// slabs. Warp roles (448 threads):
 //   warp 0      producer: per slab, one 5120-byte bulk copy of the raw Q4_1 weight tile and
 //               ceil(n/32) TMA loads (128-byte swizzle) of the sorted bf16 activation rows;
 //   warp 1      TMEM owner and MMA issuer: four tcgen05.mma (M=128, N=n rounded to 16, K=16) per
@@ -10,12 +10,16 @@
 //   warps 2-5   dequantisers: thread r turns row r of the raw tile (two GGUF blocks) into 64 bf16
 //               values in the 128-byte-swizzled K-major layout the MMA reads (w = q*d + m in f32 with
 //               the fp16 d, m widened exactly, rounded once to bf16);
-//   warps 6-9   epilogue, overlapped with the next item's main loop through the second accumulator:
+//   warps 6-13  epilogue in two halves of four warps (alternate 32-token chunks), overlapped with the
+//               next item's main loop through the second accumulator:
 //               GATE_UP  rows 0-63 of a gate_up tile are gate rows, rows 64-127 the up rows of the same
 //                        64 features: h = bf16(silu(g) * u) -> the sorted h matrix (the reference's
 //                        SwiGLU, designs/moe_batch/moe_batch.h:181-202, h rounded to bf16);
-//               DOWN     out[token][row] += w * y with red.global.add (the weighted scatter of
-//                        core.cpp:5236-5255, routing weight or shared-expert gate per row).
+//               DOWN     out[token][row] += w * y (the weighted scatter of core.cpp:5236-5255, routing
+//                        weight or shared-expert gate per row): the weighted 32-token chunk is staged
+//                        in shared memory, then each warp adds 8 token rows with red.global.add.v4.f32;
+//                        or unweighted bf16 y rows (expert parallel: in the received order, or straight
+//                        into the sending rank's buffer over peer memory).
 // Every mbarrier wait is bounded (sm100.cuh); a give-up records FM_ETIMEOUT in the error word and
 // the CTA drains its own copies, frees TMEM and returns.
 #include <cuda.h>
@@ -26,7 +30,8 @@
 
 namespace fm {
 
-constexpr int TC_THREADS = 320;
+constexpr int TC_EPI_WARPS = 8;
+constexpr int TC_THREADS = 32 * (6 + TC_EPI_WARPS);   // producer, MMA, 4 dequantisers, 8 epilogue warps
 constexpr int TC_BN = 256;                 // max tokens per work item (MMA N)
 constexpr int TC_SR = 4;                   // raw weight tile ring
 constexpr int TC_SB = 4;                   // activation tile ring
@@ -37,7 +42,8 @@ constexpr int TC_BOX_ROWS = 32;
 constexpr int TC_EPI_LD = 132;             // padded f32 row of the DOWN staging tile
 // epilogue staging: GATE_UP gate/up exchange (2 x 16 x 64 f32) + h tile (32 x 64 bf16);
 // DOWN weighted y tile (32 x 132 f32) + token / weight lists (2 x 256)
-constexpr int TC_EPI_BYTES = 32 * TC_EPI_LD * 4 + 2 * 256 * 4;
+constexpr int TC_HALF_BYTES = 32 * TC_EPI_LD * 4;            // one epilogue half's staging area
+constexpr int TC_EPI_BYTES = 2 * TC_HALF_BYTES + 2 * 256 * 4;   // two halves + token / weight lists
 
 struct TcSmem {
     // offsets from the 1024-aligned dynamic smem base
@@ -69,7 +75,11 @@ struct TcArgs {
     int k;
     int shared_base;
     const float* sgate;
-    uint16_t* y_rows;   // DOWN, expert-parallel mode: routed row r's y, unweighted bf16, goes to y_rows[pair[r]]
+    // DOWN, row mode: routed row r's y, unweighted bf16, goes to y_rows[ymap ? ymap[r] : r]; without ymap
+    // the shared expert's rows go to y_rows[r] too (a combine kernel then sums each token in ascending
+    // expert order), with ymap they are added into out (expert parallel: out holds this rank's tokens)
+    uint16_t* y_rows;
+    const int* ymap;
     // DOWN, peer expert-parallel mode: routed row r's y, unweighted bf16, goes straight to the rank that
     // sent the row: yret[meta[r] >> 24] + (meta[r] & 0xFFFFFF) rows, a store over NVLink; skipped once
     // the status word *err is set (a failed exchange: the peers may be gone)
@@ -163,7 +173,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
         for (int i = 0; i < TC_SR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 128); }
         for (int i = 0; i < TC_SB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
         for (int i = 0; i < TC_SA; ++i) { mbar_init(&a_full[i], 128); mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 128); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 32 * TC_EPI_WARPS); }
         mbar_fence_init();
         prefetch_tmap(&bmap);
     }
@@ -292,55 +302,70 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
             atomicExch(&abort_flag, 1);
         }
     } else {
-        // ------------------------------------------------------------ epilogue
+        // ------------------------------------------------------------ epilogue (8 warps, 2 halves)
+        // Warp w reads TMEM lane group w % 4; the half (w - 6) / 4 takes every other 32-column chunk
+        // (c0 = 32 half + 64 i) with its own staging area and named barrier (1 + half, 128 threads);
+        // barrier 3 spans all 256 epilogue threads.
         const int lg = warp & 3;                 // TMEM lane group this warp may access
         const int row = lg * 32 + lane;          // accumulator row = TMEM lane
-        const int et = threadIdx.x - 192;        // 0..127
-        uint8_t* epi = smem + TcSmem::epi;
+        const int et = threadIdx.x - 192;        // 0..255
+        const int half = et >> 7;
+        const int ht = et & 127;                 // thread within the half
+        const int hbar = 1 + half;
+        uint8_t* epi = smem + TcSmem::epi + half * TC_HALF_BYTES;
         float* xg = reinterpret_cast<float*>(epi);                   // GATE_UP: gate, cols 16-31 [16][64]
         float* xu = xg + 16 * 64;                                    //          up, cols 0-15 [16][64]
         uint16_t* hst = reinterpret_cast<uint16_t*>(xu + 16 * 64);   //          h tile [32][64] bf16
         float* ys = reinterpret_cast<float*>(epi);                   // DOWN: weighted y [32][TC_EPI_LD]
-        int* tok = reinterpret_cast<int*>(epi + 32 * TC_EPI_LD * 4); //       token per row [256]
-        float* wgt = reinterpret_cast<float*>(tok + 256);            //       weight per row [256]
+        int* tok = reinterpret_cast<int*>(smem + TcSmem::epi + 2 * TC_HALF_BYTES);   // token per row [256]
+        float* wgt = reinterpret_cast<float*>(tok + 256);                            // weight per row [256]
         __shared__ int epi_abort;
         if (et == 0) epi_abort = 0;
-        named_bar(1, 128);
+        named_bar(3, 256);
         int local = 0;
         for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++local) {
             const Item it = decode_item<GATE_UP>(a, i);
             const int acc = local & 1;
             const uint32_t accph = (local >> 1) & 1;
-            if (!GATE_UP) {
-                const bool peer_ok = a.meta && *reinterpret_cast<volatile const int*>(a.err) == 0;
-                for (int j = et; j < it.n; j += 128) {
-                    const int rrow = it.row0 + j;
-                    int t;
-                    float wv;
-                    if (it.g == a.shared_group) {
-                        t = rrow - a.shared_base;
-                        wv = a.sgate[t];
-                    } else if (a.meta) {
-                        t = peer_ok ? a.meta[rrow] : -1;
-                        wv = 1.0f;
-                    } else if (a.y_rows) {
-                        t = a.pair[rrow];   // expert-major row -> the received row it came from
-                        wv = 1.0f;
-                    } else {
-                        const int p = a.pair[rrow];
-                        t = p / a.k;
-                        wv = a.wpair[p];
-                    }
-                    tok[j] = t;
-                    wgt[j] = wv;
+            // DOWN: where the item's rows go -- 0 weighted red.add into out, 1 a bf16 row of y_rows,
+            // 2 a bf16 row in the sending rank's buffer (peer store)
+            const bool shared_item = it.g == a.shared_group;
+            const int mode = shared_item ? ((a.y_rows && !a.ymap && !a.meta) ? 1 : 0) : (a.meta ? 2 : (a.y_rows ? 1 : 0));
+            // DOWN: thread et looks up the destination and weight of row et while the accumulator
+            // fills; it goes to shared memory after the barrier below, when every thread is done with
+            // the previous item's lists
+            int tk = 0;
+            float wk = 0.f;
+            if (!GATE_UP && et < it.n) {
+                const int rrow = it.row0 + et;
+                if (mode == 1) {
+                    tk = (a.ymap && !shared_item) ? a.ymap[rrow] : rrow;
+                    wk = 1.0f;
+                } else if (shared_item) {
+                    tk = rrow - a.shared_base;
+                    wk = a.sgate[tk];
+                } else if (mode == 2) {
+                    tk = *reinterpret_cast<volatile const int*>(a.err) == 0 ? a.meta[rrow] : -1;
+                    wk = 1.0f;
+                } else {
+                    const int p = a.pair[rrow];
+                    tk = p / a.k;
+                    wk = a.wpair[p];
                 }
             }
             if (!mbar_wait(&acc_full[acc], accph)) epi_abort = 1;
-            named_bar(1, 128);
+            named_bar(3, 256);
             if (epi_abort) break;
+            if (!GATE_UP) {
+                if (et < it.n) {
+                    tok[et] = tk;
+                    wgt[et] = wk;
+                }
+                named_bar(3, 256);
+            }
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(lg * 32) << 16) + acc * 256;
-            for (int c0 = 0; c0 < it.n; c0 += 32) {
+            for (int c0 = 32 * half; c0 < it.n; c0 += 64) {
                 uint32_t v[32];
                 tmem_ld32(taddr + c0, v);
                 tmem_ld_wait();
@@ -353,7 +378,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
 #pragma unroll
                         for (int j = 0; j < 16; ++j) xu[j * 64 + row - 64] = __uint_as_float(v[j]);
                     }
-                    named_bar(1, 128);
+                    named_bar(hbar, 128);
                     const int f = row & 63;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
@@ -362,9 +387,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
                         const float h = __fdividef(g, 1.0f + __expf(-g)) * u;
                         hst[(lg < 2 ? j : 16 + j) * 64 + f] = f32_to_bf16_bits(h);
                     }
-                    named_bar(1, 128);
+                    named_bar(hbar, 128);
                     // 32 token rows x 128 B: 4 threads per row, 2 x 16 B each
-                    const int j = et >> 2, part = et & 3;
+                    const int j = ht >> 2, part = ht & 3;
                     if (c0 + j < it.n) {
                         const uint4* src = reinterpret_cast<const uint4*>(hst + j * 64 + part * 16);
                         uint4* dst = reinterpret_cast<uint4*>(a.h_out + (size_t)(it.row0 + c0 + j) * a.h_ld +
@@ -372,35 +397,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
                         dst[0] = src[0];
                         dst[1] = src[1];
                     }
-                    named_bar(1, 128);
+                    named_bar(hbar, 128);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) ys[j * TC_EPI_LD + row] = __uint_as_float(v[j]) * wgt[c0 + j];
-                    named_bar(1, 128);
-                    // warp w scatters tokens 8w..8w+7 of the chunk: 32 lanes x 4 floats = the 128 rows
-                    const int ew = et >> 5;
+                    named_bar(hbar, 128);
+                    // warp w of the half writes tokens 8w..8w+7 of the chunk: 32 lanes x 4 floats = 128 rows
+                    const int ew = ht >> 5;
 #pragma unroll
                     for (int jj = 0; jj < 8; ++jj) {
                         const int j = ew * 8 + jj;
                         if (c0 + j < it.n) {
                             const float4 y = *reinterpret_cast<const float4*>(ys + j * TC_EPI_LD + lane * 4);
-                            if (a.meta && it.g != a.shared_group) {
+                            if (mode == 0) {
+                                red_add_v4(a.out + (size_t)tok[c0 + j] * a.H + it.band * 128 + lane * 4, y);
+                            } else if (mode == 2) {
                                 const int m = tok[c0 + j];
                                 if (m >= 0)
                                     *reinterpret_cast<uint2*>(a.yret[m >> 24] + (size_t)(m & 0xFFFFFF) * a.H +
                                                               it.band * 128 + lane * 4) =
                                         make_uint2(pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
-                                continue;
-                            }
-                            if (a.y_rows && it.g != a.shared_group) {
+                            } else {
                                 *reinterpret_cast<uint2*>(a.y_rows + (size_t)tok[c0 + j] * a.H + it.band * 128 + lane * 4) =
                                     make_uint2(pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
-                                continue;
                             }
-                            red_add_v4(a.out + (size_t)tok[c0 + j] * a.H + it.band * 128 + lane * 4, y);
                         }
                     }
-                    named_bar(1, 128);
+                    named_bar(hbar, 128);
                 }
             }
             tc_fence_before();
@@ -490,6 +513,7 @@ int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
     a.shared_base = L.shared_base;
     a.sgate = L.sgate;
     a.y_rows = L.y_rows;
+    a.ymap = L.ymap;
     a.meta = L.meta;
     for (int i = 0; i < kMaxRanks; ++i) a.yret[i] = L.yret[i];
     a.err = L.err;

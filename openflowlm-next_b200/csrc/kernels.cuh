@@ -46,7 +46,8 @@ struct TcLaunch {
     int k;
     int shared_base;
     const float* sgate;
-    uint16_t* y_rows;
+    uint16_t* y_rows;                // DOWN row mode (see expert_tc.cu)
+    const int* ymap;
     const int* meta;                 // peer expert-parallel DOWN (see expert_tc.cu)
     uint16_t* yret[kMaxRanks];
     int* err;
@@ -85,6 +86,9 @@ int launch_seg_lists(const int* seg, int nseg, int shared_group, int shared_base
                      int gu_bands, int gu_bands_shared, int* dn_list, int dn_bands, int bn, cudaStream_t st);
 int launch_ep_regroup(const int* rc, int G, int El, const uint16_t* xrecv, int R, const uint16_t* xb, int t_real, int H,
                       int* seg, int* src_off, int* dst_off, uint16_t* xexp, int* rowmap, int* err, cudaStream_t st);
+int launch_combine_y16(const float* res, const uint16_t* y, const int* pos, const int32_t* idx, const float* w,
+                       const float* sgate, int shared_on, int T, int t_real, int k, int H, int P, float* out,
+                       cudaStream_t st);
 int launch_combine_bf16(float* out, const uint16_t* y, const int* pos, const int32_t* idx, const float* w, int T,
                         int t_real, int k, int H, cudaStream_t st);
 // Peer-memory expert parallel (ep_peer.cu). sym[g] = rank g's symmetric buffer as mapped here.
