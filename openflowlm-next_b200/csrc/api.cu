@@ -72,7 +72,14 @@ int cuda_status(cudaError_t e, const char* what) {
 constexpr int kBN = 64;        // rows per expert work item (expert_mma)
 constexpr int kBNTc = 256;     // rows per expert work item (expert_tc)
 constexpr int kTcMinTokens = 64;   // the tcgen05 path from this many tokens (below: the mma.sync path)
-constexpr int kFlagLegacy = 1, kFlagTc = 2, kFlagGemv = 3;
+constexpr int kFlagLegacy = 1, kFlagTc = 2, kFlagGemv = 3, kFlagTcSingle = 4;
+
+// The tcgen05 GEMMs run as CTA pairs (M = 256 MMAs over band pairs) when every matrix has an even
+// number of 128-row bands; flag kFlagTcSingle keeps one CTA per item.
+static bool tc_pair(const fm_layer* L) {
+    return L->flags != kFlagTcSingle && (L->ffn / 64) % 2 == 0 && (L->shared_ffn / 64) % 2 == 0 &&
+           (L->hidden / kTileRows) % 2 == 0;
+}
 constexpr int kDecodeMaxT = 32;    // the GEMV path up to this many tokens
 constexpr int kGemvRowsApi = 8;    // sorted rows per GEMV item (decode.cu)
 constexpr int kChunk = 2048;   // dispatch chunk (dispatch.cu)
@@ -133,7 +140,7 @@ static Layout make_layout(const fm_layer* L, int T) {
     auto take = [&](size_t bytes) { size_t at = off; off = align256(off + bytes); return at; };
     o.err = take(16);   // first: fm_moe_check reads the counter at the workspace start
     o.xb = take((size_t)T * H * 2);
-    o.logits = take((size_t)router_ksplit(T, H, E) * T * (E + 1) * 4);
+    o.logits = take(router_scratch_bytes(T, H, E));
     o.counts = take((size_t)G * 4);
     o.offsets = take((size_t)(G + 1) * 4);
     o.blk_hist = take((size_t)o.nblk * L->e_local * 4);
@@ -193,7 +200,8 @@ static Path pick_path(const fm_layer* L, int T) {
     const bool gemv_ok = T <= kDecodeMaxT && L->e_local < 1024 && T * L->top_k <= 1024;
     switch (L->flags) {
         case kFlagLegacy: return Path::Mma;
-        case kFlagTc: return Path::Tc;
+        case kFlagTc:
+        case kFlagTcSingle: return Path::Tc;
         case kFlagGemv: return gemv_ok ? Path::Gemv : Path::Mma;
         default: break;
     }
@@ -275,6 +283,7 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     const int P = t_real * k;
     const bool tc = path == Path::Tc;
     const int bn = tc ? kBNTc : kBN;
+    const int bdiv = (tc && tc_pair(L)) ? 2 : 1;   // list entries are band pairs for the CTA-pair kernel
     if (cudaMemsetAsync(at<int>(ws, lo.err), 0, 16, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
     const int nblk = (P + kChunk - 1) / kChunk;
     // rows of the sorted space: routed [0, P), shared [P_cap, P_cap + t_real) with P_cap = T * k
@@ -282,8 +291,8 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     prof_begin(kStageDispatch, st);
     int rc = launch_dispatch(idx, P, L->e_begin, L->e_local, E, Pcap, shared_on ? t_real : 0, at<int>(ws, lo.blk_hist), nblk,
                              at<int>(ws, lo.counts), at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
-                             at<int>(ws, lo.gu_list), L->ffn / 64, shared_on ? L->shared_ffn / 64 : 0,
-                             at<int>(ws, lo.dn_list), H / kTileRows, bn, at<int>(ws, lo.err), st);
+                             at<int>(ws, lo.gu_list), L->ffn / 64 / bdiv, shared_on ? L->shared_ffn / 64 / bdiv : 0,
+                             at<int>(ws, lo.dn_list), H / kTileRows / bdiv, bn, at<int>(ws, lo.err), st);
     if (rc) return rc;
     prof_end(kStageDispatch, st);
     prof_begin(kStageGather, st);
@@ -311,6 +320,7 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
         g.h_out = at<uint16_t>(ws, lo.hperm);
         g.h_ld = lo.fmax;
         g.err = at<int>(ws, lo.err) + 1;
+        g.cta_pair = bdiv == 2;
         prof_begin(kStageGateUp, st);
         if ((rc = launch_expert_tc(true, g, st))) return rc;
         prof_end(kStageGateUp, st);
@@ -335,6 +345,7 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
         d.shared_base = Pcap;
         d.sgate = sgate;
         d.err = at<int>(ws, lo.err) + 1;
+        d.cta_pair = bdiv == 2;
         prof_begin(kStageDown, st);
         if ((rc = launch_expert_tc(false, d, st))) return rc;
         prof_end(kStageDown, st);
@@ -570,7 +581,7 @@ static EpDispatchLayout ep_dispatch_layout(const fm_layer* L, int T) {
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t a = off; off = align256(off + bytes); return a; };
     o.err = take(16);
-    o.logits = take((size_t)router_ksplit(T, H, E) * T * (E + 1) * 4);
+    o.logits = take(router_scratch_bytes(T, H, E));
     o.counts = take((size_t)(E + 1) * 4);
     o.offsets = take((size_t)(E + 2) * 4);
     o.blk_hist = take((size_t)o.nblk * E * 4);
@@ -726,8 +737,10 @@ extern "C" FM_API int fm_ep_experts(const fm_layer* L, const uint16_t* xrecv, in
     if (rc) return rc;
     prof_end(kStageGather, st);
     prof_begin(kStageDispatch, st);
-    rc = launch_seg_lists(at<int>(workspace, lo.seg), El, El, R, srows, at<int>(workspace, lo.gu_list), L->ffn / 64,
-                          L->shared_ffn / 64, at<int>(workspace, lo.dn_list), H / kTileRows, kBNTc, st);
+    const int bdiv = tc_pair(L) ? 2 : 1;
+    rc = launch_seg_lists(at<int>(workspace, lo.seg), El, El, R, srows, at<int>(workspace, lo.gu_list),
+                          L->ffn / 64 / bdiv, L->shared_ffn / 64 / bdiv, at<int>(workspace, lo.dn_list),
+                          H / kTileRows / bdiv, kBNTc, st);
     if (rc) return rc;
     prof_end(kStageDispatch, st);
     TcLaunch g{};
@@ -746,6 +759,7 @@ extern "C" FM_API int fm_ep_experts(const fm_layer* L, const uint16_t* xrecv, in
     g.h_out = at<uint16_t>(workspace, lo.hexp);
     g.h_ld = lo.fmax;
     g.err = at<int>(workspace, lo.err) + 1;
+    g.cta_pair = bdiv == 2;
     prof_begin(kStageGateUp, st);
     if ((rc = launch_expert_tc(true, g, st))) return rc;
     prof_end(kStageGateUp, st);
@@ -770,6 +784,7 @@ extern "C" FM_API int fm_ep_experts(const fm_layer* L, const uint16_t* xrecv, in
     d.sgate = shared_gate;
     d.y_rows = yrecv;
     d.err = at<int>(workspace, lo.err) + 1;
+    d.cta_pair = bdiv == 2;
     prof_begin(kStageDown, st);
     if ((rc = launch_expert_tc(false, d, st))) return rc;
     prof_end(kStageDown, st);
@@ -835,7 +850,7 @@ static EpPeerLayout ep_peer_layout(const fm_layer* L, const fm_ep_group* g, int 
     auto take = [&](size_t bytes) { size_t a = off; off = align256(off + bytes); return a; };
     o.err = take(16);
     o.xb = take((size_t)T * H * 2);
-    o.logits = take((size_t)router_ksplit(T, H, E) * T * (E + 1) * 4);
+    o.logits = take(router_scratch_bytes(T, H, E));
     o.counts = take((size_t)(E + 1) * 4);
     o.offsets = take((size_t)(E + 2) * 4);
     o.blk_hist = take((size_t)nblk * E * 4);
@@ -971,9 +986,10 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
         return rc;
     if ((rc = launch_ep_post_counts(a, counts, st))) return rc;
     if ((rc = launch_ep_plan_peer(a, at<int>(workspace, lo.send_base), at<int>(workspace, lo.seg), st))) return rc;
+    const int bdiv = tc_pair(L) ? 2 : 1;
     if ((rc = launch_seg_lists(at<int>(workspace, lo.seg), El, El, sl.r_cap, shared_on ? t_real : 0,
-                               at<int>(workspace, lo.gu_list), L->ffn / 64, L->shared_ffn / 64,
-                               at<int>(workspace, lo.dn_list), H / kTileRows, kBNTc, st)))
+                               at<int>(workspace, lo.gu_list), L->ffn / 64 / bdiv, L->shared_ffn / 64 / bdiv,
+                               at<int>(workspace, lo.dn_list), H / kTileRows / bdiv, kBNTc, st)))
         return rc;
     prof_end(kStageDispatch, st);
     prof_begin(kStageGather, st);
@@ -1001,6 +1017,7 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     gu.h_out = at<uint16_t>(workspace, lo.hexp);
     gu.h_ld = lo.fmax;
     gu.err = a.err + 1;
+    gu.cta_pair = bdiv == 2;
     prof_begin(kStageGateUp, st);
     if ((rc = launch_expert_tc(true, gu, st))) return rc;
     prof_end(kStageGateUp, st);
@@ -1025,6 +1042,7 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     d.meta = reinterpret_cast<const int*>(mine + sl.meta);
     for (int i = 0; i < G; ++i) d.yret[i] = reinterpret_cast<uint16_t*>(a.sym[i] + sl.y);
     d.err = a.err + 1;
+    d.cta_pair = bdiv == 2;
     prof_begin(kStageDown, st);
     if ((rc = launch_expert_tc(false, d, st))) return rc;
     if ((rc = launch_ep_signal(a, 2, st))) return rc;

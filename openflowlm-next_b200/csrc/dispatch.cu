@@ -59,17 +59,31 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(int* __restrict__ b
     for (int e0 = 0; e0 < e_local; e0 += 1024) {
         const int e = e0 + threadIdx.x;
         int run = 0;
+        // chunk histograms -> exclusive per-chunk prefixes, 16 chunks' loads in flight at a time
         if (e < e_local)
-            for (int b = 0; b < nblk; ++b) {
-                const int v = blk_hist[(size_t)b * e_local + e];
-                blk_hist[(size_t)b * e_local + e] = run;
-                run += v;
+            for (int b0 = 0; b0 < nblk; b0 += 16) {
+                int v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = b0 + j < nblk ? blk_hist[(size_t)(b0 + j) * e_local + e] : 0;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (b0 + j < nblk) {
+                        blk_hist[(size_t)(b0 + j) * e_local + e] = run;
+                        run += v[j];
+                    }
             }
         const int ex = block_exclusive_scan(e < e_local ? run : 0, sh, &total);
         if (e < e_local) {
             counts[e] = run;
             offsets[e] = carry + ex;
-            for (int b = 0; b < nblk; ++b) blk_hist[(size_t)b * e_local + e] += carry + ex;
+            for (int b0 = 0; b0 < nblk; b0 += 16) {
+                int v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = b0 + j < nblk ? blk_hist[(size_t)(b0 + j) * e_local + e] : 0;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (b0 + j < nblk) blk_hist[(size_t)(b0 + j) * e_local + e] = v[j] + carry + ex;
+            }
         }
         carry += total;
         __syncthreads();

@@ -30,12 +30,21 @@
 
 namespace fm {
 
-constexpr int TC_EPI_WARPS = 8;
-constexpr int TC_THREADS = 32 * (6 + TC_EPI_WARPS);   // producer, MMA, 4 dequantisers, 8 epilogue warps
+// Warp roles: 0 weight producer, 1 MMA issuer, then DQ dequantiser warps, EPI epilogue warps, and the
+// activation producer last. gate_up (K = H = 2048, light epilogue) is dequantiser-bound: 8 + 4; down
+// (K = F = 512, a y row per token and band) is epilogue-bound: 4 + 8.
+template <bool GATE_UP>
+struct TcRoles {
+    static constexpr int DQ = GATE_UP ? 8 : 4;
+    static constexpr int EPI = GATE_UP ? 4 : 8;
+    static constexpr int EPI0 = 2 + DQ;          // first epilogue warp
+    static constexpr int BWARP = EPI0 + EPI;     // activation producer warp
+};
+constexpr int TC_BWARP = 14;
+constexpr int TC_THREADS = 32 * (TC_BWARP + 1);   // 480 threads, both GEMMs
+static_assert(TcRoles<true>::BWARP == TC_BWARP && TcRoles<false>::BWARP == TC_BWARP, "warp roles");
+constexpr int TC_BOX_BIG = 128;            // activation rows per large TMA box
 constexpr int TC_BN = 256;                 // max tokens per work item (MMA N)
-constexpr int TC_SR = 4;                   // raw weight tile ring
-constexpr int TC_SB = 4;                   // activation tile ring
-constexpr int TC_SA = 2;                   // dequantised A tile ring
 constexpr int TC_A_BYTES = 128 * 128;      // 128 rows x 64 bf16
 constexpr int TC_B_BYTES = TC_BN * 128;    // 256 rows x 64 bf16
 constexpr int TC_BOX_ROWS = 32;
@@ -45,17 +54,26 @@ constexpr int TC_EPI_LD = 132;             // padded f32 row of the DOWN staging
 constexpr int TC_HALF_BYTES = 32 * TC_EPI_LD * 4;            // one epilogue half's staging area
 constexpr int TC_EPI_BYTES = 2 * TC_HALF_BYTES + 2 * 256 * 4;   // two halves + token / weight lists
 
+// Shared-memory layout: 2 dequantised A stages, 6 raw weight tiles, and 128 KB of activation stages
+// (4 of 256 rows for one CTA per item, 8 of 128 rows for a CTA-pair member).
+template <bool PAIR>
 struct TcSmem {
+    static constexpr int SA = 2;
+    static constexpr int SB = PAIR ? 8 : 4;
+    static constexpr int SR = 6;                  // raw weight tiles in flight (streamed from HBM)
+    static constexpr int B_STAGE = PAIR ? TC_B_BYTES / 2 : TC_B_BYTES;
     // offsets from the 1024-aligned dynamic smem base
     static constexpr int a = 0;
-    static constexpr int b = a + TC_SA * TC_A_BYTES;
-    static constexpr int raw = b + TC_SB * TC_B_BYTES;
-    static constexpr int epi = raw + TC_SR * kTileBytes;
+    static constexpr int b = a + SA * TC_A_BYTES;
+    static constexpr int raw = b + SB * B_STAGE;
+    static constexpr int epi = raw + SR * kTileBytes;
     static constexpr int bars = epi + TC_EPI_BYTES;
-    static constexpr int nbars = 2 * TC_SR + 2 * TC_SB + 2 * TC_SA + 4;
+    // raw, activation, A and accumulator rings + drain
+    static constexpr int nbars = 2 * SR + 2 * SB + 2 * SA + 4 + 1;
     static constexpr int tmem = bars + nbars * 8;
     static constexpr int total = tmem + 16 + 1024;   // + alignment slack
 };
+static_assert(TcSmem<true>::total <= 232448 && TcSmem<false>::total <= 232448, "shared memory per CTA");
 
 struct TcArgs {
     const int* list;
@@ -133,12 +151,13 @@ struct Item {
     const uint8_t* w;
 };
 
-template <bool GATE_UP>
-__device__ __forceinline__ Item decode_item(const TcArgs& a, int i) {
+// PAIR: list entries name band pairs; CTA `crank` of the pair takes band 2 * entry + crank.
+template <bool PAIR>
+__device__ __forceinline__ Item decode_item(const TcArgs& a, int i, uint32_t crank) {
     const int4 it = reinterpret_cast<const int4*>(a.list + 4)[i];
     Item r;
     r.g = it.x;
-    r.band = it.y;
+    r.band = PAIR ? 2 * it.y + (int)crank : it.y;
     r.row0 = it.z;
     r.n = it.w;
     const bool sh = r.g == a.shared_group;
@@ -149,152 +168,231 @@ __device__ __forceinline__ Item decode_item(const TcArgs& a, int i) {
     return r;
 }
 
-template <bool GATE_UP>
-__global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, TcArgs a) {
+// PAIR: a cluster of two CTAs on two SMs works each item as one M = 256 MMA (tcgen05 cta_group::2):
+// CTA r dequantises band 2p + r into its own A ring and loads rows [r N/2, (r + 1) N/2) of the
+// item's tokens into its own B ring, so each SM streams half the activation bytes per MMA. The first
+// CTA's barriers gate the MMAs: its A-full barrier counts one arrival per dequantiser warp of both
+// CTAs, its B-full barrier the bytes of both CTAs' activation loads (the second CTA's loads complete
+// on it directly), its accumulator-empty barrier one arrival per epilogue warp of both CTAs; the
+// first CTA issues the MMAs and commits the stage / accumulator releases to both CTAs' barriers. No
+// load is shared between the CTAs and no multicast copy is used.
+template <bool GATE_UP, bool PAIR>
+__global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_constant__ CUtensorMap bmap,
+                                                                  const __grid_constant__ CUtensorMap bmap_big, TcArgs a) {
+    using R = TcRoles<GATE_UP>;
+    using Sm = TcSmem<PAIR>;
+    constexpr int SA = Sm::SA, SB = Sm::SB, SR = Sm::SR, B_STAGE = Sm::B_STAGE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::bars);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sm::bars);
     uint64_t* raw_full = bars;
-    uint64_t* raw_empty = raw_full + TC_SR;
-    uint64_t* b_full = raw_empty + TC_SR;
-    uint64_t* b_empty = b_full + TC_SB;
-    uint64_t* a_full = b_empty + TC_SB;
-    uint64_t* a_empty = a_full + TC_SA;
-    uint64_t* acc_full = a_empty + TC_SA;
+    uint64_t* raw_empty = raw_full + SR;
+    uint64_t* b_full = raw_empty + SR;
+    uint64_t* b_empty = b_full + SB;
+    uint64_t* a_full = b_empty + SB;
+    uint64_t* a_empty = a_full + SA;
+    uint64_t* acc_full = a_empty + SA;
     uint64_t* acc_empty = acc_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::tmem);
+    uint64_t* drain = acc_empty + 2;             // the MMA issuer's last commit
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Sm::tmem);
     __shared__ int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_items = a.list[0];
+    const uint32_t crank = PAIR ? cluster_ctarank() : 0;
+    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;   // item stride: one per CTA or pair
+    const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        for (int i = 0; i < TC_SR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 128); }
-        for (int i = 0; i < TC_SB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
-        for (int i = 0; i < TC_SA; ++i) { mbar_init(&a_full[i], 128); mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 32 * TC_EPI_WARPS); }
+        // a dequantiser group (4 warps, 128 threads) consumes a raw tile and fills an A stage
+        for (int i = 0; i < SR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 128); }
+        for (int i = 0; i < SB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
+        // arrivals are per warp: 4 dequantiser / 8 epilogue warps per CTA, both CTAs' on the first CTA's
+        for (int i = 0; i < SA; ++i) { mbar_init(&a_full[i], (PAIR ? 2 : 1) * 4); mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], (PAIR ? 2 : 1) * R::EPI); }
+        mbar_init(drain, 1);
         mbar_fence_init();
         prefetch_tmap(&bmap);
+        prefetch_tmap(&bmap_big);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(tmem_slot, 512);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, 512);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if (PAIR) cluster_sync();   // barriers initialised in both CTAs before any cross-CTA arrival
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ producer
+    if (warp == 0 || warp == R::BWARP) {
+        // ------------------------------------------------------------ producers (lane 0 of each)
+        // warp 0: the raw weight tiles (streamed from HBM, SR deep); warp TC_BWARP: the activation
+        // rows (TMA, SB deep). Separate threads, so the weight stream runs ahead of the activations.
+        const bool weights = warp == 0;
         if (lane == 0) {
-            int rs = 0, bs = 0;
-            uint32_t rph = 0, bph = 0;
-            uint32_t issued_r = 0, issued_b = 0;   // bit i: slot i has a fill in flight or landed
+            const int S = weights ? SR : SB;
+            uint64_t* full = weights ? raw_full : b_full;
+            uint64_t* empty = weights ? raw_empty : b_empty;
+            int st = 0;
+            uint32_t ph = 0, issued = 0;   // bit i: slot i has a fill in flight or landed
             bool ok = true;
-            for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-                const Item it = decode_item<GATE_UP>(a, i);
-                const int nb = (it.n + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
+            for (int i = unit; i < n_items && ok; i += n_units) {
+                const Item it = decode_item<PAIR>(a, i, crank);
+                // this CTA's token rows: all n (single), or its half of N = n rounded up to 16 (pair)
+                const int nhalf = PAIR ? ((it.n + 15) & ~15) / 2 : it.n;
+                const int rbase = it.row0 + (int)crank * nhalf;
+                // whole 128-row boxes, then 32-row boxes for the rest
+                const int nbig = nhalf / TC_BOX_BIG;
+                const int nsmall = (nhalf - nbig * TC_BOX_BIG + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
+                const int rows_loaded = nbig * TC_BOX_BIG + nsmall * TC_BOX_ROWS;
                 for (int s = 0; s < it.slabs; ++s) {
-                    if (!mbar_wait(&raw_empty[rs], rph ^ 1)) { ok = false; break; }
-                    mbar_expect_tx(&raw_full[rs], kTileBytes);
-                    bulk_load(smem + TcSmem::raw + rs * kTileBytes, it.w + (size_t)s * kTileBytes, kTileBytes, &raw_full[rs]);
-                    issued_r |= 1u << rs;
-                    if (!mbar_wait(&b_empty[bs], bph ^ 1)) { ok = false; break; }
-                    mbar_expect_tx(&b_full[bs], nb * TC_BOX_ROWS * 128);
-                    for (int j = 0; j < nb; ++j)
-                        tma_load_2d(smem + TcSmem::b + bs * TC_B_BYTES + j * TC_BOX_ROWS * 128, &bmap, s * kTileK,
-                                    it.row0 + j * TC_BOX_ROWS, &b_full[bs]);
-                    issued_b |= 1u << bs;
-                    if (++rs == TC_SR) { rs = 0; rph ^= 1; }
-                    if (++bs == TC_SB) { bs = 0; bph ^= 1; }
+                    if (!mbar_wait(&empty[st], ph ^ 1)) { ok = false; break; }
+                    if (weights) {
+                        mbar_expect_tx(&raw_full[st], kTileBytes);
+                        bulk_load(smem + Sm::raw + st * kTileBytes, it.w + (size_t)s * kTileBytes, kTileBytes, &raw_full[st]);
+                        issued |= 1u << st;
+                    } else {
+                        // the first CTA arms its B-full barrier for both halves; the second CTA's loads
+                        // complete their bytes on that barrier
+                        if (crank == 0) mbar_expect_tx(&b_full[st], (PAIR ? 2 : 1) * rows_loaded * 128);
+                        for (int j = 0; j < nbig + nsmall; ++j) {
+                            const bool big = j < nbig;
+                            const int r0 = big ? j * TC_BOX_BIG : nbig * TC_BOX_BIG + (j - nbig) * TC_BOX_ROWS;
+                            const CUtensorMap* map = big ? &bmap_big : &bmap;
+                            uint8_t* dst = smem + Sm::b + st * B_STAGE + r0 * 128;
+                            if (PAIR)
+                                tma_load_2d_pair(dst, map, s * kTileK, rbase + r0, mapa_shared(&b_full[st], 0));
+                            else
+                                tma_load_2d(dst, map, s * kTileK, rbase + r0, &b_full[st]);
+                        }
+                        if (crank == 0) issued |= 1u << st;
+                    }
+                    if (++st == S) { st = 0; ph ^= 1; }
                 }
             }
             if (!ok) {
                 fail(a.err, FM_ETIMEOUT);
                 atomicExch(&abort_flag, 1);
                 // drain: every slot's most recent fill must land before the CTA may exit
-                for (int i = 0; i < TC_SR; ++i) {
-                    const int slot = (rs + i) % TC_SR;
-                    const uint32_t ph = slot < rs ? rph : rph ^ 1;   // parity of the slot's last fill
-                    if (issued_r >> slot & 1u) mbar_wait(&raw_full[slot], ph);
-                }
-                for (int i = 0; i < TC_SB; ++i) {
-                    const int slot = (bs + i) % TC_SB;
-                    const uint32_t ph = slot < bs ? bph : bph ^ 1;
-                    if (issued_b >> slot & 1u) mbar_wait(&b_full[slot], ph);
+                for (int i = 0; i < S; ++i) {
+                    const int slot = (st + i) % S;
+                    const uint32_t p = slot < st ? ph : ph ^ 1;   // parity of the slot's last fill
+                    if (issued >> slot & 1u) mbar_wait(&full[slot], p);
                 }
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            int as = 0, bs = 0;
-            uint32_t aph = 0, bph = 0;
-            bool ok = true;
-            int local = 0;
-            for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++local) {
-                const Item it = decode_item<GATE_UP>(a, i);
-                const int acc = local & 1;
-                const uint32_t accph = (local >> 1) & 1;
-                if (!mbar_wait(&acc_empty[acc], accph ^ 1)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * 256;
-                const int N = (it.n + 15) & ~15;
-                const uint32_t idesc = idesc_bf16(128, N);
-                for (int s = 0; s < it.slabs; ++s) {
-                    if (!mbar_wait(&a_full[as], aph) || !mbar_wait(&b_full[bs], bph)) { ok = false; break; }
+        if (!PAIR || crank == 0) {
+            // -------------------------------------------------------- MMA issuer (first CTA of a pair)
+            if (lane == 0) {
+                int as = 0, bs = 0;
+                uint32_t aph = 0, bph = 0;
+                bool ok = true, issued = false;
+                int local = 0;
+                const uint32_t peer = 1;
+                for (int i = unit; i < n_items && ok; i += n_units, ++local) {
+                    const Item it = decode_item<PAIR>(a, i, crank);
+                    const int acc = local & 1;
+                    const uint32_t accph = (local >> 1) & 1;
+                    if (!mbar_wait_cluster(&acc_empty[acc], accph ^ 1)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(smem + TcSmem::a + as * TC_A_BYTES);
-                    const uint32_t sb = smem_u32(smem + TcSmem::b + bs * TC_B_BYTES);
+                    const uint32_t d_tmem = tmem_base + acc * 256;
+                    const int N = (it.n + 15) & ~15;
+                    const uint32_t idesc = idesc_bf16(PAIR ? 256 : 128, N);
+                    for (int s = 0; s < it.slabs; ++s) {
+                        if (!mbar_wait_cluster(&a_full[as], aph) || !mbar_wait(&b_full[bs], bph)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t sa = smem_u32(smem + Sm::a + as * TC_A_BYTES);
+                        const uint32_t sb = smem_u32(smem + Sm::b + bs * B_STAGE);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        tc_mma_f16(d_tmem, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc,
-                                   (s > 0 || kk > 0) ? 1u : 0u);
-                    tc_commit(&a_empty[as]);
-                    tc_commit(&b_empty[bs]);
-                    if (++as == TC_SA) { as = 0; aph ^= 1; }
-                    if (++bs == TC_SB) { bs = 0; bph ^= 1; }
+                        for (int kk = 0; kk < 4; ++kk) {
+                            if (PAIR)
+                                tc_mma_f16_pair(d_tmem, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc,
+                                                (s > 0 || kk > 0) ? 1u : 0u);
+                            else
+                                tc_mma_f16(d_tmem, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc,
+                                           (s > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        issued = true;
+                        if (PAIR) {   // both CTAs' stages are free once these MMAs completed
+                            tc_commit_pair(mapa_shared(&a_empty[as], 0));
+                            tc_commit_pair(mapa_shared(&a_empty[as], peer));
+                            tc_commit_pair(mapa_shared(&b_empty[bs], 0));
+                            tc_commit_pair(mapa_shared(&b_empty[bs], peer));
+                        } else {
+                            tc_commit(&a_empty[as]);
+                            tc_commit(&b_empty[bs]);
+                        }
+                        if (++as == SA) { as = 0; aph ^= 1; }
+                        if (++bs == SB) { bs = 0; bph ^= 1; }
+                    }
+                    if (!ok) break;
+                    if (PAIR) {
+                        tc_commit_pair(mapa_shared(&acc_full[acc], 0));
+                        tc_commit_pair(mapa_shared(&acc_full[acc], peer));
+                    } else {
+                        tc_commit(&acc_full[acc]);
+                    }
                 }
-                if (!ok) break;
-                tc_commit(&acc_full[acc]);
-            }
-            if (!ok) {
-                fail(a.err, FM_ETIMEOUT);
-                atomicExch(&abort_flag, 1);
+                if (!ok) {
+                    fail(a.err, FM_ETIMEOUT);
+                    atomicExch(&abort_flag, 1);
+                }
+                // every MMA of this CTA (and its commits' arrivals) done before the pair may exit
+                if (issued) {
+                    if (PAIR) tc_commit_pair(mapa_shared(drain, 0));
+                    else tc_commit(drain);
+                    mbar_wait(drain, 0);
+                }
             }
         }
-    } else if (warp < 6) {
+    } else if (warp < R::EPI0) {
         // ------------------------------------------------------------ dequantisers
-        const int r = threadIdx.x - 64;   // row of the 128-row tile
-        int rs = 0, as = 0;
-        uint32_t rph = 0, aph = 0;
+        // Groups of 4 warps; group g takes the slabs whose running index sc has sc % NG == g, so NG
+        // slabs are dequantised at once (the per-slab chain of barrier, shared loads and stores is
+        // latency-bound). Thread t of a group rebuilds row t of the tile (both 32-value blocks).
+        constexpr int NG = R::DQ / 4;
+        const int t = threadIdx.x - 64;
+        const int grp = t >> 7;
+        const int r = t & 127;
         bool ok = true;
-        for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-            const Item it = decode_item<GATE_UP>(a, i);
-            for (int s = 0; s < it.slabs; ++s) {
-                if (!mbar_wait(&raw_full[rs], rph)) { ok = false; break; }
-                const uint8_t* raw = smem + TcSmem::raw + rs * kTileBytes;
+        int sc = 0;   // running slab index over this CTA's items
+        for (int i = unit; i < n_items && ok; i += n_units) {
+            const Item it = decode_item<PAIR>(a, i, crank);
+            for (int s = 0; s < it.slabs; ++s, ++sc) {
+                if (sc % NG != grp) continue;
+                const int rs = sc % SR, as = sc % SA;
+                const uint32_t rph = (sc / SR) & 1, aph = (sc / SA) & 1;
+                if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[rs], rph))) { ok = false; break; }
+                const uint8_t* raw = smem + Sm::raw + rs * kTileBytes;
                 const uint4 n0 = gguf_order(*reinterpret_cast<const uint4*>(raw + r * 32));
                 const uint4 n1 = gguf_order(*reinterpret_cast<const uint4*>(raw + r * 32 + 16));
-                const uint2 sc = *reinterpret_cast<const uint2*>(raw + kTileNibBytes + r * 8);
+                const uint2 sc2 = *reinterpret_cast<const uint2*>(raw + kTileNibBytes + r * 8);
                 mbar_arrive(&raw_empty[rs]);
-                const float d0 = __half2float(__ushort_as_half((unsigned short)(sc.x & 0xFFFF)));
-                const float m0 = __half2float(__ushort_as_half((unsigned short)(sc.x >> 16)));
-                const float d1 = __half2float(__ushort_as_half((unsigned short)(sc.y & 0xFFFF)));
-                const float m1 = __half2float(__ushort_as_half((unsigned short)(sc.y >> 16)));
+                const float d0 = __half2float(__ushort_as_half((unsigned short)(sc2.x & 0xFFFF)));
+                const float m0 = __half2float(__ushort_as_half((unsigned short)(sc2.x >> 16)));
+                const float d1 = __half2float(__ushort_as_half((unsigned short)(sc2.y & 0xFFFF)));
+                const float m1 = __half2float(__ushort_as_half((unsigned short)(sc2.y >> 16)));
                 uint4 ch[8];
                 deq_block(n0, d0, m0, ch);
                 deq_block(n1, d1, m1, ch + 4);
-                if (!mbar_wait(&a_empty[as], aph ^ 1)) { ok = false; break; }
-                uint8_t* arow = smem + TcSmem::a + as * TC_A_BYTES + r * 128;
+                if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[as], aph ^ 1))) { ok = false; break; }
+                uint8_t* arow = smem + Sm::a + as * TC_A_BYTES + r * 128;
 #pragma unroll
                 for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = ch[c];
                 fence_proxy_async_smem();
-                mbar_arrive(&a_full[as]);
-                if (++rs == TC_SR) { rs = 0; rph ^= 1; }
-                if (++as == TC_SA) { as = 0; aph ^= 1; }
+                __syncwarp();
+                if (lane == 0) {   // the warp's 32 rows are in place (on the first CTA's barrier)
+                    if (PAIR && crank == 1) mbar_arrive_cluster(mapa_shared(&a_full[as], 0));
+                    else mbar_arrive(&a_full[as]);
+                }
             }
         }
         if (!ok) {
@@ -302,29 +400,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
             atomicExch(&abort_flag, 1);
         }
     } else {
-        // ------------------------------------------------------------ epilogue (8 warps, 2 halves)
-        // Warp w reads TMEM lane group w % 4; the half (w - 6) / 4 takes every other 32-column chunk
-        // (c0 = 32 half + 64 i) with its own staging area and named barrier (1 + half, 128 threads);
-        // barrier 3 spans all 256 epilogue threads.
+        // ------------------------------------------------------------ epilogue (4 or 8 warps)
+        // Warp w reads TMEM lane group w % 4. With 8 warps, the half (w - EPI0) / 4 takes every other
+        // 32-column chunk (c0 = 32 half + 64 i) with its own staging area and named barrier (1 + half,
+        // 128 threads); barrier 3 spans all epilogue threads.
+        constexpr int HALVES = R::EPI / 4;
         const int lg = warp & 3;                 // TMEM lane group this warp may access
         const int row = lg * 32 + lane;          // accumulator row = TMEM lane
-        const int et = threadIdx.x - 192;        // 0..255
+        const int et = threadIdx.x - 32 * R::EPI0;   // 0 .. 32 EPI - 1
         const int half = et >> 7;
         const int ht = et & 127;                 // thread within the half
         const int hbar = 1 + half;
-        uint8_t* epi = smem + TcSmem::epi + half * TC_HALF_BYTES;
+        uint8_t* epi = smem + Sm::epi + half * TC_HALF_BYTES;
         float* xg = reinterpret_cast<float*>(epi);                   // GATE_UP: gate, cols 16-31 [16][64]
         float* xu = xg + 16 * 64;                                    //          up, cols 0-15 [16][64]
         uint16_t* hst = reinterpret_cast<uint16_t*>(xu + 16 * 64);   //          h tile [32][64] bf16
         float* ys = reinterpret_cast<float*>(epi);                   // DOWN: weighted y [32][TC_EPI_LD]
-        int* tok = reinterpret_cast<int*>(smem + TcSmem::epi + 2 * TC_HALF_BYTES);   // token per row [256]
+        int* tok = reinterpret_cast<int*>(smem + Sm::epi + 2 * TC_HALF_BYTES);   // token per row [256]
         float* wgt = reinterpret_cast<float*>(tok + 256);                            // weight per row [256]
         __shared__ int epi_abort;
         if (et == 0) epi_abort = 0;
-        named_bar(3, 256);
+        named_bar(3, 32 * R::EPI);
         int local = 0;
-        for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++local) {
-            const Item it = decode_item<GATE_UP>(a, i);
+        for (int i = unit; i < n_items; i += n_units, ++local) {
+            const Item it = decode_item<PAIR>(a, i, crank);
             const int acc = local & 1;
             const uint32_t accph = (local >> 1) & 1;
             // DOWN: where the item's rows go -- 0 weighted red.add into out, 1 a bf16 row of y_rows,
@@ -354,18 +453,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
                 }
             }
             if (!mbar_wait(&acc_full[acc], accph)) epi_abort = 1;
-            named_bar(3, 256);
+            named_bar(3, 32 * R::EPI);
             if (epi_abort) break;
-            if (!GATE_UP) {
+            if (!GATE_UP) {   // DOWN: 8 warps, 256 threads, one row each
                 if (et < it.n) {
                     tok[et] = tk;
                     wgt[et] = wk;
                 }
-                named_bar(3, 256);
+                named_bar(3, 32 * R::EPI);
             }
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(lg * 32) << 16) + acc * 256;
-            for (int c0 = 32 * half; c0 < it.n; c0 += 64) {
+            for (int c0 = 32 * half; c0 < it.n; c0 += 32 * HALVES) {
                 uint32_t v[32];
                 tmem_ld32(taddr + c0, v);
                 tmem_ld_wait();
@@ -427,7 +526,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
                 }
             }
             tc_fence_before();
-            mbar_arrive(&acc_empty[acc]);
+            __syncwarp();
+            if (lane == 0) {   // the warp's TMEM reads are done (on the first CTA's barrier)
+                if (PAIR && crank == 1) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+                else mbar_arrive(&acc_empty[acc]);
+            }
         }
         if (epi_abort) {
             fail(a.err, FM_ETIMEOUT);
@@ -436,10 +539,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
         if (!GATE_UP && a.meta) __threadfence_system();   // the peer stores land before the rank signals
     }
     tc_fence_before();
-    __syncthreads();
+    if (PAIR) cluster_sync();   // neither CTA leaves while the other may still signal its barriers
+    else __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, 512);
+        if (PAIR) tmem_dealloc_pair(tmem_base, 512);
+        else tmem_dealloc(tmem_base, 512);
     }
 }
 
@@ -460,7 +565,7 @@ static EncodeTiledFn encode_fn() {
 }
 
 // bf16 matrix [rows, cols] with row stride ld elements -> map with a {64, 32} box, 128-byte swizzle.
-static int make_bmap(CUtensorMap* m, const uint16_t* base, int rows, int cols, int ld) {
+static int make_bmap(CUtensorMap* m, const uint16_t* base, int rows, int cols, int ld, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) {
         set_error("cuTensorMapEncodeTiled unavailable");
@@ -468,7 +573,7 @@ static int make_bmap(CUtensorMap* m, const uint16_t* base, int rows, int cols, i
     }
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    const cuuint32_t box[2] = {64, TC_BOX_ROWS};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -491,10 +596,34 @@ static int sm_count() {
     return n;
 }
 
+template <bool GATE_UP, bool PAIR>
+static cudaError_t launch_tc_variant(const CUtensorMap& bmap, const CUtensorMap& bmap_big, const TcArgs& a, int grid,
+                                     int sm, cudaStream_t st) {
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(expert_tc_kernel<GATE_UP, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        attr = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = sm;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = PAIR ? 2 : 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, expert_tc_kernel<GATE_UP, PAIR>, bmap, bmap_big, a);
+}
+
 int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
     if (L.max_items <= 0) return FM_OK;
-    CUtensorMap bmap;
-    if (int rc = make_bmap(&bmap, L.act, L.act_rows, L.act_cols, L.act_ld)) return rc;
+    CUtensorMap bmap, bmap_big;
+    if (int rc = make_bmap(&bmap, L.act, L.act_rows, L.act_cols, L.act_ld, TC_BOX_ROWS)) return rc;
+    if (int rc = make_bmap(&bmap_big, L.act, L.act_rows, L.act_cols, L.act_ld, TC_BOX_BIG)) return rc;
     TcArgs a{};
     a.list = L.list;
     a.w_routed = L.w_routed;
@@ -517,22 +646,22 @@ int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
     a.meta = L.meta;
     for (int i = 0; i < kMaxRanks; ++i) a.yret[i] = L.yret[i];
     a.err = L.err;
-    const int grid = L.max_items < sm_count() ? L.max_items : sm_count();
-    const int sm = TcSmem::total;
-    if (gate_up) {
-        static bool attr = false;
-        if (!attr) {
-            cudaFuncSetAttribute(expert_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-            attr = true;
-        }
-        expert_tc_kernel<true><<<grid, TC_THREADS, sm, st>>>(bmap, a);
+    const int sms = sm_count();
+    const int sm_single = TcSmem<false>::total, sm_pair = TcSmem<true>::total;
+    cudaError_t e;
+    if (L.cta_pair) {
+        // one pair per two SMs; items are band pairs
+        const int pairs = L.max_items < sms / 2 ? L.max_items : sms / 2;
+        e = gate_up ? launch_tc_variant<true, true>(bmap, bmap_big, a, 2 * pairs, sm_pair, st)
+                    : launch_tc_variant<false, true>(bmap, bmap_big, a, 2 * pairs, sm_pair, st);
     } else {
-        static bool attr = false;
-        if (!attr) {
-            cudaFuncSetAttribute(expert_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-            attr = true;
-        }
-        expert_tc_kernel<false><<<grid, TC_THREADS, sm, st>>>(bmap, a);
+        const int grid = L.max_items < sms ? L.max_items : sms;
+        e = gate_up ? launch_tc_variant<true, false>(bmap, bmap_big, a, grid, sm_single, st)
+                    : launch_tc_variant<false, false>(bmap, bmap_big, a, grid, sm_single, st);
+    }
+    if (e != cudaSuccess) {
+        note_launch();
+        return cuda_status(e, gate_up ? "expert_tc<gate_up>" : "expert_tc<down>");
     }
     FM_LAUNCH_CHECK(gate_up ? "expert_tc<gate_up>" : "expert_tc<down>");
     return FM_OK;

@@ -51,6 +51,7 @@ struct TcLaunch {
     const int* meta;                 // peer expert-parallel DOWN (see expert_tc.cu)
     uint16_t* yret[kMaxRanks];
     int* err;
+    bool cta_pair;                   // CTA-pair kernel (M = 256 MMAs); the list entries are band pairs
 };
 int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st);
 struct GemvLaunch {
@@ -77,6 +78,7 @@ struct GemvLaunch {
     int* err;
 };
 int router_ksplit(int T, int H, int E);
+size_t router_scratch_bytes(int T, int H, int E);   // the logits scratch of launch_router
 int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
                           int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
                           int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int* err,

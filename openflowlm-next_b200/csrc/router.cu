@@ -1,12 +1,50 @@
-// Router: logits GEMM (bf16 x bf16 -> f32 on the tensor cores) and the per-token softmax / top-k.
+// Router: logits GEMM (bf16 x bf16 -> f32 on the tensor cores: cuBLAS from 256 tokens, a split-K
+// mma.sync kernel below) and the per-token softmax / top-k.
 //
 // Follows host::router_block (src/open_qwen36/block_host.cpp:766-803): float logits, max
 // subtraction, float exp with a double denominator, p = e * float(1/denom), top-k by probability
 // (strictly greater wins, so the lowest index wins a tie), weights renormalised by a double sum.
 // The shared-expert gate (core.cpp:4370-4373) rides along as router row E.
+#include <cublas_v2.h>
+
+#include <mutex>
+
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace fm {
+
+// From this many tokens the logits are one cuBLAS bf16 GEMM (a plain library GEMM: [T, H] x [H, E+1]
+// with f32 accumulation and output); below it, the split-K mma.sync kernel here, which needs no
+// library state (the no-allocation entry point and decode graphs use it).
+constexpr int kRouterBlasMinT = 256;
+
+struct BlasState {
+    cublasHandle_t h = nullptr;
+    void* ws = nullptr;
+};
+
+// One handle per device, with a fixed 32 MiB workspace so that later calls (and stream capture) never
+// allocate. Created on the first large-T call.
+static cublasHandle_t blas_handle(cudaStream_t st) {
+    static BlasState dev_state[64];
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    BlasState& b = dev_state[dev];
+    if (!b.h) {
+        constexpr size_t kWs = size_t(32) << 20;
+        if (cublasCreate(&b.h) != CUBLAS_STATUS_SUCCESS) { b.h = nullptr; return nullptr; }
+        if (cudaMalloc(&b.ws, kWs) != cudaSuccess || cublasSetWorkspace(b.h, b.ws, kWs) != CUBLAS_STATUS_SUCCESS) {
+            cublasDestroy(b.h);
+            b.h = nullptr;
+            return nullptr;
+        }
+    }
+    if (cublasSetStream(b.h, st) != CUBLAS_STATUS_SUCCESS) return nullptr;
+    return b.h;
+}
 
 // xb[t][h] = bf16(xm[t][h]) for f32 input (the rounding the reference applies at the device
 // boundary, core.cpp:5204).
@@ -112,19 +150,20 @@ __global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __re
         }
 }
 
-// One warp per token. logits row has E + 1 entries (the last is the shared-gate logit).
-// The K chunks of the logits (ks of them, [ks][T][E + 1]) are summed in chunk order into chunk 0.
-__global__ void router_topk_kernel(float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
-                                   int ks, float* __restrict__ probs, int32_t* __restrict__ idx, float* __restrict__ w,
-                                   float* __restrict__ sgate) {
+// One warp per token. A logits row holds E + 1 values (the last is the shared-gate logit) at row
+// stride ld. The K chunks of the logits (ks of them, [ks][T][ld]) are summed in chunk order into
+// chunk 0.
+__global__ void router_topk_kernel(float* __restrict__ logits, int ld, const float* __restrict__ bias, int T, int E,
+                                   int k, int ks, float* __restrict__ probs, int32_t* __restrict__ idx,
+                                   float* __restrict__ w, float* __restrict__ sgate) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
-    float* lg = logits + (size_t)warp * (E + 1);
+    float* lg = logits + (size_t)warp * ld;
     for (int e = lane; e <= E; e += 32) {
         float part[kMaxKSplit];   // all chunk loads in flight at once, then summed in chunk order
 #pragma unroll
         for (int z = 0; z < kMaxKSplit; ++z)
-            part[z] = z < ks ? logits[(size_t)z * T * (E + 1) + (size_t)warp * (E + 1) + e] : 0.f;
+            part[z] = z < ks ? logits[(size_t)z * T * ld + (size_t)warp * ld + e] : 0.f;
         float v = part[0];
 #pragma unroll
         for (int z = 1; z < kMaxKSplit; ++z)
@@ -178,6 +217,95 @@ __global__ void router_topk_kernel(float* __restrict__ logits, const float* __re
     }
 }
 
+// The same result for E <= 256 and unsplit logits, with each lane's (up to 8) probabilities kept in
+// registers: one exp per expert, then k rounds of (lane max, warp arg-max).
+// gate_row (bf16 [H], or NULL): the shared-gate logit is not in the logits rows but computed here as
+// the f32 dot product of the token's bf16 row xb[t] with it (the cuBLAS path leaves the odd row out
+// of the GEMM so that its output stays 16-byte aligned).
+__global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, const float* __restrict__ bias, int T,
+                                    int E, int k, float* __restrict__ probs, int32_t* __restrict__ idx,
+                                    float* __restrict__ w, float* __restrict__ sgate, const uint16_t* __restrict__ xb,
+                                    const uint16_t* __restrict__ gate_row, int H) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    const float* lg = logits + (size_t)warp * ld;
+    float gl = 0.f;
+    if (gate_row) {
+        if (sgate) {
+            const uint4* xr = reinterpret_cast<const uint4*>(xb + (size_t)warp * H);
+            const uint4* gr = reinterpret_cast<const uint4*>(gate_row);
+            for (int i = lane; i < H / 8; i += 32) {
+                const uint4 a = xr[i], b = gr[i];
+                const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    gl = fmaf(__uint_as_float(av[j] << 16), __uint_as_float(bv[j] << 16), gl);
+                    gl = fmaf(__uint_as_float(av[j] & 0xFFFF0000u), __uint_as_float(bv[j] & 0xFFFF0000u), gl);
+                }
+            }
+            gl = warp_sum(gl);
+        }
+    } else {
+        gl = lg[E];
+    }
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = lane + 32 * i;
+        v[i] = e < E ? lg[e] + (bias ? bias[e] : 0.f) : -INFINITY;
+    }
+    float mx = v[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, v[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    double den = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[i] = lane + 32 * i < E ? expf(v[i] - mx) : 0.f;   // e, then p below
+        den += (double)v[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    const float inv = (float)(1.0 / den);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[i] *= inv;
+        if (probs && lane + 32 * i < E) probs[(size_t)warp * E + lane + 32 * i] = v[i];
+    }
+    float ws[kMaxTopK];
+    int ids[kMaxTopK];
+    double wsum = 0.0;
+    uint32_t taken = 0;
+    for (int s = 0; s < k; ++s) {
+        float bp = -1.0f;
+        int be = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)   // ascending e within a lane: ties keep the lower index
+            if (!(taken >> i & 1u) && lane + 32 * i < E && v[i] > bp) { bp = v[i]; be = lane + 32 * i; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (op > bp || (op == bp && oe < be)) { bp = op; be = oe; }
+        }
+        if ((be & 31) == lane) taken |= 1u << (be >> 5);
+        ids[s] = be;
+        ws[s] = bp;
+        wsum += (double)bp;
+    }
+    if (lane < k) {   // lane s writes slot s
+        float wsel = 0.f;
+        int isel = 0;
+#pragma unroll
+        for (int s = 0; s < kMaxTopK; ++s)
+            if (s == lane) { wsel = ws[s]; isel = ids[s]; }
+        idx[(size_t)warp * k + lane] = isel;
+        w[(size_t)warp * k + lane] = (float)((double)wsel / wsum);
+    }
+    if (lane == 0 && sgate) sgate[warp] = 1.0f / (1.0f + expf(-gl));
+}
+
 int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st) {
     const long long n4 = n / 4;
     const int grid = (int)((n4 + 255) / 256 < 2048 ? (n4 + 255) / 256 : 2048);
@@ -187,7 +315,15 @@ int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st) {
 }
 
 // K chunks of the router GEMM: enough CTAs to cover the SMs when few tokens give few tiles.
+// Row stride of the logits: E + 1, padded to 8 floats for the cuBLAS path (an aligned output).
+static int router_ld(int T, int E) { return T >= kRouterBlasMinT ? (E + 1 + 7) / 8 * 8 : E + 1; }
+
+size_t router_scratch_bytes(int T, int H, int E) {
+    return (size_t)router_ksplit(T, H, E) * T * router_ld(T, E) * 4;
+}
+
 int router_ksplit(int T, int H, int E) {
+    if (T >= kRouterBlasMinT) return 1;
     const int tiles = ((E + 1 + RG_BN - 1) / RG_BN) * ((T + RG_BM - 1) / RG_BM);
     int ks = 1;
     while (ks < kMaxKSplit && tiles * ks < 148 && H % (2 * ks * RG_BK) == 0) ks *= 2;
@@ -197,11 +333,40 @@ int router_ksplit(int T, int H, int E) {
 int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
                   float* logits, float* probs, int32_t* idx, float* w, float* sgate, cudaStream_t st) {
     const int ks = router_ksplit(T, H, E);
-    dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM, ks);
-    router_logits_kernel<<<grid, 128, 0, st>>>(xb, router, logits, T, E + 1, H);
-    FM_LAUNCH_CHECK("router_logits");
-    router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, E, k, ks, probs, idx, w, sgate);
-    FM_LAUNCH_CHECK("router_topk");
+    const int ld = router_ld(T, E);
+    // the register top-k computes the shared-gate logit itself on the cuBLAS path (E rows in the GEMM)
+    const bool topk8 = ks == 1 && E <= 256;
+    const bool gate_in_topk = topk8 && T >= kRouterBlasMinT;
+    const int gemm_rows = gate_in_topk ? E : E + 1;
+    if (T >= kRouterBlasMinT) {
+        // logits (row-major [T, E+1]) = xb [T, H] . router [E+1, H]^T, as column-major C = op(A) op(B)
+        cublasHandle_t h = blas_handle(st);
+        if (!h) {
+            set_error("cuBLAS handle for the router GEMM could not be created");
+            return FM_ECUDA;
+        }
+        const float one = 1.0f, zero = 0.0f;
+        const cublasStatus_t bs = cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, gemm_rows, T, H, &one, router, CUDA_R_16BF, H, xb,
+                                               CUDA_R_16BF, H, &zero, logits, CUDA_R_32F, ld, CUBLAS_COMPUTE_32F,
+                                               CUBLAS_GEMM_DEFAULT);
+        note_launch();
+        if (bs != CUBLAS_STATUS_SUCCESS) {
+            set_error("router GEMM (cublasGemmEx) failed: status %d", (int)bs);
+            return FM_ECUDA;
+        }
+    } else {
+        dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM, ks);
+        router_logits_kernel<<<grid, 128, 0, st>>>(xb, router, logits, T, E + 1, H);
+        FM_LAUNCH_CHECK("router_logits");
+    }
+    if (topk8) {
+        router_topk8_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, ld, bias, T, E, k, probs, idx, w, sgate, xb,
+                                                         gate_in_topk ? router + (size_t)E * H : nullptr, H);
+        FM_LAUNCH_CHECK("router_topk8");
+    } else {
+        router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, ld, bias, T, E, k, ks, probs, idx, w, sgate);
+        FM_LAUNCH_CHECK("router_topk");
+    }
     return FM_OK;
 }
 

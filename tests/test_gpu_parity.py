@@ -209,6 +209,20 @@ def test_tc_matches_mma_path(dev):
     assert _rel(outs[1], outs[0], c["res"]) < 2e-3
 
 
+@pytest.mark.parametrize("H,F,FS,T,seed", [(2048, 128, 128, 300, 7), (256, 256, 128, 700, 8), (512, 192, 0, 90, 9)])
+def test_tc_pair_matches_single_cta(dev, H, F, FS, T, seed):
+    """The CTA-pair tcgen05 kernel (M = 256) against the one-CTA kernel and the oracle; F = 192 has an odd
+    band count, so "tc" falls back to one CTA per item there."""
+    c = cases.make_case(H=H, E=8, F=F, FS=FS, k=2, T=T, seed=seed)
+    outs = []
+    for path in ("tc", "tc1"):
+        layer, x, res, idx, w, out = _run_block(c, dev, path=path)
+        outs.append(out)
+    ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
+    assert _rel(outs[0], ref, c["res"]) < TOL
+    assert _rel(outs[0], outs[1], c["res"]) < 2e-3
+
+
 def test_bad_expert_id_raises(dev):
     import flowmoe
     c = cases.make_case(H=256, E=8, F=128, k=2, T=4, seed=4)
