@@ -61,9 +61,8 @@ typedef struct fm_layer {
     int32_t e_local;    /* experts held by this rank; E on one GPU */
     int32_t flags;      /* 0 = pick kernels by size (GEMV up to 32 tokens, tcgen05 from 64, mma.sync between);
                            1 = force mma.sync, 2 = force tcgen05, 3 = force the GEMV (when T <= 32),
-                           4 = force tcgen05 with one CTA per item (by default the tcgen05 GEMMs run
-                           as CTA pairs, M = 256, whenever every matrix has an even number of 128-row
-                           bands) */
+                           4 = force tcgen05 as CTA pairs (M = 256 MMAs; when every matrix has an
+                           even number of 128-row bands, else one CTA per item as with 2) */
     const uint8_t* gate_up;   /* tiles, e_local x (2 x F x H x 5/8 B): gate then up, per expert */
     const uint8_t* down;      /* tiles, e_local x (H x F x 5/8 B) */
     const uint8_t* shared_gate_up; /* tiles of the shared expert, or NULL */

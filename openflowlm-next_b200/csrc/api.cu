@@ -72,12 +72,14 @@ int cuda_status(cudaError_t e, const char* what) {
 constexpr int kBN = 64;        // rows per expert work item (expert_mma)
 constexpr int kBNTc = 256;     // rows per expert work item (expert_tc)
 constexpr int kTcMinTokens = 64;   // the tcgen05 path from this many tokens (below: the mma.sync path)
-constexpr int kFlagLegacy = 1, kFlagTc = 2, kFlagGemv = 3, kFlagTcSingle = 4;
+constexpr int kFlagLegacy = 1, kFlagTc = 2, kFlagGemv = 3, kFlagTcPair = 4;
 
-// The tcgen05 GEMMs run as CTA pairs (M = 256 MMAs over band pairs) when every matrix has an even
-// number of 128-row bands; flag kFlagTcSingle keeps one CTA per item.
+// Flag kFlagTcPair runs the tcgen05 GEMMs as CTA pairs (M = 256 MMAs over band pairs) when every
+// matrix has an even number of 128-row bands. One CTA per item is the default: measured faster on
+// B200 for these shapes (the pair's cross-SM barrier hand-offs cost more than the halved activation
+// traffic saves).
 static bool tc_pair(const fm_layer* L) {
-    return L->flags != kFlagTcSingle && (L->ffn / 64) % 2 == 0 && (L->shared_ffn / 64) % 2 == 0 &&
+    return L->flags == kFlagTcPair && (L->ffn / 64) % 2 == 0 && (L->shared_ffn / 64) % 2 == 0 &&
            (L->hidden / kTileRows) % 2 == 0;
 }
 constexpr int kDecodeMaxT = 32;    // the GEMV path up to this many tokens
@@ -201,7 +203,7 @@ static Path pick_path(const fm_layer* L, int T) {
     switch (L->flags) {
         case kFlagLegacy: return Path::Mma;
         case kFlagTc:
-        case kFlagTcSingle: return Path::Tc;
+        case kFlagTcPair: return Path::Tc;
         case kFlagGemv: return gemv_ok ? Path::Gemv : Path::Mma;
         default: break;
     }

@@ -3,7 +3,8 @@
 //
 // GEMV: each work item is (group, 128-row band, up to 8 sorted rows, K chunk). One CTA per SM: a
 // producer warp keeps 24 weight tiles (120 KB) of bulk copies in flight and double-buffers each item's
-// bf16 activation rows; 8 consumer warps each own 16 rows of the band. The tensor core multiplies the
+// bf16 activation rows; 16 consumer warps in two groups take alternate slab pairs, each warp 32 rows
+// of the band and one of the slab's two 32-value blocks. The tensor core multiplies the
 // raw codes, never dequantised weights: the A operand is 128 + q as bf16 (exact; one byte permute per
 // two codes, one 32-bit load per fragment thanks to the tile's fragment byte order), the B operand the
 // bf16 activations, so per 32-value block C = sum (128 + q) x exactly in f32, and the block's exact fp16
@@ -214,7 +215,9 @@ struct GemvArgs {
     int* err;                 // FM_ETIMEOUT when a bounded wait gives up
 };
 
-constexpr int GV_CONSUMERS = 8;                       // consumer warps: 32 tile rows x one of the slab's 2 blocks
+constexpr int GV_GWARPS = 8;                          // warps of a consumer group: 32 tile rows x one of 2 blocks
+constexpr int GV_GROUPS = 2;                          // groups take alternate slab pairs of an item
+constexpr int GV_CONSUMERS = GV_GWARPS * GV_GROUPS;   // consumer warps
 constexpr int GV_THREADS = 32 * (GV_CONSUMERS + 1);   // + one producer warp
 constexpr int GV_MAX_K = 2048;                        // activation K per item (one chunk)
 constexpr int GV_WSTAGES = 24;                        // weight tiles in flight per CTA (120 KB)
@@ -226,7 +229,8 @@ struct GvSmem {
     static constexpr int act = w + GV_WSTAGES * kTileBytes;
     static constexpr int tab = act + 2 * GV_ACT_BYTES;                 // [8 warps][2 slabs][32] (d, m - 128 d)
     static constexpr int xch = tab + GV_CONSUMERS * 64 * 8;            // [128][8] f32 (block-1 partials, up rows)
-    static constexpr int bars = xch + 128 * kGemvRows * 4;
+    static constexpr int xch2 = xch + 128 * kGemvRows * 4;             // [2][128][8] f32 (group-1 partials)
+    static constexpr int bars = xch2 + 2 * 128 * kGemvRows * 4;
     static constexpr int total = bars + (2 * GV_WSTAGES + 4) * 8 + 128;
 };
 
@@ -332,7 +336,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_kernel(GemvArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_items = a.list[0], KC = a.list[1];
     if (threadIdx.x == 0) {
-        for (int i = 0; i < GV_WSTAGES; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], GV_CONSUMERS); }
+        for (int i = 0; i < GV_WSTAGES; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], GV_GWARPS); }
         for (int i = 0; i < 2; ++i) { mbar_init(&act_full[i], 1); mbar_init(&act_empty[i], GV_CONSUMERS); }
         s_abort = 0;
         mbar_fence_init();
@@ -382,28 +386,34 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_kernel(GemvArgs a) {
         }
     } else {
         // ------------------------------------------------------------ consumer warps
+        // Two groups of 8 warps take alternate slab pairs of each item (two independent chains of
+        // barrier waits, shared loads and MMAs per SM); group 1 hands its sums to group 0 at the end.
         const int g = lane >> 2, c = lane & 3;
-        const int rg = warp & 3, blk = warp >> 2;          // rows 32 rg .. 32 rg + 31, block blk of each slab
+        const int grp = warp >> 3;
+        const int rg = warp & 3, blk = (warp >> 2) & 1;    // rows 32 rg .. 32 rg + 31, block blk of each slab
         float2* tab = reinterpret_cast<float2*>(smem + GvSmem::tab) + warp * 64;
-        int ws = 0, ab = 0;
-        uint32_t wph = 0, aph = 0;
+        float* xch2 = reinterpret_cast<float*>(smem + GvSmem::xch2);
+        int ab = 0;
+        uint32_t aph = 0;
+        int sc0 = 0;   // running slab index of the item's first slab (the producer's fill order)
         for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
             const GvItem it = gv_decode(a, i, KC);
             bool ok = __all_sync(0xffffffffu, mbar_wait(&act_full[ab], aph));
             const uint16_t* xs = reinterpret_cast<const uint16_t*>(smem + GvSmem::act + ab * GV_ACT_BYTES);
             float acc2[2][4] = {};
-            for (int s = 0; s < it.slabs && ok; s += 2) {
+            for (int s = 2 * grp; s < it.slabs && ok; s += 2 * GV_GROUPS) {
+                const int ws = (sc0 + s) % GV_WSTAGES;
+                const uint32_t wph = ((sc0 + s) / GV_WSTAGES) & 1;
                 if (s + 1 == it.slabs) {   // an odd last slab
                     if (!__all_sync(0xffffffffu, mbar_wait(&w_full[ws], wph))) { ok = false; break; }
                     const uint8_t* t1[1] = {smem + GvSmem::w + ws * kTileBytes};
                     gv_blocks<1>(t1, xs, tab, s, blk, rg, lane, acc2);
                     if (lane == 0) mbar_arrive(&w_empty[ws]);
-                    if (++ws == GV_WSTAGES) { ws = 0; wph ^= 1; }
                     break;
                 }
                 // two slabs at a time: independent chains
-                const int ws1 = ws + 1 == GV_WSTAGES ? 0 : ws + 1;
-                const uint32_t wph1 = ws + 1 == GV_WSTAGES ? wph ^ 1 : wph;
+                const int ws1 = (sc0 + s + 1) % GV_WSTAGES;
+                const uint32_t wph1 = ((sc0 + s + 1) / GV_WSTAGES) & 1;
                 if (!__all_sync(0xffffffffu, mbar_wait(&w_full[ws], wph) && mbar_wait(&w_full[ws1], wph1))) {
                     ok = false;
                     break;
@@ -414,9 +424,8 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_kernel(GemvArgs a) {
                     mbar_arrive(&w_empty[ws]);
                     mbar_arrive(&w_empty[ws1]);
                 }
-                ws = ws1 + 1 == GV_WSTAGES ? 0 : ws1 + 1;
-                wph = ws1 + 1 == GV_WSTAGES ? wph1 ^ 1 : wph1;
             }
+            sc0 += it.slabs;
             __syncwarp();
             if (lane == 0) mbar_arrive(&act_empty[ab]);
             if (++ab == 2) { ab = 0; aph ^= 1; }
@@ -424,18 +433,28 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_kernel(GemvArgs a) {
             named_bar(1, 32 * GV_CONSUMERS);
             if (s_abort) break;
             // C fragments: acc2[mt][0..1] = tile row 32 rg + 16 mt + g, tokens 2c, 2c+1; [2..3] = row +8.
-            // As 8 values h = 2 mt + (row half), token 2c + (h & 1): rows trs[h >> 1]. The block-1 warps
-            // hand their partial sums to the block-0 warps, which own the rows from here on.
+            // As 8 values h = 2 mt + (row half), token 2c + (h & 1): rows trs[h >> 1]. Group 1 hands its
+            // sums to group 0, then the block-1 warps to the block-0 warps, which own the rows from here on.
             float acc[8];
 #pragma unroll
             for (int h = 0; h < 8; ++h) acc[h] = acc2[h >> 2][h & 3];
             const int trs[4] = {rg * 32 + g, rg * 32 + g + 8, rg * 32 + 16 + g, rg * 32 + 24 + g};
-            if (blk == 1) {
+            if (grp == 1) {
+#pragma unroll
+                for (int h = 0; h < 8; ++h) xch2[(blk * 128 + trs[h >> 1]) * kGemvRows + 2 * c + (h & 1)] = acc[h];
+            }
+            named_bar(1, 32 * GV_CONSUMERS);
+            if (grp == 0) {
+#pragma unroll
+                for (int h = 0; h < 8; ++h) acc[h] += xch2[(blk * 128 + trs[h >> 1]) * kGemvRows + 2 * c + (h & 1)];
+            }
+            if (grp == 0 && blk == 1) {
 #pragma unroll
                 for (int h = 0; h < 8; ++h) xch[trs[h >> 1] * kGemvRows + 2 * c + (h & 1)] = acc[h];
             }
             named_bar(1, 32 * GV_CONSUMERS);
-            if (blk == 0) {
+            const bool owner = grp == 0 && blk == 0;
+            if (owner) {
 #pragma unroll
                 for (int h = 0; h < 8; ++h) acc[h] += xch[trs[h >> 1] * kGemvRows + 2 * c + (h & 1)];
             }
@@ -450,7 +469,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_kernel(GemvArgs a) {
 #pragma unroll
                 for (int h = 0; h < 8; ++h) {
                     const int t = 2 * c + (h & 1);
-                    if (blk == 0 && t < it.n) part[(size_t)(it.row0 + t) * ncols + colof(trs[h >> 1])] = acc[h];
+                    if (owner && t < it.n) part[(size_t)(it.row0 + t) * ncols + colof(trs[h >> 1])] = acc[h];
                 }
                 __threadfence();
                 named_bar(1, 32 * GV_CONSUMERS);
@@ -461,7 +480,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_kernel(GemvArgs a) {
 #pragma unroll
                 for (int h = 0; h < 8; ++h) {
                     const int t = 2 * c + (h & 1);
-                    if (blk == 0 && t < it.n) {
+                    if (owner && t < it.n) {
                         float v = 0.f;
                         for (int q = 0; q < KC; ++q)
                             v += __ldcg(a.part + (size_t)q * a.part_rows * ncols + (size_t)(it.row0 + t) * ncols + colof(trs[h >> 1]));
@@ -471,12 +490,12 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_kernel(GemvArgs a) {
             }
             if (GATE_UP) {
                 // up rows (rg 2-3) hand their sums to the gate rows (rg 0-1); h = bf16(silu(g) * u)
-                if (blk == 0 && rg >= 2) {
+                if (owner && rg >= 2) {
 #pragma unroll
                     for (int h = 0; h < 8; ++h) xch[(trs[h >> 1] - 64) * kGemvRows + 2 * c + (h & 1)] = acc[h];
                 }
                 named_bar(1, 32 * GV_CONSUMERS);
-                if (blk == 0 && rg < 2) {
+                if (owner && rg < 2) {
 #pragma unroll
                     for (int h = 0; h < 8; ++h) {
                         const int t = 2 * c + (h & 1), tr = trs[h >> 1];
@@ -485,7 +504,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_kernel(GemvArgs a) {
                     }
                 }
                 named_bar(1, 32 * GV_CONSUMERS);
-            } else if (blk == 0) {
+            } else if (owner) {
 #pragma unroll
                 for (int h = 0; h < 8; ++h) {
                     const int t = 2 * c + (h & 1);

@@ -130,13 +130,13 @@ class MoELayer:
                           router.data_ptr(), _ptr(self.router_bias))
         self._ws: torch.Tensor | None = None
 
-    PATHS = {"auto": 0, "mma": 1, "tc": 2, "gemv": 3, "tc1": 4}
+    PATHS = {"auto": 0, "mma": 1, "tc": 2, "gemv": 3, "tc2": 4}
 
     @property
     def path(self) -> str:
         """Kernel choice: "auto" (GEMV up to 32 tokens, tcgen05 from 64, mma.sync between), or forced
-        "mma", "tc" (CTA pairs where the band counts allow), "tc1" (tcgen05, one CTA per item), "gemv"
-        (the GEMV only applies up to 32 tokens)."""
+        "mma", "tc" (tcgen05, one CTA per item), "tc2" (tcgen05 as CTA pairs where the band counts
+        allow), "gemv" (the GEMV only applies up to 32 tokens)."""
         return {v: k for k, v in self.PATHS.items()}[self._L.flags]
 
     @path.setter

@@ -212,10 +212,10 @@ def test_tc_matches_mma_path(dev):
 @pytest.mark.parametrize("H,F,FS,T,seed", [(2048, 128, 128, 300, 7), (256, 256, 128, 700, 8), (512, 192, 0, 90, 9)])
 def test_tc_pair_matches_single_cta(dev, H, F, FS, T, seed):
     """The CTA-pair tcgen05 kernel (M = 256) against the one-CTA kernel and the oracle; F = 192 has an odd
-    band count, so "tc" falls back to one CTA per item there."""
+    band count, so "tc2" falls back to one CTA per item there."""
     c = cases.make_case(H=H, E=8, F=F, FS=FS, k=2, T=T, seed=seed)
     outs = []
-    for path in ("tc", "tc1"):
+    for path in ("tc2", "tc"):
         layer, x, res, idx, w, out = _run_block(c, dev, path=path)
         outs.append(out)
     ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
