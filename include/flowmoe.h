@@ -191,7 +191,7 @@ FM_API int fm_ep_combine(const fm_layer* L, float* out, const uint16_t* ysorted,
 typedef struct fm_ep_group {
     int32_t rank, n_ranks;           /* this process's rank, the group size (<= FM_EP_MAX_RANKS) */
     int32_t t_cap;                   /* the most tokens any rank passes to one call */
-    int32_t timeout_ms;              /* bound of each device wait on the peers (0: 2000) */
+    int32_t timeout_ms;              /* bound of each device wait on the peers (0: 10000) */
     void* sym[FM_EP_MAX_RANKS];      /* each rank's symmetric buffer as mapped here; sym[rank] is our own */
 } fm_ep_group;
 

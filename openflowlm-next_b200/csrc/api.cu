@@ -953,7 +953,7 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     a.H = H;
     a.k = k;
     a.r_cap = sl.r_cap;
-    a.timeout_ns = (long long)(g->timeout_ms > 0 ? g->timeout_ms : 2000) * 1000000ll;
+    a.timeout_ns = (long long)(g->timeout_ms > 0 ? g->timeout_ms : 10000) * 1000000ll;
     if (cudaMemsetAsync(a.err, 0, 16, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
     const uint16_t* xb = static_cast<const uint16_t*>(xm);
     if (xm_dtype == FM_F32) {

@@ -163,7 +163,7 @@ class PeerGroup:
     (fm_ipc_alloc), the IPC handles are all-gathered over ``group`` (host objects only), each rank maps
     the others' (fm_ipc_open). ``layer`` must hold this rank's expert range."""
 
-    def __init__(self, layer: MoELayer, t_cap: int, group=None, timeout_ms: int = 2000):
+    def __init__(self, layer: MoELayer, t_cap: int, group=None, timeout_ms: int = 10000):
         self.layer = layer
         self.group = group
         G, r = dist.get_world_size(group), dist.get_rank(group)
@@ -214,7 +214,7 @@ class PeerEPMoELayer:
     """The MoE block of one rank over peer memory: one fm_ep_peer_layer call per layer, rows and y rows
     stored straight into their owners' buffers over NVLink, no NCCL and no host round trip."""
 
-    def __init__(self, layer: MoELayer, t_cap: int, group=None, timeout_ms: int = 2000):
+    def __init__(self, layer: MoELayer, t_cap: int, group=None, timeout_ms: int = 10000):
         self.cfg = layer.cfg
         self.layer = layer
         self.peers = PeerGroup(layer, t_cap, group, timeout_ms)
