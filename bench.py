@@ -259,6 +259,50 @@ def sweep(hbm, tfl_burst):
                                     "TFLOP_s": round(tf, 2), "tensor_frac": round(tf / tfl_burst, 4), "stages_ms": st,
                                     "gate_up_TFLOP_s": round(gu_tf, 1) if gu_tf else None,
                                     "max_expert_rows": int(cnt.max()), "empty_experts": int((cnt == 0).sum())})
+    # config 5 on one GPU: 48 C36 layers of x + MoE(RMSNorm(x)), decode T=64, the stack captured in one
+    # CUDA graph; HBM bytes = per layer the touched experts' Q4_1 + shared expert + router
+    from flowmoe.stack import MoEStack
+    from flowmoe.synth import C36, synth_stack
+    cfg36 = flowmoe.MoEConfig(**C36)
+    del layer
+    torch.cuda.empty_cache()
+    layers, norms = synth_stack(cfg36, 48, seed=5)
+    T = 64
+    x, _ = synth_tokens(T, cfg36.hidden, seed=5)
+    x = x.float()
+    e_bytes = 3 * cfg36.hidden * cfg36.ffn * 5 // 8
+    fixed = 3 * cfg36.hidden * cfg36.shared_ffn * 5 // 8 + (cfg36.n_experts + 1) * cfg36.hidden * 2
+    stack_runs = []
+    for path in ("gemv", "auto"):
+        for L in layers:
+            L.path = path
+        stack = MoEStack(layers, norms).capture(T)   # the 48 layers as one CUDA graph
+        for _ in range(3):
+            stack.forward(x)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            stack.forward(x)
+        b.record()
+        torch.cuda.synchronize()
+        stack_runs.append((a.elapsed_time(b) / 10, path))
+        del stack
+    ms, path = min(stack_runs)
+    # bytes of one step: each layer's touched experts (one eager pass records the routing)
+    idx = torch.empty(T, cfg36.top_k, dtype=torch.int32, device="cuda")
+    with torch.no_grad():
+        cur = x.clone()
+        nbytes = 0
+        for L, nw in zip(layers, norms):
+            cur = L.forward_norm(cur, nw, out=torch.empty_like(cur), idx=idx)
+            nbytes += int(torch.unique(idx).numel()) * e_bytes + fixed
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    out["stack_c36_T64"] = {"layers": 48, "T": T, "path": path, "ms": round(ms, 3),
+                            "tokens_per_s": round(T / ms * 1e3, 1), "GB_per_step": round(nbytes / 1e9, 2),
+                            "GB_s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+                            "both_paths_ms": {p: round(m, 3) for m, p in stack_runs}}
+    del layers
     return out
 
 

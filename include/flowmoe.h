@@ -60,7 +60,7 @@ typedef struct fm_layer {
     int32_t e_begin;    /* first expert held by this rank (expert parallel); 0 on one GPU */
     int32_t e_local;    /* experts held by this rank; E on one GPU */
     int32_t flags;      /* 0 = pick kernels by size (GEMV up to 32 tokens, tcgen05 from 64, mma.sync between);
-                           1 = force mma.sync, 2 = force tcgen05, 3 = force the GEMV (when T <= 32),
+                           1 = force mma.sync, 2 = force tcgen05, 3 = force the GEMV (when T <= 64),
                            4 = force tcgen05 as CTA pairs (M = 256 MMAs; when every matrix has an
                            even number of 128-row bands, else one CTA per item as with 2) */
     const uint8_t* gate_up;   /* tiles, e_local x (2 x F x H x 5/8 B): gate then up, per expert */
@@ -122,6 +122,14 @@ FM_API int fm_moe_block(const fm_layer* L, const void* xm, int32_t xm_dtype, con
  * routing. */
 FM_API int fm_moe_layer(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, int32_t T, int32_t t_real,
                  float* out, int32_t* idx, float* w, void* workspace, size_t workspace_bytes, void* stream);
+
+/* One layer of the MoE stack: x_{l+1} = x + MoE(RMSNorm(x)). The post-attention RMSNorm (weight norm_w
+ * bf16 [H], eps; Core::rmsnorm_host, core.cpp:3014-3044, fp64 reduction) is fused with the bf16
+ * conversion, then the layer runs as fm_moe_layer with xm = RMSNorm(x) and res = x (the staged_tail ->
+ * ffn_block sequence, core.cpp:4934-4957). x and out [T, H] f32 (out may not alias x). */
+FM_API int fm_moe_layer_norm(const fm_layer* L, const float* x, const uint16_t* norm_w, float eps, int32_t T,
+                             int32_t t_real, float* out, int32_t* idx, float* w, void* workspace, size_t workspace_bytes,
+                             void* stream);
 
 /* The dispatch stage alone: per local expert counts [e_local], exclusive offsets [e_local + 1] (the
  * last = routed pair count), pos [t_real, k] = row of each (token, slot) pair in the expert-sorted

@@ -82,7 +82,10 @@ static bool tc_pair(const fm_layer* L) {
     return L->flags == kFlagTcPair && (L->ffn / 64) % 2 == 0 && (L->shared_ffn / 64) % 2 == 0 &&
            (L->hidden / kTileRows) % 2 == 0;
 }
-constexpr int kDecodeMaxT = 32;    // the GEMV path up to this many tokens
+constexpr int kDecodeMaxT = 32;    // the GEMV path up to this many tokens (auto)
+constexpr int kGemvMaxT = 64;      // ... and up to this many when the GEMV is forced (flags = 3)
+
+static int gemv_max_t(const fm_layer* L) { return L->flags == kFlagGemv ? kGemvMaxT : kDecodeMaxT; }
 constexpr int kGemvRowsApi = 8;    // sorted rows per GEMV item (decode.cu)
 constexpr int kChunk = 2048;   // dispatch chunk (dispatch.cu)
 
@@ -128,7 +131,7 @@ static Layout make_layout(const fm_layer* L, int T) {
     const int rt_shared = (T + kBN - 1) / kBN;
     o.max_gu = rt_routed * (L->ffn / 64) + rt_shared * (L->shared_ffn / 64);
     o.max_dn = (rt_routed + (L->shared_ffn ? rt_shared : 0)) * (H / kTileRows);
-    const bool decode = T <= kDecodeMaxT;
+    const bool decode = T <= gemv_max_t(L);
     if (decode) {
         // GEMV items: 16-row tiles, up to 4 K chunks each
         const int tt = o.P / kGemvRowsApi + L->e_local + (T + kGemvRowsApi - 1) / kGemvRowsApi;
@@ -199,7 +202,7 @@ static int xm_to_bf16(const fm_layer* L, const void* xm, int dtype, int T, void*
 enum class Path { Mma, Tc, Gemv };
 
 static Path pick_path(const fm_layer* L, int T) {
-    const bool gemv_ok = T <= kDecodeMaxT && L->e_local < 1024 && T * L->top_k <= 1024;
+    const bool gemv_ok = T <= gemv_max_t(L) && L->e_local < 1024 && T * L->top_k <= 1024;
     switch (L->flags) {
         case kFlagLegacy: return Path::Mma;
         case kFlagTc:
@@ -447,6 +450,43 @@ extern "C" FM_API int fm_moe_block(const fm_layer* L, const void* xm, int32_t xm
     return run_block(L, xb, res, idx, w, shared_gate, T, t_real, out, workspace, lo, st);
 }
 
+namespace fm {
+// Router + shared expert + experts over bf16 activations xb (shared by fm_moe_layer and
+// fm_moe_layer_norm).
+static int moe_layer_xb(const fm_layer* L, const uint16_t* xb, const float* res, int T, int t_real, float* out,
+                        int32_t* idx, float* w, void* workspace, const Layout& lo, cudaStream_t st) {
+    int32_t* ids = idx ? idx : at<int32_t>(workspace, lo.idx);
+    float* ws_w = w ? w : at<float>(workspace, lo.w);
+    float* sg = at<float>(workspace, lo.sgate);
+    prof_begin(kStageRouter, st);
+    if (int rc = launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k,
+                               at<float>(workspace, lo.logits), nullptr, ids, ws_w, sg, st))
+        return rc;
+    prof_end(kStageRouter, st);
+    return run_block(L, xb, res, ids, ws_w, sg, T, t_real, out, workspace, lo, st);
+}
+}  // namespace fm
+
+extern "C" FM_API int fm_moe_layer_norm(const fm_layer* L, const float* x, const uint16_t* norm_w, float eps, int32_t T,
+                                        int32_t t_real, float* out, int32_t* idx, float* w, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+    g_err[0] = 0;
+    if (int rc = validate(L, T)) return rc;
+    if (t_real < 0 || t_real > T || !norm_w || !(eps >= 0.f)) {
+        set_error("t_real %d outside [0, T=%d], or no norm weight / a negative eps", t_real, T);
+        return FM_EINVAL_SHAPE;
+    }
+    if (T == 0) return FM_OK;
+    const Layout lo = make_layout(L, T);
+    if (int rc = check_ws(lo, workspace, workspace_bytes)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    uint16_t* xb = at<uint16_t>(workspace, lo.xb);
+    prof_begin(kStageToBf16, st);
+    if (int rc = launch_rmsnorm_bf16(x, norm_w, eps, T, L->hidden, xb, st)) return rc;
+    prof_end(kStageToBf16, st);
+    return moe_layer_xb(L, xb, x, T, t_real, out, idx, w, workspace, lo, st);
+}
+
 extern "C" FM_API int fm_moe_layer(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, int32_t T,
                             int32_t t_real, float* out, int32_t* idx, float* w, void* workspace, size_t workspace_bytes,
                             void* stream) {
@@ -462,15 +502,7 @@ extern "C" FM_API int fm_moe_layer(const fm_layer* L, const void* xm, int32_t xm
     cudaStream_t st = (cudaStream_t)stream;
     const uint16_t* xb = nullptr;
     if (int rc = xm_to_bf16(L, xm, xm_dtype, T, workspace, lo, &xb, st)) return rc;
-    int32_t* ids = idx ? idx : at<int32_t>(workspace, lo.idx);
-    float* ws_w = w ? w : at<float>(workspace, lo.w);
-    float* sg = at<float>(workspace, lo.sgate);
-    prof_begin(kStageRouter, st);
-    if (int rc = launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k,
-                               at<float>(workspace, lo.logits), nullptr, ids, ws_w, sg, st))
-        return rc;
-    prof_end(kStageRouter, st);
-    return run_block(L, xb, res, ids, ws_w, sg, T, t_real, out, workspace, lo, st);
+    return moe_layer_xb(L, xb, res, T, t_real, out, idx, w, workspace, lo, st);
 }
 
 extern "C" FM_API int fm_moe_dispatch(const fm_layer* L, const int32_t* idx, int32_t T, int32_t t_real, int32_t* counts,

@@ -6,6 +6,7 @@
 namespace fm {
 
 int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st);
+int launch_rmsnorm_bf16(const float* x, const uint16_t* w, float eps, int T, int H, uint16_t* xb, cudaStream_t st);
 int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
                   float* logits, float* probs, int32_t* idx, float* w, float* sgate, cudaStream_t st);
 int launch_dispatch(const int32_t* idx, int P, int e_begin, int e_local, int E, int shared_base, int shared_rows,

@@ -306,6 +306,42 @@ __global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, co
     if (lane == 0 && sgate) sgate[warp] = 1.0f / (1.0f + expf(-gl));
 }
 
+// Post-attention RMSNorm fused with the bf16 conversion, one warp per token: xb[t] = bf16(f32((x[t] /
+// sqrt(mean(x[t]^2) + eps)) * w)) with the sum of squares, the rms, the division and the product in
+// fp64 (Core::rmsnorm_host, src/open_qwen36/core.cpp:3014-3044, groups = 1; weight bf16).
+__global__ void rmsnorm_bf16_kernel(const float* __restrict__ x, const uint16_t* __restrict__ w, double eps, int T, int H,
+                                    uint16_t* __restrict__ xb) {
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (t >= T) return;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * H);
+    double ss = 0.0;
+    for (int i = lane; i < H / 4; i += 32) {
+        const float4 v = xr[i];
+        ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const double rms = sqrt(ss / (double)H + eps);
+    const uint2* wr = reinterpret_cast<const uint2*>(w);
+    uint2* o = reinterpret_cast<uint2*>(xb + (size_t)t * H);
+    for (int i = lane; i < H / 4; i += 32) {
+        const float4 v = xr[i];
+        const uint2 ww = wr[i];
+        const float a = (float)(((double)v.x / rms) * (double)__uint_as_float(ww.x << 16));
+        const float b = (float)(((double)v.y / rms) * (double)__uint_as_float(ww.x & 0xFFFF0000u));
+        const float c = (float)(((double)v.z / rms) * (double)__uint_as_float(ww.y << 16));
+        const float d = (float)(((double)v.w / rms) * (double)__uint_as_float(ww.y & 0xFFFF0000u));
+        o[i] = make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
+    }
+}
+
+int launch_rmsnorm_bf16(const float* x, const uint16_t* w, float eps, int T, int H, uint16_t* xb, cudaStream_t st) {
+    if (T <= 0) return FM_OK;
+    rmsnorm_bf16_kernel<<<(T + 7) / 8, 256, 0, st>>>(x, w, (double)eps, T, H, xb);
+    FM_LAUNCH_CHECK("rmsnorm_bf16");
+    return FM_OK;
+}
+
 int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st) {
     const long long n4 = n / 4;
     const int grid = (int)((n4 + 255) / 256 < 2048 ? (n4 + 255) / 256 : 2048);

@@ -136,7 +136,7 @@ class MoELayer:
     def path(self) -> str:
         """Kernel choice: "auto" (GEMV up to 32 tokens, tcgen05 from 64, mma.sync between), or forced
         "mma", "tc" (tcgen05, one CTA per item), "tc2" (tcgen05 as CTA pairs where the band counts
-        allow), "gemv" (the GEMV only applies up to 32 tokens)."""
+        allow), "gemv" (the GEMV, up to 64 tokens)."""
         return {v: k for k, v in self.PATHS.items()}[self._L.flags]
 
     @path.setter
@@ -273,6 +273,24 @@ class MoELayer:
         return out
 
     __call__ = forward
+
+    def forward_norm(self, x: torch.Tensor, norm_w: torch.Tensor, eps: float = 1e-6, t_real: int | None = None,
+                     out: torch.Tensor | None = None, idx: torch.Tensor | None = None,
+                     w: torch.Tensor | None = None) -> torch.Tensor:
+        """One layer of the MoE stack: out = x + MoE(RMSNorm(x)) (fm_moe_layer_norm). x f32 [T, H]; norm_w
+        bf16 [H] (the post-attention RMSNorm weight)."""
+        if x.dtype != torch.float32 or x.device != self.device or x.dim() != 2 or not x.is_contiguous():
+            raise ValueError(f"x must be a contiguous f32 [T, {self.cfg.hidden}] tensor on {self.device}")
+        T = x.shape[0]
+        t_real = T if t_real is None else t_real
+        out = torch.empty_like(x) if out is None else out
+        if out.data_ptr() == x.data_ptr():
+            raise ValueError("out may not alias x")
+        nw = norm_w.to(self.device, torch.bfloat16).contiguous()
+        ws = self.workspace(T)
+        call("fm_moe_layer_norm", ctypes.byref(self._L), x.data_ptr(), nw.data_ptr(), ctypes.c_float(eps), T, t_real,
+             out.data_ptr(), _ptr(idx), _ptr(w), ws.data_ptr(), ws.numel(), _stream(self.device))
+        return out
 
 
 def router_block(xm: torch.Tensor, Wr: torch.Tensor, topk: int):

@@ -62,3 +62,37 @@ def synth_tokens(T: int, H: int, seed: int = 0, device="cuda"):
     x = torch.randn(T, H, generator=g, device=device).to(torch.bfloat16)
     res = torch.randn(T, H, generator=g, device=device)
     return x, res
+
+
+def random_q4_1(rows: int, k: int, gen: torch.Generator, device="cuda") -> torch.Tensor:
+    """GGUF Q4_1 blocks uint8[rows, k/32, 20] drawn directly (fp16 d ~ |N(0, 0.0013)|, fp16 m ~ -8 d, random
+    nibbles), so values spread like N(0, 0.02) weights quantised, without running the quantiser: for
+    benchmarks that only need the bytes (the layer stack's 24 GB of experts)."""
+    nb = k // 32
+    d = (torch.randn(rows, nb, generator=gen, device=device).abs() * 0.0013 + 1e-4).to(torch.float16)
+    m = (-8.0 * d.float() + torch.randn(rows, nb, generator=gen, device=device) * 1e-3).to(torch.float16)
+    blocks = torch.empty(rows, nb, 20, dtype=torch.uint8, device=device)
+    blocks[:, :, 0:2] = d.view(torch.uint8).view(rows, nb, 2)
+    blocks[:, :, 2:4] = m.view(torch.uint8).view(rows, nb, 2)
+    blocks[:, :, 4:] = torch.randint(0, 256, (rows, nb, 16), generator=gen, device=device, dtype=torch.uint8)
+    return blocks
+
+
+def synth_stack(cfg: MoEConfig, n_layers: int, seed: int = 0, device="cuda"):
+    """n_layers independent seeded layers of geometry cfg (random Q4_1 blocks, bf16 N(0, 0.02) router and
+    shared gate) and their RMSNorm weights bf16 1 + N(0, 0.01)."""
+    H, F, FS, E = cfg.hidden, cfg.ffn, cfg.shared_ffn, cfg.local
+    layers, norms = [], []
+    for l in range(n_layers):
+        g = _gen(seed * 7919 + l, device)
+        gate = random_q4_1(E * F, H, g, device).view(E, F, H // 32, 20)
+        up = random_q4_1(E * F, H, g, device).view(E, F, H // 32, 20)
+        down = random_q4_1(E * H, F, g, device).view(E, H, F // 32, 20)
+        wr = (torch.randn(H, cfg.n_experts, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        shared = None
+        if FS:
+            sgw = (torch.randn(H, generator=g, device=device) * 0.02).to(torch.bfloat16)
+            shared = (random_q4_1(FS, H, g, device), random_q4_1(FS, H, g, device), random_q4_1(H, FS, g, device), sgw)
+        layers.append(MoELayer.from_q4_1(cfg, gate, up, down, wr, shared=shared, device=device))
+        norms.append((1.0 + torch.randn(H, generator=g, device=device) * 0.01).to(torch.bfloat16))
+    return layers, norms

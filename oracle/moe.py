@@ -51,6 +51,28 @@ def sigmoid(x):
     return 1 / (1 + np.exp(-x))
 
 
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+    """Post-attention RMSNorm -> xm (f32): ``Core::rmsnorm_host`` (``src/open_qwen36/core.cpp:3014-3044``,
+    groups = 1): the sum of squares, the rms and the product with the weight in fp64,
+    out = f32((x / sqrt(mean(x^2) + eps)) * w); the weight arrives as bf16 values."""
+    xd = np.asarray(x, np.float64)
+    rms = np.sqrt((xd * xd).sum(-1, keepdims=True) / xd.shape[-1] + eps)
+    return ((xd / rms) * np.asarray(w, np.float64)).astype(np.float32)
+
+
+def moe_stack_f64(x, layers, eps: float = 1e-6, engine_rounding: bool = True):
+    """x_{l+1} = x_l + MoE_l(RMSNorm_l(x_l)) over a list of layers, each a dict with ``norm_w``, ``Wr``,
+    ``gate``, ``up``, ``down``, ``shared``, ``k`` (the staged_tail -> ffn_block sequence of
+    ``core.cpp:4934-4957`` repeated per layer; ``replica.py:121-143``)."""
+    x = np.asarray(x, np.float32)
+    for L in layers:
+        xm = rmsnorm(x, L["norm_w"], eps)
+        _, idx, w = router_block(bf16_round(xm), L["Wr"], L["k"])
+        x = moe_block_f64(xm, x, idx, w, L["gate"], L["up"], L["down"], shared=L["shared"],
+                          engine_rounding=engine_rounding).astype(np.float32)
+    return x
+
+
 def router_block(xm: np.ndarray, Wr: np.ndarray, topk: int, bias: np.ndarray | None = None):
     """(probs [T, E], idx int32 [T, topk], w [T, topk]) in fp64.
 

@@ -233,3 +233,23 @@ def test_bad_expert_id_raises(dev):
     w = torch.full((4, 2), 0.5, device=dev)
     with pytest.raises(flowmoe._lib.FlowMoeError, match="FM_EINVAL_EXPERT"):
         layer.moe_block(x, res, idx, w)
+
+
+@pytest.mark.parametrize("T,path", [(5, "auto"), (64, "auto"), (64, "gemv")])
+def test_moe_stack_rmsnorm_matches_oracle(dev, T, path):
+    """Three layers of x + MoE(RMSNorm(x)) (config 5's stack, small) against the fp64 oracle stack."""
+    import flowmoe
+    from flowmoe.stack import MoEStack
+    rng = np.random.default_rng(T)
+    cs, layers, nws = [], [], []
+    for l in range(3):
+        c = cases.make_case(H=256, E=16, F=128, FS=128, k=4, T=T, seed=100 + l)
+        c["norm_w"] = OM.bf16_round((1.0 + rng.normal(0, 0.01, c["H"])).astype(np.float32))
+        cs.append(c)
+        layers.append(_layer(c, dev, path))
+        nws.append(torch.from_numpy(c["norm_w"]))
+    x0 = cs[0]["res"]
+    got = MoEStack(layers, nws).forward(torch.from_numpy(x0).to(dev)).cpu().numpy()
+    want = OM.moe_stack_f64(x0, cs)
+    # relative to the total change the stack makes to x
+    assert float(np.abs(got - want).max() / np.abs(want - x0).max()) < TOL

@@ -144,3 +144,10 @@ def test_reference_cpp_router_agrees_with_oracle(golden):
     r = golden["router"]
     assert np.array_equal(idx, r["c1_idx"])
     np.testing.assert_allclose(w, r["c1_w"], rtol=1e-4)
+
+
+def test_rmsnorm_matches_reference_route(golden):
+    """The post-attention RMSNorm (xm of replica.route, reference open_kernels/model/replica.py:121-124)."""
+    g = golden["moe"]
+    xm = OM.rmsnorm(g["xres"], g["postln"])
+    np.testing.assert_array_equal(xm, g["xm"])
