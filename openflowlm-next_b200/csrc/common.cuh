@@ -89,6 +89,20 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* sh, int* total) 
     return base + x - v;
 }
 
+// One warp copies a row of n16 16-byte words: each lane issues up to 8 loads before its stores, so a
+// row's loads are in flight together.
+__device__ __forceinline__ void warp_copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int n16, int lane) {
+    for (int c0 = lane; c0 < n16; c0 += 32 * 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (c0 + 32 * u < n16) v[u] = __ldg(src + c0 + 32 * u);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (c0 + 32 * u < n16) dst[c0 + 32 * u] = v[u];
+    }
+}
+
 // Workspace layout shared by the entry points (byte offsets, 256-aligned). Built on the host.
 struct Workspace {
     size_t logits;      // f32 [T, E+1]

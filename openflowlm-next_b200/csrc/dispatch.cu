@@ -187,7 +187,7 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ xb, const int* _
     else return;
     const uint4* src = reinterpret_cast<const uint4*>(xb + (size_t)t * H);
     uint4* dst = reinterpret_cast<uint4*>(xperm + (size_t)row * H);
-    for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
+    warp_copy_row(dst, src, H / 8, lane);
 }
 
 // Work lists from a segment table seg[i] = (local expert, first row, rows) (expert parallel: the rows
@@ -305,7 +305,7 @@ __global__ void ep_regroup_kernel(const uint16_t* __restrict__ xrecv, int R, con
         return;
     }
     uint4* d = reinterpret_cast<uint4*>(xexp + (size_t)dst * H);
-    for (int i = lane; i < H / 8; i += 32) d[i] = src[i];
+    warp_copy_row(d, src, H / 8, lane);
 }
 
 int launch_ep_regroup(const int* rc, int G, int El, const uint16_t* xrecv, int R, const uint16_t* xb, int t_real, int H,

@@ -120,10 +120,10 @@ __global__ void __launch_bounds__(1024) ep_plan_peer_kernel(EpPeerArgs a, int* _
     }
 }
 
-// Rows -> owners. Warp per sorted row p < P: pair q = pair[p], token q / k, expert idx[q], owner
+// Rows -> owners. Warp per sorted row p: pair q = pair[p], token q / k, expert idx[q], owner
 // d = expert / El, destination row send_base[e] + (p - offsets[e]) of d's receive buffer (a peer store
-// of H bf16, 16 bytes per lane) and its metadata word. Rows P.. P + t_real - 1 of the walk copy this
-// rank's own tokens to its receive buffer's shared-expert rows. The last block to finish publishes the
+// of H bf16, 16 bytes per lane) and its metadata word. After the sorted rows, the walk copies this rank's
+// own t_real tokens to its receive buffer's shared-expert rows. The last block to finish publishes the
 // rows-arrived flag on every rank (after each block's system-scope fence).
 __global__ void __launch_bounds__(256) ep_scatter_rows_kernel(EpPeerArgs a, const uint16_t* __restrict__ xb,
                                                               const int* __restrict__ pair,
@@ -133,13 +133,28 @@ __global__ void __launch_bounds__(256) ep_scatter_rows_kernel(EpPeerArgs a, cons
     const int lane = threadIdx.x & 31;
     const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
     const bool live = *reinterpret_cast<volatile int*>(a.err + 1) == 0;
-    const int Ps = min(P, offsets[a.E]);   // sorted rows: pairs with an id outside [0, E) were left out
+    // The sorted rows for owner d are the contiguous range [offsets[d El], offsets[(d + 1) El]). The
+    // walk interleaves the owners (slot i -> owner i % G, its (i / G)-th row), so that at any moment
+    // the stores spread over every peer's links instead of draining one owner after another.
+    __shared__ int dstart[kMaxRanks + 1];
+    __shared__ int maxlen;
+    if (threadIdx.x <= a.G) dstart[threadIdx.x] = offsets[min((int)threadIdx.x * a.El, a.E)];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int m = 0;
+        for (int d = 0; d < a.G; ++d) m = max(m, dstart[d + 1] - dstart[d]);
+        maxlen = m;
+    }
+    __syncthreads();
+    const int nslots = a.G * maxlen;
     if (live) {
-        for (int r = wid; r < P + t_real; r += nw) {
+        for (int i = wid; i < nslots + t_real; i += nw) {
             const uint4* src;
             uint4* dst;
-            if (r < P) {
-                if (r >= Ps) continue;
+            if (i < nslots) {
+                const int d0 = i % a.G, j = i / a.G;
+                if (j >= dstart[d0 + 1] - dstart[d0]) continue;
+                const int r = dstart[d0] + j;
                 const int q = pair[r];
                 const int e = idx[q];
                 const int d = e / a.El;
@@ -148,11 +163,11 @@ __global__ void __launch_bounds__(256) ep_scatter_rows_kernel(EpPeerArgs a, cons
                 dst = reinterpret_cast<uint4*>(a.sym[d] + a.off_x + (size_t)row * a.H * 2);
                 if (lane == 0) reinterpret_cast<int*>(a.sym[d] + a.off_meta)[row] = (a.rank << 24) | r;
             } else {
-                const int t = r - P;
+                const int t = i - nslots;
                 src = reinterpret_cast<const uint4*>(xb + (size_t)t * a.H);
                 dst = reinterpret_cast<uint4*>(a.sym[a.rank] + a.off_x + (size_t)(a.r_cap + t) * a.H * 2);
             }
-            for (int i = lane; i < a.H / 8; i += 32) dst[i] = __ldg(src + i);
+            warp_copy_row(dst, src, a.H / 8, lane);
         }
     }
     __threadfence_system();
