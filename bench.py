@@ -473,6 +473,23 @@ def run_flowmoe(args):
     return 0
 
 
+def profile_case(name: str, calls: int = 6) -> int:
+    """A few plain layer calls for an ncu capture (no timing, no JSON): "decode" = C30 T=32 (GEMV path),
+    "prefill" = the headline C36 T=8192 layer."""
+    import flowmoe
+    from flowmoe.synth import C30, C36, synth_layer, synth_tokens
+    cfg = flowmoe.MoEConfig(**(C30 if name == "decode" else C36))
+    T = 32 if name == "decode" else T_HEADLINE
+    layer = synth_layer(cfg, seed=0)
+    x, res = synth_tokens(T, cfg.hidden, seed=T)
+    out = torch.empty_like(res)
+    for _ in range(calls):
+        layer.forward(x, res, out=out)
+    torch.cuda.synchronize()
+    print(f"profile case {name}: {calls} calls", flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -484,7 +501,11 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="N > 1: the expert-parallel exchange (peer-memory stores, or NCCL all-to-all)")
+    ap.add_argument("--profile-case", choices=["decode", "prefill"], default=None,
+                    help="run a few plain layer calls for an ncu capture and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        return profile_case(args.profile_case)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

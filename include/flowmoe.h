@@ -90,6 +90,11 @@ FM_API int fm_gate_up_to_tiles(const uint8_t* gate, const uint8_t* up, int32_t F
 /* Tile layout -> GGUF Q4_1 blocks (the inverse; used to prove the repack is a permutation). */
 FM_API int fm_tiles_to_q4_1(const uint8_t* tiles, int32_t rows, int32_t k, uint8_t* blocks, void* stream);
 
+/* The reference's q4nx pool numerics (open_kernels/q4_1_pack.py:18-37, scale_dtype=bfloat16): every
+ * fp16 d and m of n_tiles tiles rounded in place to bf16 precision (round to nearest even), so the
+ * kernels dequantise with the narrowed scales. For bit-level agreement with the NPU's pool. */
+FM_API int fm_tiles_narrow_scales(uint8_t* tiles, int64_t n_tiles, void* stream);
+
 /* Router weight bf16 Wr [H, E] row-major (the reference's layout, block_host.cpp:775-777) and the
  * shared-expert gate bf16 sgw [H] (or NULL) -> the layer's router array bf16 [E + 1, H]. */
 FM_API int fm_router_pack(const uint16_t* wr, const uint16_t* sgw, int32_t hidden, int32_t n_experts, uint16_t* router,

@@ -154,6 +154,33 @@ extern "C" FM_API int fm_tiles_to_q4_1(const uint8_t* tiles, int32_t rows, int32
     return FM_OK;
 }
 
+// q4nx numerics: every d and m of a tile array rounded to bf16 precision (round to nearest even) and
+// stored back as fp16. A bf16-rounded fp16 value keeps at most 8 significant bits and its fp16
+// exponent range, so the fp16 store is exact (up to an overflow at the very top of the fp16 range,
+// past 65504, which Q4_1 weight scales do not reach); the kernels then see the narrowed scales.
+__global__ void narrow_scales_kernel(uint8_t* __restrict__ tiles, long long n_tiles) {
+    const long long n = n_tiles * (kTileBytes - kTileNibBytes) / 2;   // fp16 scale values
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long tile = i / 512, j = i % 512;
+        __half* h = reinterpret_cast<__half*>(tiles + tile * kTileBytes + kTileNibBytes) + j;
+        const float f = __half2float(*h);
+        *h = __float2half_rn(__bfloat162float(__float2bfloat16_rn(f)));
+    }
+}
+
+extern "C" FM_API int fm_tiles_narrow_scales(uint8_t* tiles, int64_t n_tiles, void* stream) {
+    if (!tiles || n_tiles < 0) {
+        set_error("fm_tiles_narrow_scales: null tiles or negative count");
+        return FM_EINVAL_SHAPE;
+    }
+    if (n_tiles == 0) return FM_OK;
+    const long long n = n_tiles * 512;
+    const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    narrow_scales_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(tiles, n_tiles);
+    FM_LAUNCH_CHECK("narrow_scales");
+    return FM_OK;
+}
+
 extern "C" FM_API int fm_router_pack(const uint16_t* wr, const uint16_t* sgw, int32_t hidden, int32_t n_experts,
                               uint16_t* router, void* stream) {
     if (hidden <= 0 || n_experts <= 0) {

@@ -55,6 +55,7 @@ SIGNATURES = {
     "fm_q4_1_to_tiles": [P, I32, I32, P, P],
     "fm_tiles_to_q4_1": [P, I32, I32, P, P],
     "fm_gate_up_to_tiles": [P, P, I32, I32, P, P],
+    "fm_tiles_narrow_scales": [P, ctypes.c_int64, P],
     "fm_router_pack": [P, P, I32, I32, P, P],
     "fm_workspace_size": [LP, I32, ctypes.POINTER(SZ)],
     "fm_router_topk": [LP, P, I32, I32, P, P, P, P, P, SZ, P],

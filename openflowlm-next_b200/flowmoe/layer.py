@@ -106,6 +106,15 @@ def tiles_to_q4_1(tiles: torch.Tensor, rows: int, k: int) -> torch.Tensor:
     return dst
 
 
+def narrow_scales(tiles: torch.Tensor) -> torch.Tensor:
+    """In place: every d and m of a tile array rounded to bf16 precision (fm_tiles_narrow_scales)."""
+    n = tiles.numel()
+    if n % 5120:
+        raise ValueError("not a whole number of 5120-byte tiles")
+    call("fm_tiles_narrow_scales", tiles.data_ptr(), n // 5120, _stream(tiles.device))
+    return tiles
+
+
 def _bf16(t, device) -> torch.Tensor:
     if isinstance(t, np.ndarray):
         if t.dtype == np.uint16:
@@ -146,10 +155,13 @@ class MoELayer:
     # ---- construction from the reference's block layout
     @classmethod
     def from_q4_1(cls, cfg: MoEConfig, gate_blocks, up_blocks, down_blocks, router_w, shared=None, device="cuda",
-                  router_bias=None):
+                  router_bias=None, scales: str = "fp16"):
         """gate/up blocks [E_local, F, H/32, 20], down [E_local, H, F/32, 20] (numpy or torch uint8),
         router_w [H, E] (bf16 values), shared = (gate, up, down blocks, sgw [H]) or None,
-        router_bias [E] f32 added to the logits (or None)."""
+        router_bias [E] f32 added to the logits (or None). scales="bf16" narrows every block's d and m
+        to bf16 first: the reference's q4nx pool numerics."""
+        if scales not in ("fp16", "bf16"):
+            raise ValueError(f"scales must be 'fp16' or 'bf16', not {scales!r}")
         H, F, E = cfg.hidden, cfg.ffn, cfg.local
         g = _as_dev_u8(gate_blocks, device).reshape(E, -1)
         u = _as_dev_u8(up_blocks, device).reshape(E, -1)
@@ -176,6 +188,10 @@ class MoELayer:
         call("fm_router_pack", wr.data_ptr(), _ptr(sgw_t), H, cfg.n_experts, router.data_ptr(), _stream(device))
         if router_bias is not None and not isinstance(router_bias, torch.Tensor):
             router_bias = torch.from_numpy(np.asarray(router_bias, np.float32))
+        if scales == "bf16":
+            for t in (gate_up, down, sgu, sdn):
+                if t is not None:
+                    narrow_scales(t)
         return cls(cfg, gate_up.reshape(-1), down.reshape(-1), router, sgu, sdn, router_bias)
 
     # ---- workspace

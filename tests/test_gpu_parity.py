@@ -253,3 +253,32 @@ def test_moe_stack_rmsnorm_matches_oracle(dev, T, path):
     want = OM.moe_stack_f64(x0, cs)
     # relative to the total change the stack makes to x
     assert float(np.abs(got - want).max() / np.abs(want - x0).max()) < TOL
+
+
+def test_bf16_scales_narrowing(dev, golden):
+    """q4nx numerics: tiles with narrowed scales map back to exactly the blocks with d, m rounded to bf16,
+    and a layer built with scales="bf16" matches the oracle's bf16-scale dequantisation."""
+    import flowmoe
+    from flowmoe.layer import narrow_scales
+    blocks = golden["q4_1"]["blocks"]                       # [64, 256/32, 20]
+    rows, k = blocks.shape[0], blocks.shape[1] * 32
+    pad = np.concatenate([blocks, blocks])                   # 128 rows: one tile band
+    t = flowmoe.q4_1_to_tiles(pad, 2 * rows, k, dev)
+    back = flowmoe.tiles_to_q4_1(narrow_scales(t), 2 * rows, k).cpu().numpy().reshape(pad.shape)
+    d = np.ascontiguousarray(pad[..., 0:4]).view(np.float16).astype(np.float32)
+    want = pad.copy()
+    want[..., 0:4] = OQ.bf16_narrow(d).astype(np.float16).view(np.uint8).reshape(want[..., 0:4].shape)
+    assert np.array_equal(back, want)
+    assert np.array_equal(OQ.dequant_q4_1(back[:rows]), golden["q4_1"]["dequant_bf16_scales"])
+    c = cases.make_case(H=256, E=8, F=128, FS=0, k=2, T=40, seed=21)
+    cfg = flowmoe.MoEConfig(hidden=c["H"], n_experts=c["E"], top_k=c["k"], ffn=c["F"], shared_ffn=0)
+    layer = flowmoe.MoELayer.from_q4_1(cfg, c["gate"], c["up"], c["down"], c["Wr"], device=dev, scales="bf16")
+    x = torch.from_numpy(c["x"]).to(dev).to(torch.bfloat16)
+    res = torch.from_numpy(c["res"]).to(dev)
+    _, idx, w = layer.router_block(x)
+    out = layer.moe_block(x, res, idx, w).cpu().numpy()
+    narrow = lambda bl: np.stack([flowmoe.tiles_to_q4_1(narrow_scales(flowmoe.q4_1_to_tiles(b, b.shape[0], b.shape[1] * 32, dev)),
+                                                        b.shape[0], b.shape[1] * 32).cpu().numpy().reshape(b.shape) for b in bl])
+    ref = OM.moe_block_f64(c["x"], c["res"], idx.cpu().numpy(), w.cpu().numpy(), narrow(c["gate"]), narrow(c["up"]),
+                           narrow(c["down"]))
+    assert _rel(out, ref, c["res"]) < TOL

@@ -151,3 +151,9 @@ def test_rmsnorm_matches_reference_route(golden):
     g = golden["moe"]
     xm = OM.rmsnorm(g["xres"], g["postln"])
     np.testing.assert_array_equal(xm, g["xm"])
+
+
+def test_dequant_bf16_scales_bit_exact(golden):
+    """The q4nx numerics (d, m narrowed to bf16): the reference's dequant_q4_1(scale_dtype=bfloat16)."""
+    g = golden["q4_1"]
+    assert np.array_equal(OQ.dequant_q4_1(g["blocks"], bf16_scales=True), g["dequant_bf16_scales"])
