@@ -63,7 +63,10 @@ def _ptr(t: torch.Tensor | None) -> int | None:
 
 def _as_dev_u8(blocks, device) -> torch.Tensor:
     if isinstance(blocks, np.ndarray):
-        blocks = torch.from_numpy(np.ascontiguousarray(blocks, np.uint8))
+        b = np.ascontiguousarray(blocks, np.uint8)
+        if not b.flags.writeable:   # e.g. a read-only memory map of a model file: copy once
+            b = b.copy()
+        blocks = torch.from_numpy(b)
     return blocks.to(device=device, dtype=torch.uint8).contiguous()
 
 
