@@ -2,7 +2,7 @@
 //
 // One persistent CTA per SM walks the work list (group, band, first sorted row, rows). A work item
 // is D[128 weight rows x n tokens] = W_band[128 x K] . X[n x K]^T with n <= 256, K walked in 64-wide
-// slabs. Warp roles (448 threads):
+// slabs. Warp roles (480 threads for gate_up, 576 for down):
 //   warp 0      producer: per slab, one 5120-byte bulk copy of the raw Q4_1 weight tile and
 //               ceil(n/32) TMA loads (128-byte swizzle) of the sorted bf16 activation rows;
 //   warp 1      TMEM owner and MMA issuer: four tcgen05.mma (M=128, N=n rounded to 16, K=16) per
@@ -30,19 +30,17 @@
 
 namespace fm {
 
-// Warp roles: 0 weight producer, 1 MMA issuer, then DQ dequantiser warps, EPI epilogue warps, and the
-// activation producer last. gate_up (K = H = 2048, light epilogue) is dequantiser-bound: 8 + 4; down
-// (K = F = 512, a y row per token and band) is epilogue-bound: 4 + 8.
+// Warp roles: 0 weight producer, 1 MMA issuer, then DQ dequantiser warps (groups of 4 working alternate
+// slabs), EPI epilogue warps, and the activation producer last. gate_up (K = H = 2048, light epilogue):
+// 8 + 4, 480 threads; down (K = F = 512, a y row per token and band): 8 + 8, 576 threads.
 template <bool GATE_UP>
 struct TcRoles {
-    static constexpr int DQ = GATE_UP ? 8 : 4;
+    static constexpr int DQ = 8;
     static constexpr int EPI = GATE_UP ? 4 : 8;
     static constexpr int EPI0 = 2 + DQ;          // first epilogue warp
     static constexpr int BWARP = EPI0 + EPI;     // activation producer warp
+    static constexpr int THREADS = 32 * (BWARP + 1);
 };
-constexpr int TC_BWARP = 14;
-constexpr int TC_THREADS = 32 * (TC_BWARP + 1);   // 480 threads, both GEMMs
-static_assert(TcRoles<true>::BWARP == TC_BWARP && TcRoles<false>::BWARP == TC_BWARP, "warp roles");
 constexpr int TC_BOX_BIG = 128;            // activation rows per large TMA box
 constexpr int TC_BN = 256;                 // max tokens per work item (MMA N)
 constexpr int TC_A_BYTES = 128 * 128;      // 128 rows x 64 bf16
@@ -177,7 +175,7 @@ __device__ __forceinline__ Item decode_item(const TcArgs& a, int i, uint32_t cra
 // first CTA issues the MMAs and commits the stage / accumulator releases to both CTAs' barriers. No
 // load is shared between the CTAs and no multicast copy is used.
 template <bool GATE_UP, bool PAIR>
-__global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_constant__ CUtensorMap bmap,
+__global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel(const __grid_constant__ CUtensorMap bmap,
                                                                   const __grid_constant__ CUtensorMap bmap_big, TcArgs a) {
     using R = TcRoles<GATE_UP>;
     using Sm = TcSmem<PAIR>;
@@ -233,7 +231,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) expert_tc_kernel(const __grid_c
 
     if (warp == 0 || warp == R::BWARP) {
         // ------------------------------------------------------------ producers (lane 0 of each)
-        // warp 0: the raw weight tiles (streamed from HBM, SR deep); warp TC_BWARP: the activation
+        // warp 0: the raw weight tiles (streamed from HBM, SR deep); warp R::BWARP: the activation
         // rows (TMA, SB deep). Separate threads, so the weight stream runs ahead of the activations.
         const bool weights = warp == 0;
         if (lane == 0) {
@@ -606,7 +604,7 @@ static cudaError_t launch_tc_variant(const CUtensorMap& bmap, const CUtensorMap&
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(TC_THREADS);
+    cfg.blockDim = dim3(TcRoles<GATE_UP>::THREADS);
     cfg.dynamicSmemBytes = sm;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
