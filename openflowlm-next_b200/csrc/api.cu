@@ -6,6 +6,8 @@
 #include <cstdio>
 #include <cstring>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -867,8 +869,9 @@ static EpSymLayout ep_sym_layout(const fm_layer* L, const fm_ep_group* g) {
 
 struct EpPeerLayout {
     size_t err, xb, logits, counts, offsets, blk_hist, pos, pair, idx, w, sgate, send_base, seg, gu_list, dn_list, hexp;
+    size_t gu_list_sh, dn_list_sh;
     size_t total;
-    int max_gu, max_dn, fmax;
+    int max_gu, max_dn, fmax, max_gu_sh, max_dn_sh;
 };
 
 static EpPeerLayout ep_peer_layout(const fm_layer* L, const fm_ep_group* g, int T) {
@@ -898,9 +901,40 @@ static EpPeerLayout ep_peer_layout(const fm_layer* L, const fm_ep_group* g, int 
     o.gu_list = take((size_t)(4 + 4 * o.max_gu) * 4);
     o.dn_list = take((size_t)(4 + 4 * o.max_dn) * 4);
     o.hexp = take(((size_t)r_cap + tc) * o.fmax * 2);
+    o.max_gu_sh = rt_shared * (L->shared_ffn / 64);
+    o.max_dn_sh = L->shared_ffn ? rt_shared * (H / kTileRows) : 0;
+    o.gu_list_sh = take((size_t)(4 + 4 * o.max_gu_sh) * 4);
+    o.dn_list_sh = take((size_t)(4 + 4 * o.max_dn_sh) * 4);
     o.total = off;
     return o;
 }
+
+// A second stream and fork / join events per device (the shared expert of the expert-parallel layer
+// runs beside the row exchange). Created on the first call, outside any stream capture.
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+static SideStream* side_stream() {
+    static SideStream per_dev[64];
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    SideStream& x = per_dev[dev];
+    if (!x.s) {
+        if (cudaStreamCreateWithFlags(&x.s, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&x.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming) != cudaSuccess) {
+            x.s = nullptr;
+            return nullptr;
+        }
+    }
+    return &x;
+}
+
+constexpr int kScatterSms = 20;   // SMs left to the row exchange while the shared expert runs
 
 static int ep_group_check(const fm_layer* L, const fm_ep_group* g, bool need_sym = true) {
     if (int rc = validate(L, 0)) return rc;
@@ -1018,22 +1052,82 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
                               counts, offsets, at<int>(workspace, lo.pos), at<int>(workspace, lo.pair),
                               at<int>(workspace, lo.gu_list), 0, 0, at<int>(workspace, lo.dn_list), 0, kBNTc, a.err, st)))
         return rc;
+    // out = res before the fork: the shared expert adds into it on the side stream
+    if (T > 0 && cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "out = res");
+    const int bdiv = tc_pair(L) ? 2 : 1;
+    // The shared expert needs no exchange: it runs on a side stream over this rank's own bf16 rows, on
+    // all SMs but kScatterSms, while the rows travel; the combine waits for it (both add into out).
+    SideStream* side = shared_on ? side_stream() : nullptr;
+    if (shared_on && !side) {
+        set_error("expert parallel: could not create the side stream");
+        return FM_ECUDA;
+    }
+    if (shared_on) {
+        cudaStream_t s2 = side->s;
+        if (cudaEventRecord(side->fork, st) != cudaSuccess || cudaStreamWaitEvent(s2, side->fork, 0) != cudaSuccess)
+            return cuda_status(cudaGetLastError(), "fork the shared expert");
+        if ((rc = launch_seg_lists(nullptr, 0, El, 0, t_real, at<int>(workspace, lo.gu_list_sh), L->ffn / 64 / bdiv,
+                                   L->shared_ffn / 64 / bdiv, at<int>(workspace, lo.dn_list_sh),
+                                   H / kTileRows / bdiv, kBNTc, s2)))
+            return rc;
+        uint16_t* hsh = at<uint16_t>(workspace, lo.hexp) + (size_t)sl.r_cap * lo.fmax;
+        TcLaunch sgu{};
+        sgu.max_items = lo.max_gu_sh;
+        sgu.max_ctas = sm_count_api() - kScatterSms;
+        sgu.list = at<int>(workspace, lo.gu_list_sh);
+        sgu.act = xb;
+        sgu.act_rows = T;
+        sgu.act_cols = H;
+        sgu.act_ld = H;
+        sgu.w_routed = L->gate_up;
+        sgu.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
+        sgu.w_shared = L->shared_gate_up;
+        sgu.shared_group = El;
+        sgu.K_routed = H;
+        sgu.K_shared = H;
+        sgu.h_out = hsh;
+        sgu.h_ld = lo.fmax;
+        sgu.err = a.err + 1;
+        sgu.cta_pair = bdiv == 2;
+        if ((rc = launch_expert_tc(true, sgu, s2))) return rc;
+        TcLaunch sdn{};
+        sdn.max_items = lo.max_dn_sh;
+        sdn.max_ctas = sm_count_api() - kScatterSms;
+        sdn.list = at<int>(workspace, lo.dn_list_sh);
+        sdn.act = hsh;
+        sdn.act_rows = T;
+        sdn.act_cols = lo.fmax;
+        sdn.act_ld = lo.fmax;
+        sdn.w_routed = L->down;
+        sdn.w_routed_stride = (size_t)H * L->ffn / 32 * 20;
+        sdn.w_shared = L->shared_down;
+        sdn.shared_group = El;
+        sdn.K_routed = L->ffn;
+        sdn.K_shared = L->shared_ffn;
+        sdn.out = out;
+        sdn.H = H;
+        sdn.k = k;
+        sdn.shared_base = 0;
+        sdn.sgate = sg;
+        sdn.err = a.err + 1;
+        sdn.cta_pair = bdiv == 2;
+        if ((rc = launch_expert_tc(false, sdn, s2))) return rc;
+        if (cudaEventRecord(side->join, s2) != cudaSuccess) return cuda_status(cudaGetLastError(), "join event");
+    }
     if ((rc = launch_ep_post_counts(a, counts, st))) return rc;
     if ((rc = launch_ep_plan_peer(a, at<int>(workspace, lo.send_base), at<int>(workspace, lo.seg), st))) return rc;
-    const int bdiv = tc_pair(L) ? 2 : 1;
-    if ((rc = launch_seg_lists(at<int>(workspace, lo.seg), El, El, sl.r_cap, shared_on ? t_real : 0,
-                               at<int>(workspace, lo.gu_list), L->ffn / 64 / bdiv, L->shared_ffn / 64 / bdiv,
-                               at<int>(workspace, lo.dn_list), H / kTileRows / bdiv, kBNTc, st)))
+    if ((rc = launch_seg_lists(at<int>(workspace, lo.seg), El, El, sl.r_cap, 0, at<int>(workspace, lo.gu_list),
+                               L->ffn / 64 / bdiv, L->shared_ffn / 64 / bdiv, at<int>(workspace, lo.dn_list),
+                               H / kTileRows / bdiv, kBNTc, st)))
         return rc;
     prof_end(kStageDispatch, st);
     prof_begin(kStageGather, st);
     if ((rc = launch_ep_scatter_rows(a, xb, at<int>(workspace, lo.pair), ids, offsets, at<int>(workspace, lo.send_base), P,
-                                     shared_on ? t_real : 0, sm_count_api(), st)))
+                                     0, sm_count_api(), st)))
         return rc;
     if ((rc = launch_ep_wait(a, 1, st))) return rc;
     prof_end(kStageGather, st);
-    if (T > 0 && cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-        return cuda_status(cudaGetLastError(), "out = res");
     uint8_t* mine = a.sym[g->rank];
     TcLaunch gu{};
     gu.max_items = lo.max_gu;
@@ -1083,6 +1177,8 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     prof_end(kStageDown, st);
     prof_begin(kStageCombine, st);
     if ((rc = launch_ep_wait(a, 2, st))) return rc;
+    if (shared_on && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "join the shared expert");
     rc = launch_combine_bf16(out, reinterpret_cast<const uint16_t*>(mine + sl.y), at<int>(workspace, lo.pos), ids, wts, T,
                              t_real, k, H, st);
     prof_end(kStageCombine, st);

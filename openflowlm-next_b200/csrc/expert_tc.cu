@@ -644,7 +644,8 @@ int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
     a.meta = L.meta;
     for (int i = 0; i < kMaxRanks; ++i) a.yret[i] = L.yret[i];
     a.err = L.err;
-    const int sms = sm_count();
+    int sms = sm_count();
+    if (L.max_ctas > 0 && L.max_ctas < sms) sms = L.max_ctas;
     const int sm_single = TcSmem<false>::total, sm_pair = TcSmem<true>::total;
     cudaError_t e;
     if (L.cta_pair) {

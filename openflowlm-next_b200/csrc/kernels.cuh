@@ -53,6 +53,7 @@ struct TcLaunch {
     uint16_t* yret[kMaxRanks];
     int* err;
     bool cta_pair;                   // CTA-pair kernel (M = 256 MMAs); the list entries are band pairs
+    int max_ctas;                    // grid cap (0: one CTA per SM); leaves SMs to concurrent work
 };
 int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st);
 struct GemvLaunch {
