@@ -418,7 +418,9 @@ def run_flowmoe(args):
         dist.all_reduce(mine)
         pairs = int(mine.item())
     gu_ms = stages["gate_up"] / args.steps
-    gu_tflops = gate_up_flops(cfg, pairs, T) / (gu_ms * 1e-3) / 1e12
+    # the gate_up stage events bracket the routed items only: the shared expert runs on a side stream
+    # beside the dispatch (one GPU) or the row exchange (expert parallel)
+    gu_tflops = gate_up_flops(cfg, pairs, 0) / (gu_ms * 1e-3) / 1e12
 
     # end to end through the public API with host buffers
     xh = x.cpu().pin_memory()
@@ -457,7 +459,7 @@ def run_flowmoe(args):
                               if world > 1 else {}),
                            "l2": "expert weights 503 MB > 126 MB L2 streamed every step",
                            **({"experts_per_gpu": cfg.local, "recv_rows_rank0": pairs} if world > 1 else {})},
-                "roofline": {"bound": "tensor", "kernel": "expert_gemm<gate_up>",
+                "roofline": {"bound": "tensor", "kernel": "expert_tc<gate_up> (routed items)",
                              "achieved": round(gu_tflops, 2), "peak": tfl_sus, "unit": "TFLOP/s",
                              "frac": round(gu_tflops / tfl_sus, 4), "traffic": traffic,
                              "peak_kind": f"{peak_kind} bf16 sustained"},

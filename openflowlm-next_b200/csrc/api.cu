@@ -93,9 +93,36 @@ constexpr int kChunk = 2048;   // dispatch chunk (dispatch.cu)
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// A second stream and fork / join events per device (the shared expert runs beside the dispatch and
+// the row exchange). Created on the first call, outside any stream capture.
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+static SideStream* side_stream() {
+    static SideStream per_dev[64];
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    SideStream& x = per_dev[dev];
+    if (!x.s) {
+        if (cudaStreamCreateWithFlags(&x.s, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&x.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming) != cudaSuccess) {
+            x.s = nullptr;
+            return nullptr;
+        }
+    }
+    return &x;
+}
+
+
+
 struct Layout {
     size_t err, xb, logits, counts, offsets, blk_hist, pos, pair, gu_list, dn_list, xperm, hperm, yperm, sgate, idx, w;
-    size_t part, done;
+    size_t part, done, gu_list_sh, dn_list_sh;
     size_t total;
     int nblk, max_gu, max_dn, P, rows, fmax, max_slots, part_cols;
 };
@@ -161,6 +188,8 @@ static Layout make_layout(const fm_layer* L, int T) {
     o.sgate = take((size_t)T * 4);
     o.idx = take((size_t)o.P * 4);
     o.w = take((size_t)o.P * 4);
+    o.gu_list_sh = take((size_t)(4 + 4 * rt_shared * (L->shared_ffn / 64)) * 4);
+    o.dn_list_sh = take((size_t)(4 + 4 * rt_shared * (H / kTileRows)) * 4);
     if (decode) {
         o.part = take((size_t)4 * o.rows * o.part_cols * 4);
         o.done = take((size_t)2 * o.max_slots * 4);
@@ -281,6 +310,76 @@ static int run_block_gemv(const fm_layer* L, const uint16_t* xb, const float* re
     return rc;
 }
 
+static int sm_count_api() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+// The shared expert as its own pair of tcgen05 launches on the side stream (forked from st at this
+// point): gate_up over x rows [0, t_real) straight from xb, h into h_rows, down adding
+// sgate * y into out. Leaves `spare_sms` SMs to the work that runs beside it. Records side->join.
+static int launch_shared_side(const fm_layer* L, const uint16_t* xb, const float* sgate, int T, int t_real, float* out,
+                              int* gu_list, int* dn_list, uint16_t* h_rows, int h_ld, int bdiv, int spare_sms, int* err,
+                              SideStream* side, cudaStream_t st) {
+    const int H = L->hidden, El = L->e_local;
+    cudaStream_t s2 = side->s;
+    if (cudaEventRecord(side->fork, st) != cudaSuccess || cudaStreamWaitEvent(s2, side->fork, 0) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "fork the shared expert");
+    int rc = launch_seg_lists(nullptr, 0, El, 0, t_real, gu_list, L->ffn / 64 / bdiv, L->shared_ffn / 64 / bdiv, dn_list,
+                              H / kTileRows / bdiv, kBNTc, s2);
+    if (rc) return rc;
+    const int rt = (T + kBNTc - 1) / kBNTc;
+    TcLaunch g{};
+    g.max_items = rt * (L->shared_ffn / 64);
+    g.max_ctas = spare_sms > 0 ? sm_count_api() - spare_sms : 0;
+    g.list = gu_list;
+    g.act = xb;
+    g.act_rows = T;
+    g.act_cols = H;
+    g.act_ld = H;
+    g.w_routed = L->gate_up;
+    g.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
+    g.w_shared = L->shared_gate_up;
+    g.shared_group = El;
+    g.K_routed = H;
+    g.K_shared = H;
+    g.h_out = h_rows;
+    g.h_ld = h_ld;
+    g.err = err;
+    g.cta_pair = bdiv == 2;
+    if ((rc = launch_expert_tc(true, g, s2))) return rc;
+    TcLaunch d{};
+    d.max_items = rt * (H / kTileRows);
+    d.max_ctas = g.max_ctas;
+    d.list = dn_list;
+    d.act = h_rows;
+    d.act_rows = T;
+    d.act_cols = h_ld;
+    d.act_ld = h_ld;
+    d.w_routed = L->down;
+    d.w_routed_stride = (size_t)H * L->ffn / 32 * 20;
+    d.w_shared = L->shared_down;
+    d.shared_group = El;
+    d.K_routed = L->ffn;
+    d.K_shared = L->shared_ffn;
+    d.out = out;
+    d.H = H;
+    d.k = L->top_k;
+    d.shared_base = 0;
+    d.sgate = sgate;
+    d.err = err;
+    d.cta_pair = bdiv == 2;
+    if ((rc = launch_expert_tc(false, d, s2))) return rc;
+    if (cudaEventRecord(side->join, s2) != cudaSuccess) return cuda_status(cudaGetLastError(), "join event");
+    return FM_OK;
+}
+
 static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, const int32_t* idx, const float* w,
                      const float* sgate, int T, int t_real, float* out, void* ws, const Layout& lo, cudaStream_t st) {
     const int H = L->hidden, k = L->top_k, E = L->n_experts;
@@ -295,11 +394,28 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     const int nblk = (P + kChunk - 1) / kChunk;
     // rows of the sorted space: routed [0, P), shared [P_cap, P_cap + t_real) with P_cap = T * k
     const int Pcap = lo.P;
+    // tcgen05 path: the shared expert reads x directly and runs on a side stream while the routed rows
+    // are dispatched and gathered (those kernels leave most SMs idle); out = res must precede it
+    SideStream* side = (tc && shared_on) ? side_stream() : nullptr;
+    if (tc && shared_on && !side) {
+        set_error("could not create the side stream");
+        return FM_ECUDA;
+    }
+    int rc = FM_OK;
+    if (tc) {
+        if (cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            return cuda_status(cudaGetLastError(), "out = res");
+        if (side && (rc = launch_shared_side(L, xb, sgate, T, t_real, out, at<int>(ws, lo.gu_list_sh),
+                                             at<int>(ws, lo.dn_list_sh), at<uint16_t>(ws, lo.hperm) + (size_t)Pcap * lo.fmax,
+                                             lo.fmax, bdiv, 0, at<int>(ws, lo.err) + 1, side, st)))
+            return rc;
+    }
+    const bool shared_in_lists = shared_on && !side;
     prof_begin(kStageDispatch, st);
-    int rc = launch_dispatch(idx, P, L->e_begin, L->e_local, E, Pcap, shared_on ? t_real : 0, at<int>(ws, lo.blk_hist), nblk,
-                             at<int>(ws, lo.counts), at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
-                             at<int>(ws, lo.gu_list), L->ffn / 64 / bdiv, shared_on ? L->shared_ffn / 64 / bdiv : 0,
-                             at<int>(ws, lo.dn_list), H / kTileRows / bdiv, bn, at<int>(ws, lo.err), st);
+    rc = launch_dispatch(idx, P, L->e_begin, L->e_local, E, Pcap, shared_in_lists ? t_real : 0, at<int>(ws, lo.blk_hist),
+                         nblk, at<int>(ws, lo.counts), at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
+                         at<int>(ws, lo.gu_list), L->ffn / 64 / bdiv, shared_in_lists ? L->shared_ffn / 64 / bdiv : 0,
+                         at<int>(ws, lo.dn_list), H / kTileRows / bdiv, bn, at<int>(ws, lo.err), st);
     if (rc) return rc;
     prof_end(kStageDispatch, st);
     prof_begin(kStageGather, st);
@@ -308,9 +424,7 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
         return rc;
     prof_end(kStageGather, st);
     if (tc) {
-        // out = res first (rows past t_real stay res); the down GEMM then adds w * y into it
-        if (cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-            return cuda_status(cudaGetLastError(), "out = res");
+        // out = res was set above (rows past t_real stay res); the down GEMM adds w * y into it
         TcLaunch g{};
         g.max_items = lo.max_gu;
         g.list = at<int>(ws, lo.gu_list);
@@ -356,6 +470,8 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
         prof_begin(kStageDown, st);
         if ((rc = launch_expert_tc(false, d, st))) return rc;
         prof_end(kStageDown, st);
+        if (side && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
+            return cuda_status(cudaGetLastError(), "join the shared expert");
         return FM_OK;
     }
     GroupedArgs a{};
@@ -909,31 +1025,6 @@ static EpPeerLayout ep_peer_layout(const fm_layer* L, const fm_ep_group* g, int 
     return o;
 }
 
-// A second stream and fork / join events per device (the shared expert of the expert-parallel layer
-// runs beside the row exchange). Created on the first call, outside any stream capture.
-struct SideStream {
-    cudaStream_t s = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
-};
-
-static SideStream* side_stream() {
-    static SideStream per_dev[64];
-    static std::mutex mu;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    std::lock_guard<std::mutex> lock(mu);
-    SideStream& x = per_dev[dev];
-    if (!x.s) {
-        if (cudaStreamCreateWithFlags(&x.s, cudaStreamNonBlocking) != cudaSuccess ||
-            cudaEventCreateWithFlags(&x.fork, cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming) != cudaSuccess) {
-            x.s = nullptr;
-            return nullptr;
-        }
-    }
-    return &x;
-}
-
 constexpr int kScatterSms = 20;   // SMs left to the row exchange while the shared expert runs
 
 static int ep_group_check(const fm_layer* L, const fm_ep_group* g, bool need_sym = true) {
@@ -960,16 +1051,6 @@ static int ep_group_check(const fm_layer* L, const fm_ep_group* g, bool need_sym
     return FM_OK;
 }
 
-static int sm_count_api() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
 
 }  // namespace fm
 
@@ -1063,58 +1144,11 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
         set_error("expert parallel: could not create the side stream");
         return FM_ECUDA;
     }
-    if (shared_on) {
-        cudaStream_t s2 = side->s;
-        if (cudaEventRecord(side->fork, st) != cudaSuccess || cudaStreamWaitEvent(s2, side->fork, 0) != cudaSuccess)
-            return cuda_status(cudaGetLastError(), "fork the shared expert");
-        if ((rc = launch_seg_lists(nullptr, 0, El, 0, t_real, at<int>(workspace, lo.gu_list_sh), L->ffn / 64 / bdiv,
-                                   L->shared_ffn / 64 / bdiv, at<int>(workspace, lo.dn_list_sh),
-                                   H / kTileRows / bdiv, kBNTc, s2)))
-            return rc;
-        uint16_t* hsh = at<uint16_t>(workspace, lo.hexp) + (size_t)sl.r_cap * lo.fmax;
-        TcLaunch sgu{};
-        sgu.max_items = lo.max_gu_sh;
-        sgu.max_ctas = sm_count_api() - kScatterSms;
-        sgu.list = at<int>(workspace, lo.gu_list_sh);
-        sgu.act = xb;
-        sgu.act_rows = T;
-        sgu.act_cols = H;
-        sgu.act_ld = H;
-        sgu.w_routed = L->gate_up;
-        sgu.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
-        sgu.w_shared = L->shared_gate_up;
-        sgu.shared_group = El;
-        sgu.K_routed = H;
-        sgu.K_shared = H;
-        sgu.h_out = hsh;
-        sgu.h_ld = lo.fmax;
-        sgu.err = a.err + 1;
-        sgu.cta_pair = bdiv == 2;
-        if ((rc = launch_expert_tc(true, sgu, s2))) return rc;
-        TcLaunch sdn{};
-        sdn.max_items = lo.max_dn_sh;
-        sdn.max_ctas = sm_count_api() - kScatterSms;
-        sdn.list = at<int>(workspace, lo.dn_list_sh);
-        sdn.act = hsh;
-        sdn.act_rows = T;
-        sdn.act_cols = lo.fmax;
-        sdn.act_ld = lo.fmax;
-        sdn.w_routed = L->down;
-        sdn.w_routed_stride = (size_t)H * L->ffn / 32 * 20;
-        sdn.w_shared = L->shared_down;
-        sdn.shared_group = El;
-        sdn.K_routed = L->ffn;
-        sdn.K_shared = L->shared_ffn;
-        sdn.out = out;
-        sdn.H = H;
-        sdn.k = k;
-        sdn.shared_base = 0;
-        sdn.sgate = sg;
-        sdn.err = a.err + 1;
-        sdn.cta_pair = bdiv == 2;
-        if ((rc = launch_expert_tc(false, sdn, s2))) return rc;
-        if (cudaEventRecord(side->join, s2) != cudaSuccess) return cuda_status(cudaGetLastError(), "join event");
-    }
+    if (shared_on && (rc = launch_shared_side(L, xb, sg, T, t_real, out, at<int>(workspace, lo.gu_list_sh),
+                                              at<int>(workspace, lo.dn_list_sh),
+                                              at<uint16_t>(workspace, lo.hexp) + (size_t)sl.r_cap * lo.fmax, lo.fmax,
+                                              bdiv, kScatterSms, a.err + 1, side, st)))
+        return rc;
     if ((rc = launch_ep_post_counts(a, counts, st))) return rc;
     if ((rc = launch_ep_plan_peer(a, at<int>(workspace, lo.send_base), at<int>(workspace, lo.seg), st))) return rc;
     if ((rc = launch_seg_lists(at<int>(workspace, lo.seg), El, El, sl.r_cap, 0, at<int>(workspace, lo.gu_list),
