@@ -188,9 +188,10 @@ def cpu_baseline(layer_blocks, cfg, x, res, budget_s=20.0, threads=None):
 
 
 # ------------------------------------------------------------------ sweep (configs 2 and 3)
-def graph_time(fn, reps=30):
-    """Capture fn in a CUDA graph and replay it: ms per replay of the plain graph, and the stage
-    durations from a second capture with the stage events inside it (its last replay)."""
+def graph_time(fn, reps=30, calls=1):
+    """Capture fn in a CUDA graph and replay it: ms per layer call (fn makes `calls` of them) of the
+    plain graph, and the stage durations per call from a second capture with the stage events inside it
+    (its last replay)."""
     from flowmoe import _lib
     for _ in range(3):
         fn()
@@ -207,7 +208,7 @@ def graph_time(fn, reps=30):
         g.replay()
     b.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / reps
+    ms = a.elapsed_time(b) / reps / calls
     gp = torch.cuda.CUDAGraph()
     _lib.profile(True)
     with torch.cuda.graph(gp):
@@ -218,7 +219,7 @@ def graph_time(fn, reps=30):
     stages = _lib.profile_read()
     _lib.profile(False)
     del g, gp
-    return ms, {k: round(v, 4) for k, v in stages.items() if v}
+    return ms, {k: round(v / calls, 4) for k, v in stages.items() if v}
 
 
 def sweep(hbm, tfl_burst):
@@ -229,17 +230,25 @@ def sweep(hbm, tfl_burst):
     layer = synth_layer(cfg, seed=0)
     expert_bytes = 3 * cfg.hidden * cfg.ffn * 5 // 8
     gu_bytes = 2 * cfg.hidden * cfg.ffn * 5 // 8
+    # Each replay runs R layer calls on R different token batches, so the experts they touch together
+    # (most of the layer's 377 MB) exceed the 126 MB L2 and every call streams its experts from HBM.
+    R = 16
     for T in (1, 4, 8, 16, 32):
-        x, res = synth_tokens(T, cfg.hidden, seed=T)
-        o = torch.empty_like(res)
-        idx = torch.empty(T, cfg.top_k, dtype=torch.int32, device="cuda")
-        w = torch.empty(T, cfg.top_k, device="cuda")
-        ms, st = graph_time(lambda: layer.forward(x, res, out=o, idx=idx, w=w))
-        U = int(torch.unique(idx).numel())
+        batches = [synth_tokens(T, cfg.hidden, seed=100 * T + r) for r in range(R)]
+        outs = [torch.empty_like(res) for _, res in batches]
+        idxs = [torch.empty(T, cfg.top_k, dtype=torch.int32, device="cuda") for _ in range(R)]
+        ws = [torch.empty(T, cfg.top_k, device="cuda") for _ in range(R)]
+
+        def calls():
+            for (x, res), o, idx, w in zip(batches, outs, idxs, ws):
+                layer.forward(x, res, out=o, idx=idx, w=w)
+
+        ms, st = graph_time(calls, calls=R)
+        U = sum(int(torch.unique(i).numel()) for i in idxs) / R
         nbytes = U * expert_bytes + (cfg.n_experts + 1) * cfg.hidden * 2 + T * cfg.hidden * (2 + 4 + 4)
         gbs = nbytes / (ms * 1e-3) / 1e9
         gu = U * gu_bytes / (st["gate_up"] * 1e-3) / 1e9 if st.get("gate_up") else None
-        out["decode"].append({"T": T, "experts_touched": U, "ms": round(ms, 4), "tokens_per_s": round(T / ms * 1e3, 1),
+        out["decode"].append({"T": T, "experts_touched": round(U, 2), "batches_per_replay": R, "ms": round(ms, 4), "tokens_per_s": round(T / ms * 1e3, 1),
                               "GB_s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4), "stages_ms": st,
                               "gemv_gate_up_GB_s": round(gu, 1) if gu else None,
                               "gemv_gate_up_hbm_frac": round(gu / hbm, 4) if gu else None})
@@ -477,11 +486,11 @@ def run_flowmoe(args):
 
 def profile_case(name: str, calls: int = 6) -> int:
     """A few plain layer calls for an ncu capture (no timing, no JSON): "decode" = C30 T=32 (GEMV path),
-    "prefill" = the headline C36 T=8192 layer."""
+    "decode1" = C30 T=1, "prefill" = the headline C36 T=8192 layer."""
     import flowmoe
     from flowmoe.synth import C30, C36, synth_layer, synth_tokens
-    cfg = flowmoe.MoEConfig(**(C30 if name == "decode" else C36))
-    T = 32 if name == "decode" else T_HEADLINE
+    cfg = flowmoe.MoEConfig(**(C36 if name == "prefill" else C30))
+    T = {"decode": 32, "decode1": 1}.get(name, T_HEADLINE)
     layer = synth_layer(cfg, seed=0)
     x, res = synth_tokens(T, cfg.hidden, seed=T)
     out = torch.empty_like(res)
@@ -503,7 +512,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="N > 1: the expert-parallel exchange (peer-memory stores, or NCCL all-to-all)")
-    ap.add_argument("--profile-case", choices=["decode", "prefill"], default=None,
+    ap.add_argument("--profile-case", choices=["decode", "decode1", "prefill"], default=None,
                     help="run a few plain layer calls for an ncu capture and exit")
     args = ap.parse_args()
     if args.profile_case:

@@ -124,7 +124,7 @@ struct Layout {
     size_t err, xb, logits, counts, offsets, blk_hist, pos, pair, gu_list, dn_list, xperm, hperm, yperm, sgate, idx, w;
     size_t part, done, gu_list_sh, dn_list_sh;
     size_t total;
-    int nblk, max_gu, max_dn, P, rows, fmax, max_slots, part_cols;
+    int nblk, max_gu, max_dn, P, rows, fmax, max_slots, part_cols, kc_cap;
 };
 
 static int validate(const fm_layer* L, int T) {
@@ -166,8 +166,9 @@ static Layout make_layout(const fm_layer* L, int T) {
         const int tt = o.P / kGemvRowsApi + L->e_local + (T + kGemvRowsApi - 1) / kGemvRowsApi;
         const int bands = (L->ffn > L->shared_ffn ? L->ffn : L->shared_ffn) / 64;
         o.max_slots = tt * (bands > H / kTileRows ? bands : H / kTileRows);
-        if (4 * o.max_slots > o.max_gu) o.max_gu = 4 * o.max_slots;
-        if (4 * o.max_slots > o.max_dn) o.max_dn = 4 * o.max_slots;
+        o.kc_cap = gemv_chunk_cap(T);
+        if (o.kc_cap * o.max_slots > o.max_gu) o.max_gu = o.kc_cap * o.max_slots;
+        if (o.kc_cap * o.max_slots > o.max_dn) o.max_dn = o.kc_cap * o.max_slots;
         o.part_cols = 2 * o.fmax > H ? 2 * o.fmax : H;
     }
     size_t off = 0;
@@ -191,8 +192,8 @@ static Layout make_layout(const fm_layer* L, int T) {
     o.gu_list_sh = take((size_t)(4 + 4 * rt_shared * (L->shared_ffn / 64)) * 4);
     o.dn_list_sh = take((size_t)(4 + 4 * rt_shared * (H / kTileRows)) * 4);
     if (decode) {
-        o.part = take((size_t)4 * o.rows * o.part_cols * 4);
-        o.done = take((size_t)2 * o.max_slots * 4);
+        o.part = take((size_t)o.kc_cap * o.rows * o.part_cols * 4);
+        o.done = take((size_t)kGemvWarps * o.max_slots * 4);
     }
     o.total = off;
     return o;
@@ -251,15 +252,13 @@ static int run_block_gemv(const fm_layer* L, const uint16_t* xb, const float* re
     const int H = L->hidden, k = L->top_k;
     const bool shared_on = L->shared_ffn > 0 && sgate && L->shared_gate_up && L->shared_down && t_real > 0;
     const int P = t_real * k, Pcap = lo.P;
-    if (cudaMemsetAsync(at<int>(ws, lo.err), 0, 16, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
-    if (cudaMemsetAsync(at<int>(ws, lo.done), 0, (size_t)2 * lo.max_slots * 4, st) != cudaSuccess)
-        return cuda_status(cudaGetLastError(), "memset");
-    prof_begin(kStageDispatch, st);
+    prof_begin(kStageDispatch, st);   // the dispatch kernel clears the status words
     int rc = launch_dispatch_small(idx, P, L->e_begin, L->e_local, Pcap, shared_on ? t_real : 0, at<int>(ws, lo.counts),
                                    at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
                                    at<int>(ws, lo.gu_list), L->ffn / 64, shared_on ? L->shared_ffn / 64 : 0,
                                    H / kTileK, at<int>(ws, lo.dn_list), H / kTileRows, L->ffn / kTileK,
-                                   shared_on ? L->shared_ffn / kTileK : L->ffn / kTileK, at<int>(ws, lo.err), st);
+                                   shared_on ? L->shared_ffn / kTileK : L->ffn / kTileK, lo.kc_cap,
+                                   at<int>(ws, lo.done), at<int>(ws, lo.err), st);
     if (rc) return rc;
     prof_end(kStageDispatch, st);
     GemvLaunch g{};
@@ -278,11 +277,16 @@ static int run_block_gemv(const fm_layer* L, const uint16_t* xb, const float* re
     g.shared_base = Pcap;
     g.part = at<float>(ws, lo.part);
     g.part_rows = lo.rows;
+    g.part_ld = lo.part_cols;
     g.done = at<int>(ws, lo.done);
     g.h_out = at<uint16_t>(ws, lo.hperm);
     g.h_ld = lo.fmax;
     g.F_routed = L->ffn;
     g.F_shared = L->shared_ffn;
+    g.dn_list = at<int>(ws, lo.dn_list);
+    g.y_out = at<float>(ws, lo.yperm);
+    g.y_rows = lo.rows;
+    g.H = H;
     g.err = at<int>(ws, lo.err) + 1;
     prof_begin(kStageGateUp, st);
     if ((rc = launch_gemv(true, g, st))) return rc;
@@ -297,7 +301,7 @@ static int run_block_gemv(const fm_layer* L, const uint16_t* xb, const float* re
     d.K_shared = L->shared_ffn;
     d.act = at<uint16_t>(ws, lo.hperm);
     d.act_ld = lo.fmax;
-    d.done = at<int>(ws, lo.done) + lo.max_slots;
+    d.done = nullptr;   // K chunks of the down GEMM add into y
     d.y_out = at<float>(ws, lo.yperm);
     d.H = H;
     prof_begin(kStageDown, st);

@@ -1,18 +1,23 @@
-// Decode-size path (T <= 32 tokens): small-T router logits, single-CTA dispatch that also builds the
-// GEMV work lists, and the bandwidth-bound grouped Q4_1 GEMV.
+// Decode-size path (T <= 32 tokens): single-CTA dispatch that also builds the GEMV work lists, and the
+// bandwidth-bound grouped Q4_1 GEMV.
 //
-// GEMV: each work item is (group, 128-row band, up to 8 sorted rows, K chunk). One CTA per SM: a
-// producer warp keeps 24 weight tiles (120 KB) of bulk copies in flight and double-buffers each item's
-// bf16 activation rows; 16 consumer warps in two groups take alternate slab pairs, each warp 32 rows
-// of the band and one of the slab's two 32-value blocks. The tensor core multiplies the
-// raw codes, never dequantised weights: the A operand is 128 + q as bf16 (exact; one byte permute per
-// two codes, one 32-bit load per fragment thanks to the tile's fragment byte order), the B operand the
-// bf16 activations, so per 32-value block C = sum (128 + q) x exactly in f32, and the block's exact fp16
-// scale d and min m are applied after the MMA:
-//   y += d * C + (m - 128 d) * X,   X = sum of the block's activations,
-// i.e. the oracle's exact dequantisation (q4_1_pack.py:104-109) with only f32 roundings. K is split
-// into up to 4 chunks when fewer than half the SMs would have work; the last CTA to finish a (group,
-// band, rows) item reduces the chunks in order.
+// GEMV: a work item is (group, 128-row band, up to 8 sorted rows, K chunk). Each SM runs four
+// independent CTAs of one producer warp + four consumer warps. The producer streams the item's slabs
+// into a ring of 8 stages, each one 5120-byte weight tile (one bulk copy) plus the item's activation
+// rows for the same 64 K (one 128-byte bulk copy per row). Consumer warp j owns tile rows 16j..16j+15
+// and 64+16j..64+16j+15 over the whole K chunk: for gate/up these are the gate and up rows of the same
+// 16 features, so SwiGLU happens in registers and no warp waits for another.
+// The tensor core multiplies the raw codes, never dequantised weights: the A operand is 128 + q as bf16
+// (exact; one byte permute per two codes, one 32-bit load per fragment thanks to the tile's fragment
+// byte order), the B operand the bf16 activations, so per 32-value block C = sum (128 + q) x exactly in
+// f32, and the block's exact fp16 scale d and min m are applied after the MMA:
+//   y += d * C + (m - 128 d) * X,   X = sum of the block's activations (an all-ones MMA),
+// i.e. the oracle's exact dequantisation (q4_1_pack.py:104-109) with only f32 roundings. With few tokens
+// per item the MMA's 8 columns hold several blocks (column = token x block phase), so the per-block
+// scale work is done once per 8 / tokens blocks instead of per block.
+// K is split into chunks only when there are fewer items than CTA slots. gate/up: the last warp to
+// finish a (slot, rows) reduces the chunks' partial sums in chunk order (deterministic), then applies
+// SwiGLU; down: chunks add into the y rows with red.add (the gate/up kernel clears them first).
 //   GATE_UP: tile rows 0-63 gate, 64-127 up of 64 features -> h = bf16(silu(g) * u) (moe_batch.h:181-202)
 //   DOWN:    y rows (f32) -> combine_kernel sums each token's experts in ascending order.
 #include "common.cuh"
@@ -65,24 +70,37 @@ __device__ int block_sum_1024(int v, int* sh) {
     return t;
 }
 
-// K split per item group: only when fewer than half the SMs would otherwise have work (a split costs a
-// round trip through the partial buffer and a completion counter).
-__device__ int choose_chunks(int base_items, int slabs) {
-    int kc = base_items >= 74 ? 1 : base_items >= 37 ? 2 : 4;
-    while (kc > 1 && slabs % kc) kc >>= 1;
-    return kc;
+// K chunks per item: the smallest divisor of the slab counts (at least two slabs per chunk, at most
+// kc_cap chunks) that gives `target` items (one per GEMV CTA slot), else the largest such divisor. Splits
+// are kept few: each costs a round trip of n x 128 partial sums through L2, a completion counter and
+// the ramp of another item, measured dearer than the load imbalance they remove.
+__device__ int choose_chunks(int base_items, int slabs, int slabs_other, int kc_cap, int target) {
+    int best = 1;
+    if (base_items >= target) return 1;
+    for (int kc = 2; kc <= kc_cap; ++kc) {
+        if (slabs % kc || slabs / kc < 2) continue;
+        if (slabs_other && (slabs_other % kc || slabs_other / kc < 2)) continue;
+        best = kc;
+        if (base_items * kc >= target) break;
+    }
+    return best;
 }
 
 __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
     const int32_t* __restrict__ idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
     int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ pos, int* __restrict__ pair,
     int* __restrict__ gu_list, int gu_bands, int gu_bands_shared, int gu_slabs, int* __restrict__ dn_list, int dn_bands,
-    int dn_slabs, int dn_slabs_shared, int* __restrict__ err) {
+    int dn_slabs, int dn_slabs_shared, int kc_cap, int target, int* __restrict__ done, int* __restrict__ err) {
     extern __shared__ int sm[];
     int* cnt = sm;                                  // [e_local]
     int* wcnt = cnt + e_local;                      // [32][e_local]
     int* scan_sh = wcnt + 32 * e_local;             // [32]
+    int* off_s = scan_sh + 32;                      // [e_local + 1] group row offsets
+    int* gu0 = off_s + e_local + 1;                 // [e_local + 2] first GEMV slot of each group (gate/up)
+    int* dn0 = gu0 + e_local + 2;                   // [e_local + 2] (down)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x < 4) err[threadIdx.x] = 0;   // this call's status words (bad ids, GEMV timeouts)
+    __syncthreads();
     for (int e = threadIdx.x; e < e_local; e += blockDim.x) {
         cnt[e] = 0;
         for (int w = 0; w < 32; ++w) wcnt[w * e_local + e] = 0;
@@ -138,11 +156,13 @@ __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
         if (threadIdx.x < e_local) {
             counts[threadIdx.x] = v;
             offsets[threadIdx.x] = ex;
+            off_s[threadIdx.x] = ex;
         }
         if (threadIdx.x == 0) {
             counts[e_local] = shared_rows;
             offsets[e_local] = scan_sh[31];
             offsets[e_local + 1] = shared_base;
+            off_s[e_local] = shared_base;
         }
         __syncthreads();
     }
@@ -153,34 +173,47 @@ __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
     } else if (p < P) {
         pos[p] = -1;
     }
-    // GEMV work lists: thread g emits group g's items (G <= 1024 groups)
+    // GEMV work lists. Group g (G <= 1024: the local experts, then the shared expert) has ceil(rows / 8)
+    // row chunks x its bands of slots, each slot kc K-chunk items; slots are numbered group-major. All
+    // threads write the items: item e -> slot e / kc, found by a binary search over the groups' first slots.
     const int G = e_local + (shared_rows > 0 ? 1 : 0);
     const int gi = threadIdx.x;
-    int c_g = 0, r0_g = 0, bands_g = 0, tt = 0;
+    int c_g = 0, bands_g = 0, tt = 0;
     if (gi < G) {
-        c_g = gi < e_local ? counts[gi] : shared_rows;
-        r0_g = gi < e_local ? offsets[gi] : shared_base;
+        c_g = gi < e_local ? cnt[gi] : shared_rows;
         bands_g = gi < e_local ? gu_bands : gu_bands_shared;
         tt = (c_g + kGemvRows - 1) / kGemvRows;
     }
     const int bgu = tt * bands_g, bdn = tt * dn_bands;
     const int tot_gu = block_sum_1024(bgu, scan_sh), tot_dn = block_sum_1024(bdn, scan_sh);
-    const int kc_gu = choose_chunks(tot_gu, gu_slabs);
-    int kc_dn = choose_chunks(tot_dn, dn_slabs);
-    if (shared_rows > 0) while (kc_dn > 1 && dn_slabs_shared % kc_dn) kc_dn >>= 1;
+    const int kc_gu = choose_chunks(tot_gu, gu_slabs, 0, kc_cap, target);
+    const int kc_dn = choose_chunks(tot_dn, dn_slabs, shared_rows > 0 ? dn_slabs_shared : 0, kc_cap, target);
     const int slot_gu = block_exclusive_scan_1024(bgu, scan_sh), slot_dn = block_exclusive_scan_1024(bdn, scan_sh);
-    if (gi < G && c_g > 0) {
-        int ngu = slot_gu * kc_gu, ndn = slot_dn * kc_dn, sgu = slot_gu, sdn = slot_dn;
-        for (int r = 0; r < c_g; r += kGemvRows) {
-            const int n = min(kGemvRows, c_g - r);
-            for (int b = 0; b < bands_g; ++b, ++sgu)
-                for (int kc = 0; kc < kc_gu; ++kc, ++ngu)
-                    reinterpret_cast<int4*>(gu_list + 4)[ngu] = make_int4(gi | (b << 16), r0_g + r, n | (kc << 16), sgu);
-            for (int b = 0; b < dn_bands; ++b, ++sdn)
-                for (int kc = 0; kc < kc_dn; ++kc, ++ndn)
-                    reinterpret_cast<int4*>(dn_list + 4)[ndn] = make_int4(gi | (b << 16), r0_g + r, n | (kc << 16), sdn);
-        }
+    if (gi <= G) {
+        gu0[gi] = gi < G ? slot_gu : tot_gu;
+        dn0[gi] = gi < G ? slot_dn : tot_dn;
     }
+    // the GEMV's per-(item slot, warp) completion counters start at zero
+    for (int i = threadIdx.x; i < tot_gu * kGemvWarps; i += blockDim.x) done[i] = 0;
+    __syncthreads();
+    auto emit = [&](int* list, const int* first, int total, int kc, int bands_routed, int bands_shared) {
+        for (int e = threadIdx.x; e < total * kc; e += blockDim.x) {
+            const int slot = e / kc, q = e - slot * kc;
+            int lo = 0, hi = G - 1;   // last group whose first slot <= slot
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (first[mid] <= slot) lo = mid; else hi = mid - 1;
+            }
+            const int grp = lo, local = slot - first[grp];
+            const int bands = grp < e_local ? bands_routed : bands_shared;
+            const int r = local / bands, b = local - r * bands;
+            const int rows = grp < e_local ? cnt[grp] : shared_rows;
+            const int n = min(kGemvRows, rows - r * kGemvRows);
+            reinterpret_cast<int4*>(list + 4)[e] = make_int4(grp | (b << 16), off_s[grp] + r * kGemvRows, n | (q << 16), slot);
+        }
+    };
+    emit(gu_list, gu0, tot_gu, kc_gu, gu_bands, gu_bands_shared);
+    emit(dn_list, dn0, tot_dn, kc_dn, dn_bands, dn_bands);
     if (threadIdx.x == 0) {
         gu_list[0] = tot_gu * kc_gu;
         gu_list[1] = kc_gu;
@@ -188,6 +221,7 @@ __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
         dn_list[1] = kc_dn;
     }
 }
+
 
 // ------------------------------------------------------------------ grouped Q4_1 GEMV
 struct GemvArgs {
@@ -204,34 +238,32 @@ struct GemvArgs {
     int k;
     int shared_base;
     // outputs
-    float* part;              // [4][rows][out_cols] f32 partial sums (K split)
-    int part_rows;
-    int* done;                // completion counters per item slot (zeroed per call)
+    float* part;              // [KC][part_rows][part_ld] f32 partial sums (K split)
+    int part_rows, part_ld;
+    int* done;                // completion counters per (item slot, consumer warp), zeroed by the dispatch
     uint16_t* h_out;          // GATE_UP final: bf16 h [rows, h_ld]
     int h_ld;
     int F_routed, F_shared;   // GATE_UP: features per matrix
-    float* y_out;             // DOWN final: f32 [rows, H]
+    float* y_out;             // DOWN final: f32 [rows, H]; with K chunks the chunks add into it (red.add)
     int H;
+    const int* dn_list;       // GATE_UP: the down list, whose K-chunk count says whether y starts at zero
+    int y_rows;               // rows of y_out
     int* err;                 // FM_ETIMEOUT when a bounded wait gives up
 };
 
-constexpr int GV_GWARPS = 8;                          // warps of a consumer group: 32 tile rows x one of 2 blocks
-constexpr int GV_GROUPS = 2;                          // groups take alternate slab pairs of an item
-constexpr int GV_CONSUMERS = GV_GWARPS * GV_GROUPS;   // consumer warps
-constexpr int GV_THREADS = 32 * (GV_CONSUMERS + 1);   // + one producer warp
-constexpr int GV_MAX_K = 2048;                        // activation K per item (one chunk)
-constexpr int GV_WSTAGES = 24;                        // weight tiles in flight per CTA (120 KB)
-constexpr int GV_XLD = GV_MAX_K + 8;                  // bf16 row of the staged activations (bank spread)
-constexpr int GV_ACT_BYTES = kGemvRows * GV_XLD * 2;  // bf16 rows of one item
-
+// CTA = one producer warp + GV_WARPS consumer warps working on one item at a time; GV_CTAS_PER_SM such
+// CTAs share an SM, each with its own ring of GV_STAGES slabs (a 5120-byte weight tile plus the item's
+// activation rows for the same 64 K).
+constexpr int GV_WARPS = kGemvWarps;
+constexpr int GV_THREADS = 32 * (GV_WARPS + 1);
+constexpr int GV_CTAS_PER_SM = 4;
+constexpr int GV_STAGES = 8;
+constexpr int GV_XROW = 144;                                  // staged activation row: 64 bf16 + 16 B (bank spread)
+constexpr int GV_STAGE = kTileBytes + kGemvRows * GV_XROW;    // 6272 B
 struct GvSmem {
-    static constexpr int w = 0;
-    static constexpr int act = w + GV_WSTAGES * kTileBytes;
-    static constexpr int tab = act + 2 * GV_ACT_BYTES;                 // [8 warps][2 slabs][32] (d, m - 128 d)
-    static constexpr int xch = tab + GV_CONSUMERS * 64 * 8;            // [128][8] f32 (block-1 partials, up rows)
-    static constexpr int xch2 = xch + 128 * kGemvRows * 4;             // [2][128][8] f32 (group-1 partials)
-    static constexpr int bars = xch2 + 2 * 128 * kGemvRows * 4;
-    static constexpr int total = bars + (2 * GV_WSTAGES + 4) * 8 + 128;
+    static constexpr int zero = GV_STAGES * GV_STAGE;         // 64 zero bytes (B operand of off-phase columns)
+    static constexpr int bars = zero + 64;
+    static constexpr int total = bars + 2 * GV_STAGES * 8 + 128;   // + alignment slack
 };
 
 __device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
@@ -241,72 +273,156 @@ __device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// One 32-value block (blk) of NS consecutive slabs (their tiles in tiles[]) for the warp's 32 rows
-// (two m16 tiles) and 8 token columns: acc[tile] (C fragments of m16n8) += the exact Q4_1 products.
-// xs: staged activations [8][GV_XLD] from the chunk start; tab: this warp's (d, m - 128 d) per row and
-// slab. The block sums X come from the tensor core too: an MMA with an all-ones A operand, shared by
-// both row tiles. The NS slabs are independent chains, interleaved by the compiler.
-template <int NS>
-__device__ __forceinline__ void gv_blocks(const uint8_t* const* tiles, const uint16_t* xs, float2* tab, int s0, int blk,
-                                          int rg, int lane, float (*acc)[4]) {
-    const int g = lane >> 2, c = lane & 3;
-#pragma unroll
-    for (int j = 0; j < NS; ++j) {   // lane r converts the scale pair of row 32 rg + r of this block
-        const uint32_t sc = *reinterpret_cast<const uint32_t*>(tiles[j] + kTileNibBytes + (rg * 32 + lane) * 8 + blk * 4);
-        const float d = __half2float(__ushort_as_half((unsigned short)(sc & 0xFFFF)));
-        const float m = __half2float(__ushort_as_half((unsigned short)(sc >> 16)));
-        tab[j * 32 + lane] = make_float2(d, fmaf(-128.f, d, m));
-    }
-    uint32_t u[NS][4];   // rows g, g+8, g+16, g+24 of the warp's 32
-#pragma unroll
-    for (int j = 0; j < NS; ++j)
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-            u[j][r] = *reinterpret_cast<const uint32_t*>(tiles[j] + (rg * 32 + g + 8 * r) * 32 + blk * 16 + c * 4);
-    float cb[NS][2][4] = {}, cx[NS][4] = {};
+// Shared-memory loads by 32-bit shared address (no generic-to-shared conversion per access). Volatile
+// so they stay after the mbarrier waits that make the data visible.
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+// (d, m - 128 d) of row `row`, block `blk` of the tile at shared address w, in f32 (d and m are exact
+// fp16 values).
+__device__ __forceinline__ float2 gv_scale(uint32_t w, int row, int blk) {
+    const uint32_t sc = lds32(w + kTileNibBytes + row * 8 + blk * 4);
+    const float d = __half2float(__ushort_as_half((unsigned short)(sc & 0xFFFF)));
+    const float m = __half2float(__ushort_as_half((unsigned short)(sc >> 16)));
+    return make_float2(d, fmaf(-128.f, d, m));
+}
+
+// One 16-value K step (hi = 0: values 0-15 of the block, 1: values 16-31) of the warp's two m16 row
+// tiles: cb[mt] += (128 + q) x on the tensor core, cx += 1 x (the block sums of each column).
+// u[mt][h]: the lane's fragment word of tile row (16 j + g + 8 h + 64 mt): low nibbles are values
+// 2c, 2c+1, 2c+8, 2c+9 of the block, high nibbles the same + 16.
+__device__ __forceinline__ void gv_kstep(const uint32_t (&u)[2][2], int hi, uint32_t b0, uint32_t b1, float (&cb)[2][4],
+                                         float (&cx)[4]) {
     const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
 #pragma unroll
-    for (int hi = 0; hi < 2; ++hi) {
+    for (int mt = 0; mt < 2; ++mt) {
+        const uint32_t ta = (hi ? u[mt][0] >> 4 : u[mt][0]) & 0x0F0F0F0Fu;
+        const uint32_t tb = (hi ? u[mt][1] >> 4 : u[mt][1]) & 0x0F0F0F0Fu;
+        uint32_t af[4];
+        af[0] = __byte_perm(ta, 0x43434343u, 0x5140);   // bf16 128 + q of values 2c, 2c+1 (row g)
+        af[1] = __byte_perm(tb, 0x43434343u, 0x5140);   // row g + 8
+        af[2] = __byte_perm(ta, 0x43434343u, 0x5342);   // values 2c+8, 2c+9
+        af[3] = __byte_perm(tb, 0x43434343u, 0x5342);
+        mma_bf16(cb[mt], af, b0, b1);
+    }
+    mma_bf16(cx, ones, b0, b1);
+}
+
+// One item's K range for a consumer warp, TC = token columns (n <= TC <= 8). The 8 columns of the MMA
+// are (token t, block phase p) with t = col % TC, p = col / TC: a lane loads its B column's activations
+// only for blocks whose index within the group is p (else zeros), so one C fragment collects P = 8 / TC
+// consecutive blocks without mixing them, and the exact per-block scales are applied once per group of
+// P blocks: acc += d C + (m - 128 d) X. A group's stages are released after its scales are read.
+template <int TC>
+__device__ __forceinline__ bool gv_item(uint8_t* smem, uint64_t* full, uint64_t* empty, int& st, uint32_t& ph, int slabs,
+                                        int j, int lane, float (&acc)[2][4]) {
+    constexpr int P = 8 / TC;
+    constexpr int GS = P >= 2 ? P / 2 : 1;    // slabs per scale group
+    const int g = lane >> 2, c = lane & 3;
+    const int bt = g % TC, bp = g / TC;       // this lane's B column: token bt, block phase bp
+    const int r0 = 16 * j + g;
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t zero = sbase + GvSmem::zero + 4 * c;
+    for (int s0 = 0; s0 < slabs; s0 += GS) {
+        const int gs = min(GS, slabs - s0);
+        const int st0 = st;
+        float cb[2][4] = {}, cx[4] = {};
 #pragma unroll
-        for (int j = 0; j < NS; ++j) {
-            const uint16_t* xr = xs + g * GV_XLD + (s0 + j) * kTileK + blk * 32 + hi * 16 + 2 * c;
-            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xr), b1 = *reinterpret_cast<const uint32_t*>(xr + 8);
+        for (int q = 0; q < GS; ++q) {
+            if (q < gs) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[st], ph))) return false;
+                const uint32_t w = sbase + st * GV_STAGE;
+                const uint32_t wr = w + r0 * 32 + 4 * c;                       // row r0's fragment word
+                const uint32_t xr = w + kTileBytes + bt * GV_XROW + 4 * c;     // this lane's B column
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                const uint32_t ta = (u[j][2 * mt] >> (4 * hi)) & 0x0F0F0F0Fu, tb = (u[j][2 * mt + 1] >> (4 * hi)) & 0x0F0F0F0Fu;
-                uint32_t af[4];
-                af[0] = __byte_perm(ta, 0x4343u, 0x5140);   // 128 + q of values 2c, 2c+1
-                af[1] = __byte_perm(tb, 0x4343u, 0x5140);
-                af[2] = __byte_perm(ta, 0x4343u, 0x5342);   // values 2c+8, 2c+9
-                af[3] = __byte_perm(tb, 0x4343u, 0x5342);
-                mma_bf16(cb[j][mt], af, b0, b1);
+                for (int blk = 0; blk < 2; ++blk) {
+                    const bool on = P == 1 || bp == (2 * q + blk) % P;
+                    const uint32_t xb = on ? xr + blk * 64 : zero;
+                    uint32_t u[2][2];
+#pragma unroll
+                    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) u[mt][h] = lds32(wr + (64 * mt + 8 * h) * 32 + blk * 16);
+#pragma unroll
+                    for (int hi = 0; hi < 2; ++hi) {
+                        const uint32_t b0 = lds32(xb + hi * 32);
+                        const uint32_t b1 = lds32(xb + hi * 32 + 16);
+                        gv_kstep(u, hi, b0, b1, cb, cx);
+                    }
+                    if (P == 1) {   // every column is this block: apply its scales now
+#pragma unroll
+                        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const float2 sc = gv_scale(w, r0 + 64 * mt + 8 * h, blk);
+#pragma unroll
+                                for (int cc = 0; cc < 2; ++cc) {
+                                    acc[mt][2 * h + cc] = fmaf(sc.x, cb[mt][2 * h + cc], fmaf(sc.y, cx[cc], acc[mt][2 * h + cc]));
+                                    cb[mt][2 * h + cc] = 0.f;
+                                }
+                            }
+                        cx[0] = cx[1] = cx[2] = cx[3] = 0.f;
+                    }
+                }
+                if (P == 1) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[st]);
+                }
+                if (++st == GV_STAGES) { st = 0; ph ^= 1; }
             }
-            mma_bf16(cx[j], ones, b0, b1);
+        }
+        if (P > 1) {
+            // this lane's C columns 2c and 2c+1 hold block phases p0 and p1 of the group (the same
+            // phase unless TC == 1); a short last group lacks the phases past its slabs
+#pragma unroll
+            for (int cc = 0; cc < (TC == 1 ? 2 : 1); ++cc) {
+                const int pc = (2 * c + cc) / TC;
+                if (pc / 2 < gs) {
+                    int sidx = st0 + pc / 2;
+                    if (sidx >= GV_STAGES) sidx -= GV_STAGES;
+                    const uint32_t w = sbase + sidx * GV_STAGE;
+#pragma unroll
+                    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const float2 sc = gv_scale(w, r0 + 64 * mt + 8 * h, pc & 1);
+#pragma unroll
+                            for (int e = cc; e < 2; e += (TC == 1 ? 2 : 1))
+                                acc[mt][2 * h + e] = fmaf(sc.x, cb[mt][2 * h + e], fmaf(sc.y, cx[e], acc[mt][2 * h + e]));
+                        }
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                for (int q = 0; q < gs; ++q) mbar_arrive(&empty[(st0 + q) % GV_STAGES]);
         }
     }
-    __syncwarp();
-    // cx[0] / cx[1]: sum of the block's activations of tokens 2c / 2c+1 (every row alike)
-#pragma unroll
-    for (int j = 0; j < NS; ++j)
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-            const float2 sa = tab[j * 32 + 16 * mt + g], sb = tab[j * 32 + 16 * mt + g + 8];
-            acc[mt][0] = fmaf(sa.x, cb[j][mt][0], fmaf(sa.y, cx[j][0], acc[mt][0]));
-            acc[mt][1] = fmaf(sa.x, cb[j][mt][1], fmaf(sa.y, cx[j][1], acc[mt][1]));
-            acc[mt][2] = fmaf(sb.x, cb[j][mt][2], fmaf(sb.y, cx[j][0], acc[mt][2]));
-            acc[mt][3] = fmaf(sb.x, cb[j][mt][3], fmaf(sb.y, cx[j][1], acc[mt][3]));
-        }
-    __syncwarp();
+    return true;
 }
 
 struct GvItem {
-    int grp, bnd, row0, n, kc, slot, slabs, s0, kn;
+    int grp, bnd, row0, n, kc, slot, slabs, s0;
     bool sh;
     const uint8_t* wband;
 };
 
-__device__ __forceinline__ GvItem gv_decode(const GemvArgs& a, int i, int KC) {
-    const int4 it = reinterpret_cast<const int4*>(a.list + 4)[i];
+__device__ __forceinline__ int4 gv_entry(const GemvArgs& a, int i, int n_items) {
+    return i < n_items ? __ldg(reinterpret_cast<const int4*>(a.list + 4) + i) : make_int4(0, 0, 0, 0);
+}
+
+// Sorted row -> row of the activation matrix (GATE_UP: the token; DOWN: the sorted h row).
+template <bool GATE_UP>
+__device__ __forceinline__ int gv_src_row(const GemvArgs& a, int4 e, int lane) {
+    const int n = e.z & 0xFFFF, row = e.y + lane;
+    if (lane >= n) return 0;
+    if (!GATE_UP) return row;
+    return (e.x & 0xFFFF) == a.shared_group ? row - a.shared_base : __ldg(a.pair + row) / a.k;
+}
+
+__device__ __forceinline__ GvItem gv_decode(const GemvArgs& a, int4 it, int KC) {
     GvItem r;
     r.grp = it.x & 0xFFFF;
     r.bnd = it.x >> 16;
@@ -318,224 +434,184 @@ __device__ __forceinline__ GvItem gv_decode(const GemvArgs& a, int i, int KC) {
     const int K = r.sh ? a.K_shared : a.K_routed;
     r.slabs = K / kTileK / KC;
     r.s0 = r.kc * r.slabs;
-    r.kn = r.slabs * kTileK;
     r.wband = (r.sh ? a.w_shared : a.w_routed + (size_t)r.grp * a.w_routed_stride) + (size_t)r.bnd * (K / kTileK) * kTileBytes;
     return r;
 }
 
+// Items: (group, 128-row band, up to 8 sorted rows, K chunk). Consumer warp j owns tile rows
+// 16j..16j+15 (m16 tile 0) and 64+16j..64+16j+15 (m16 tile 1): for GATE_UP the gate and up rows of the
+// same 16 features, so SwiGLU needs no exchange between warps; every warp covers the item's whole K
+// chunk, so no reduction between warps either. The last warp to finish a (slot, warp) over the K chunks
+// reduces them in chunk order (deterministic).
 template <bool GATE_UP>
-__global__ void __launch_bounds__(GV_THREADS, 1) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(GV_THREADS, GV_CTAS_PER_SM) gemv_kernel(GemvArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + GvSmem::bars);
-    uint64_t* w_empty = w_full + GV_WSTAGES;
-    uint64_t* act_full = w_empty + GV_WSTAGES;
-    uint64_t* act_empty = act_full + 2;
-    float* xch = reinterpret_cast<float*>(smem + GvSmem::xch);
-    __shared__ int s_last, s_abort;   // s_abort: consumer warps only
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + GvSmem::bars);
+    uint64_t* empty = full + GV_STAGES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_items = a.list[0], KC = a.list[1];
     if (threadIdx.x == 0) {
-        for (int i = 0; i < GV_WSTAGES; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], GV_GWARPS); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&act_full[i], 1); mbar_init(&act_empty[i], GV_CONSUMERS); }
-        s_abort = 0;
+        for (int i = 0; i < GV_STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], GV_WARPS);
+        }
         mbar_fence_init();
     }
+    if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(smem + GvSmem::zero)[threadIdx.x] = 0u;
     __syncthreads();
+    const int n_items = a.list[0], KC = a.list[1];
+    if (GATE_UP && a.dn_list[1] > 1) {   // the down GEMM will add its K chunks into y: clear it first
+        float4* y4 = reinterpret_cast<float4*>(a.y_out);
+        const long long n4 = (long long)a.y_rows * a.H / 4;
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x)
+            y4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 
-    if (warp == GV_CONSUMERS) {
+    if (warp == GV_WARPS) {
         // ------------------------------------------------------------ producer warp
-        int ws = 0, ab = 0;
-        uint32_t wph = 0, aph = 0;
+        int st = 0;
+        uint32_t ph = 0;
         bool ok = true;
-        for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-            const GvItem it = gv_decode(a, i, KC);
-            // the item's activations: int16 rows by bulk copy, block scales and sums by the lanes
-            int got = 1;
-            if (lane == 0) got = mbar_wait(&act_empty[ab], aph ^ 1) ? 1 : 0;
-            if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }
-            uint16_t* xs = reinterpret_cast<uint16_t*>(smem + GvSmem::act + ab * GV_ACT_BYTES);
-            const int k0 = it.s0 * kTileK;
-            if (lane == 0) mbar_expect_tx(&act_full[ab], it.n * it.kn * 2);
-            __syncwarp();
-            if (lane < it.n) {   // one row per lane, all issued at once
-                const int r = lane;
-                const int src = GATE_UP ? (it.sh ? it.row0 + r - a.shared_base : a.pair[it.row0 + r] / a.k) : it.row0 + r;
-                bulk_load(xs + r * GV_XLD, a.act + (size_t)src * a.act_ld + k0, it.kn * 2, &act_full[ab]);
-            }
-            if (++ab == 2) { ab = 0; aph ^= 1; }
-            // the item's weight tiles
-            if (lane == 0) {
-                for (int s = 0; s < it.slabs; ++s) {
-                    if (!mbar_wait(&w_empty[ws], wph ^ 1)) { ok = false; break; }
-                    mbar_expect_tx(&w_full[ws], kTileBytes);
-                    bulk_load(smem + GvSmem::w + ws * kTileBytes, it.wband + (size_t)(it.s0 + s) * kTileBytes, kTileBytes,
-                              &w_full[ws]);
-                    if (++ws == GV_WSTAGES) { ws = 0; wph ^= 1; }
-                }
-            }
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-            ws = __shfl_sync(0xffffffffu, ws, 0);
-            wph = __shfl_sync(0xffffffffu, wph, 0);
-        }
-        if (!ok && lane == 0) atomicCAS(a.err, 0, FM_ETIMEOUT);
-        // drain: every issued copy lands before the CTA can exit
-        if (lane == 0) {
-            for (int i = 0; i < GV_WSTAGES; ++i) mbar_wait(&w_full[i], i < ws ? wph : wph ^ 1);
-            for (int i = 0; i < 2; ++i) mbar_wait(&act_full[i], i < ab ? aph : aph ^ 1);
-        }
-    } else {
-        // ------------------------------------------------------------ consumer warps
-        // Two groups of 8 warps take alternate slab pairs of each item (two independent chains of
-        // barrier waits, shared loads and MMAs per SM); group 1 hands its sums to group 0 at the end.
-        const int g = lane >> 2, c = lane & 3;
-        const int grp = warp >> 3;
-        const int rg = warp & 3, blk = (warp >> 2) & 1;    // rows 32 rg .. 32 rg + 31, block blk of each slab
-        float2* tab = reinterpret_cast<float2*>(smem + GvSmem::tab) + warp * 64;
-        float* xch2 = reinterpret_cast<float*>(smem + GvSmem::xch2);
-        int ab = 0;
-        uint32_t aph = 0;
-        int sc0 = 0;   // running slab index of the item's first slab (the producer's fill order)
-        for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
-            const GvItem it = gv_decode(a, i, KC);
-            bool ok = __all_sync(0xffffffffu, mbar_wait(&act_full[ab], aph));
-            const uint16_t* xs = reinterpret_cast<const uint16_t*>(smem + GvSmem::act + ab * GV_ACT_BYTES);
-            float acc2[2][4] = {};
-            for (int s = 2 * grp; s < it.slabs && ok; s += 2 * GV_GROUPS) {
-                const int ws = (sc0 + s) % GV_WSTAGES;
-                const uint32_t wph = ((sc0 + s) / GV_WSTAGES) & 1;
-                if (s + 1 == it.slabs) {   // an odd last slab
-                    if (!__all_sync(0xffffffffu, mbar_wait(&w_full[ws], wph))) { ok = false; break; }
-                    const uint8_t* t1[1] = {smem + GvSmem::w + ws * kTileBytes};
-                    gv_blocks<1>(t1, xs, tab, s, blk, rg, lane, acc2);
-                    if (lane == 0) mbar_arrive(&w_empty[ws]);
-                    break;
-                }
-                // two slabs at a time: independent chains
-                const int ws1 = (sc0 + s + 1) % GV_WSTAGES;
-                const uint32_t wph1 = ((sc0 + s + 1) / GV_WSTAGES) & 1;
-                if (!__all_sync(0xffffffffu, mbar_wait(&w_full[ws], wph) && mbar_wait(&w_full[ws1], wph1))) {
+        // list entries two items ahead and source rows one item ahead are in flight while an item's
+        // slabs are issued
+        const int G = gridDim.x;
+        int4 e0 = gv_entry(a, blockIdx.x, n_items), e1 = gv_entry(a, blockIdx.x + G, n_items);
+        int row0 = gv_src_row<GATE_UP>(a, e0, lane);
+        for (int i = blockIdx.x; i < n_items && ok; i += G) {
+            const int4 e2 = gv_entry(a, i + 2 * G, n_items);
+            const int row1 = gv_src_row<GATE_UP>(a, e1, lane);
+            const GvItem it = gv_decode(a, e0, KC);
+            // lane r < n: token row r of the item, from the chunk's first K
+            const uint16_t* src = a.act + (size_t)row0 * a.act_ld + (size_t)it.s0 * kTileK;
+            e0 = e1;
+            e1 = e2;
+            row0 = row1;
+            for (int s = 0; s < it.slabs; ++s) {
+                int got = 1;
+                if (lane == 0) got = mbar_wait(&empty[st], ph ^ 1) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, got, 0)) {
                     ok = false;
                     break;
                 }
-                const uint8_t* tiles[2] = {smem + GvSmem::w + ws * kTileBytes, smem + GvSmem::w + ws1 * kTileBytes};
-                gv_blocks<2>(tiles, xs, tab, s, blk, rg, lane, acc2);
+                uint8_t* stage = smem + st * GV_STAGE;
                 if (lane == 0) {
-                    mbar_arrive(&w_empty[ws]);
-                    mbar_arrive(&w_empty[ws1]);
+                    mbar_expect_tx(&full[st], kTileBytes + it.n * kTileK * 2);
+                    bulk_load(stage, it.wband + (size_t)(it.s0 + s) * kTileBytes, kTileBytes, &full[st]);
+                }
+                __syncwarp();
+                if (lane < it.n) bulk_load(stage + kTileBytes + lane * GV_XROW, src + s * kTileK, kTileK * 2, &full[st]);
+                if (++st == GV_STAGES) { st = 0; ph ^= 1; }
+            }
+        }
+        if (!ok && lane == 0) atomicCAS(a.err, 0, FM_ETIMEOUT);
+        // drain: every issued copy lands before the CTA can exit
+        if (lane == 0)
+            for (int i = 0; i < GV_STAGES; ++i) mbar_wait(&full[i], i < st ? ph : ph ^ 1);
+    } else {
+        // ------------------------------------------------------------ consumer warps
+        const int j = warp, g = lane >> 2, c = lane & 3;
+        int st = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        int4 e0 = gv_entry(a, blockIdx.x, n_items);
+        for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+            const int4 e1 = gv_entry(a, i + gridDim.x, n_items);   // the next item's entry, in flight
+            const GvItem it = gv_decode(a, e0, KC);
+            e0 = e1;
+            float acc[2][4] = {};
+            const int tc = it.n <= 1 ? 1 : it.n <= 2 ? 2 : it.n <= 4 ? 4 : 8;
+            switch (tc) {
+                case 1: ok = gv_item<1>(smem, full, empty, st, ph, it.slabs, j, lane, acc); break;
+                case 2: ok = gv_item<2>(smem, full, empty, st, ph, it.slabs, j, lane, acc); break;
+                case 4: ok = gv_item<4>(smem, full, empty, st, ph, it.slabs, j, lane, acc); break;
+                default: ok = gv_item<8>(smem, full, empty, st, ph, it.slabs, j, lane, acc); break;
+            }
+            if (!ok) break;
+            // per (row, token) sums: add the lane's columns of the same token (other block phases)
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                if (tc == 1) {
+                    acc[mt][0] += acc[mt][1];
+                    acc[mt][2] += acc[mt][3];
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    if (tc <= 2) acc[mt][e] += __shfl_xor_sync(0xffffffffu, acc[mt][e], 1);
+                    if (tc <= 4) acc[mt][e] += __shfl_xor_sync(0xffffffffu, acc[mt][e], 2);
                 }
             }
-            sc0 += it.slabs;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&act_empty[ab]);
-            if (++ab == 2) { ab = 0; aph ^= 1; }
-            if (!ok) s_abort = 1;
-            named_bar(1, 32 * GV_CONSUMERS);
-            if (s_abort) break;
-            // C fragments: acc2[mt][0..1] = tile row 32 rg + 16 mt + g, tokens 2c, 2c+1; [2..3] = row +8.
-            // As 8 values h = 2 mt + (row half), token 2c + (h & 1): rows trs[h >> 1]. Group 1 hands its
-            // sums to group 0, then the block-1 warps to the block-0 warps, which own the rows from here on.
-            float acc[8];
+            // lane c owns tokens 2c, 2c+1 (tc >= 2) or token 0 (tc == 1, lane c = 0, column 0)
+            bool own[2];
 #pragma unroll
-            for (int h = 0; h < 8; ++h) acc[h] = acc2[h >> 2][h & 3];
-            const int trs[4] = {rg * 32 + g, rg * 32 + g + 8, rg * 32 + 16 + g, rg * 32 + 24 + g};
-            if (grp == 1) {
-#pragma unroll
-                for (int h = 0; h < 8; ++h) xch2[(blk * 128 + trs[h >> 1]) * kGemvRows + 2 * c + (h & 1)] = acc[h];
-            }
-            named_bar(1, 32 * GV_CONSUMERS);
-            if (grp == 0) {
-#pragma unroll
-                for (int h = 0; h < 8; ++h) acc[h] += xch2[(blk * 128 + trs[h >> 1]) * kGemvRows + 2 * c + (h & 1)];
-            }
-            if (grp == 0 && blk == 1) {
-#pragma unroll
-                for (int h = 0; h < 8; ++h) xch[trs[h >> 1] * kGemvRows + 2 * c + (h & 1)] = acc[h];
-            }
-            named_bar(1, 32 * GV_CONSUMERS);
-            const bool owner = grp == 0 && blk == 0;
-            if (owner) {
-#pragma unroll
-                for (int h = 0; h < 8; ++h) acc[h] += xch[trs[h >> 1] * kGemvRows + 2 * c + (h & 1)];
-            }
-            named_bar(1, 32 * GV_CONSUMERS);
+            for (int cc = 0; cc < 2; ++cc)
+                own[cc] = (tc == 1 ? (c == 0 && cc == 0) : (2 * c < tc)) && 2 * c + cc < it.n;
             const int F = it.sh ? a.F_shared : a.F_routed;
-            const int ncols = GATE_UP ? 2 * F : a.H;
-            auto colof = [&](int tr) {
-                return GATE_UP ? (tr < 64 ? it.bnd * 64 + tr : F + it.bnd * 64 + tr - 64) : it.bnd * kTileRows + tr;
+            const int ncols = a.part_ld;   // one row stride for every group (F and F_s may differ)
+            auto colof = [&](int mt, int h) {
+                const int r = 16 * j + g + 8 * h;
+                return GATE_UP ? mt * F + it.bnd * 64 + r : it.bnd * kTileRows + 64 * mt + r;
             };
+            if (!GATE_UP && KC > 1) {   // y rows were cleared by the gate/up kernel: add this chunk
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc)
+                        if (own[cc]) {
+                            const size_t row = (size_t)(it.row0 + 2 * c + cc);
+                            atomicAdd(a.y_out + row * a.H + colof(0, h), acc[0][2 * h + cc]);
+                            atomicAdd(a.y_out + row * a.H + colof(1, h), acc[1][2 * h + cc]);
+                        }
+                continue;
+            }
             if (KC > 1) {
                 float* part = a.part + (size_t)it.kc * a.part_rows * ncols;
 #pragma unroll
-                for (int h = 0; h < 8; ++h) {
-                    const int t = 2 * c + (h & 1);
-                    if (owner && t < it.n) part[(size_t)(it.row0 + t) * ncols + colof(trs[h >> 1])] = acc[h];
-                }
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc)
+                            if (own[cc]) part[(size_t)(it.row0 + 2 * c + cc) * ncols + colof(mt, h)] = acc[mt][2 * h + cc];
                 __threadfence();
-                named_bar(1, 32 * GV_CONSUMERS);
-                if (threadIdx.x == 0) s_last = atomicAdd(&a.done[it.slot], 1) == KC - 1;
-                named_bar(1, 32 * GV_CONSUMERS);
-                if (!s_last) continue;
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) last = atomicAdd(&a.done[it.slot * GV_WARPS + j], 1) == KC - 1;
+                if (!__shfl_sync(0xffffffffu, last, 0)) continue;
                 __threadfence();
 #pragma unroll
-                for (int h = 0; h < 8; ++h) {
-                    const int t = 2 * c + (h & 1);
-                    if (owner && t < it.n) {
-                        float v = 0.f;
-                        for (int q = 0; q < KC; ++q)
-                            v += __ldcg(a.part + (size_t)q * a.part_rows * ncols + (size_t)(it.row0 + t) * ncols + colof(trs[h >> 1]));
-                        acc[h] = v;
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc)
+                            if (own[cc]) {
+                                const size_t o = (size_t)(it.row0 + 2 * c + cc) * ncols + colof(mt, h);
+                                float v = 0.f;
+                                for (int q = 0; q < KC; ++q) v += __ldcg(a.part + (size_t)q * a.part_rows * ncols + o);
+                                acc[mt][2 * h + cc] = v;
+                            }
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    if (!own[cc]) continue;
+                    const size_t row = (size_t)(it.row0 + 2 * c + cc);
+                    if (GATE_UP) {
+                        const float hv = silu_f(acc[0][2 * h + cc]) * acc[1][2 * h + cc];   // h = bf16(silu(g) u)
+                        a.h_out[row * a.h_ld + it.bnd * 64 + 16 * j + g + 8 * h] = f32_to_bf16_bits(hv);
+                    } else {
+                        a.y_out[row * a.H + colof(0, h)] = acc[0][2 * h + cc];
+                        a.y_out[row * a.H + colof(1, h)] = acc[1][2 * h + cc];
                     }
                 }
-            }
-            if (GATE_UP) {
-                // up rows (rg 2-3) hand their sums to the gate rows (rg 0-1); h = bf16(silu(g) * u)
-                if (owner && rg >= 2) {
-#pragma unroll
-                    for (int h = 0; h < 8; ++h) xch[(trs[h >> 1] - 64) * kGemvRows + 2 * c + (h & 1)] = acc[h];
-                }
-                named_bar(1, 32 * GV_CONSUMERS);
-                if (owner && rg < 2) {
-#pragma unroll
-                    for (int h = 0; h < 8; ++h) {
-                        const int t = 2 * c + (h & 1), tr = trs[h >> 1];
-                        const uint16_t hb = f32_to_bf16_bits(silu_f(acc[h]) * xch[tr * kGemvRows + t]);
-                        if (t < it.n) a.h_out[(size_t)(it.row0 + t) * a.h_ld + it.bnd * 64 + tr] = hb;
-                    }
-                }
-                named_bar(1, 32 * GV_CONSUMERS);
-            } else if (owner) {
-#pragma unroll
-                for (int h = 0; h < 8; ++h) {
-                    const int t = 2 * c + (h & 1);
-                    if (t < it.n) a.y_out[(size_t)(it.row0 + t) * a.H + colof(trs[h >> 1])] = acc[h];
-                }
-            }
         }
-        if (s_abort && threadIdx.x == 0) atomicCAS(a.err, 0, FM_ETIMEOUT);
+        if (!ok && lane == 0) atomicCAS(a.err, 0, FM_ETIMEOUT);
     }
-    __syncthreads();
 }
 
 // ------------------------------------------------------------------ launchers
-int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
-                          int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
-                          int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int* err,
-                          cudaStream_t st) {
-    const size_t sm = (size_t)(e_local * 33 + 32) * 4;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(dispatch_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        attr = true;
-    }
-    dispatch_small_kernel<<<1, kDispSmallThreads, sm, st>>>(idx, P, e_begin, e_local, shared_base, shared_rows, counts,
-                                                           offsets, pos, pair, gu_list, gu_bands, gu_bands_shared,
-                                                           gu_slabs, dn_list, dn_bands, dn_slabs, dn_slabs_shared, err);
-    FM_LAUNCH_CHECK("dispatch_small");
-    return FM_OK;
-}
-
-static int gemv_grid(int max_items) {
+static int sm_count_decode() {
     static int n = 0;
     if (!n) {
         int dev = 0;
@@ -543,7 +619,31 @@ static int gemv_grid(int max_items) {
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
         if (n <= 0) n = 148;
     }
-    return max_items < n ? max_items : n;
+    return n;
+}
+
+int gemv_chunk_cap(int T) {
+    const int cap = T <= 4 ? 16 : 64 / T;
+    return cap < 2 ? 2 : cap;
+}
+
+int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
+                          int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
+                          int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int kc_cap,
+                          int* done, int* err, cudaStream_t st) {
+    const size_t sm = (size_t)(e_local * 33 + 32 + 3 * (e_local + 2)) * 4;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(dispatch_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        attr = true;
+    }
+    const int target = GV_CTAS_PER_SM * sm_count_decode();   // one item per CTA slot
+    dispatch_small_kernel<<<1, kDispSmallThreads, sm, st>>>(idx, P, e_begin, e_local, shared_base, shared_rows, counts,
+                                                           offsets, pos, pair, gu_list, gu_bands, gu_bands_shared,
+                                                           gu_slabs, dn_list, dn_bands, dn_slabs, dn_slabs_shared, kc_cap,
+                                                           target, done, err);
+    FM_LAUNCH_CHECK("dispatch_small");
+    return FM_OK;
 }
 
 int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st) {
@@ -563,6 +663,7 @@ int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st) {
     a.shared_base = L.shared_base;
     a.part = L.part;
     a.part_rows = L.part_rows;
+    a.part_ld = L.part_ld;
     a.done = L.done;
     a.h_out = L.h_out;
     a.h_ld = L.h_ld;
@@ -570,8 +671,11 @@ int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st) {
     a.F_shared = L.F_shared;
     a.y_out = L.y_out;
     a.H = L.H;
+    a.dn_list = L.dn_list;
+    a.y_rows = L.y_rows;
     a.err = L.err;
-    const int grid = gemv_grid(L.max_items);
+    const int slots = GV_CTAS_PER_SM * sm_count_decode();
+    const int grid = L.max_items < slots ? L.max_items : slots;
     if (gate_up) {
         static bool attr = false;
         if (!attr) {

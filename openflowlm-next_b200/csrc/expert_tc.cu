@@ -2,16 +2,18 @@
 //
 // One persistent CTA per SM walks the work list (group, band, first sorted row, rows). A work item
 // is D[128 weight rows x n tokens] = W_band[128 x K] . X[n x K]^T with n <= 256, K walked in 64-wide
-// slabs. Warp roles (480 threads for gate_up, 576 for down):
-//   warp 0      producer: per slab, one 5120-byte bulk copy of the raw Q4_1 weight tile and
-//               ceil(n/32) TMA loads (128-byte swizzle) of the sorted bf16 activation rows;
+// slabs. Warp roles (480 threads for gate_up, 608 for down):
+//   warp 0      weight producer: per slab, one 5120-byte bulk copy of the raw Q4_1 weight tile;
+//   last warp   activation producer: per slab, 128- and 32-row TMA loads (128-byte swizzle) of the
+//               sorted bf16 activation rows;
 //   warp 1      TMEM owner and MMA issuer: four tcgen05.mma (M=128, N=n rounded to 16, K=16) per
 //               slab into one of two TMEM accumulators (2 x 256 columns), commits release the rings;
-//   warps 2-5   dequantisers: thread r turns row r of the raw tile (two GGUF blocks) into 64 bf16
+//   warps 2-9   dequantisers, two groups taking alternate slabs: thread r of a group turns row r of
+//               the raw tile (two GGUF blocks) into 64 bf16
 //               values in the 128-byte-swizzled K-major layout the MMA reads (w = q*d + m in f32 with
 //               the fp16 d, m widened exactly, rounded once to bf16);
-//   warps 6-13  epilogue in two halves of four warps (alternate 32-token chunks), overlapped with the
-//               next item's main loop through the second accumulator:
+//   warps 10-   epilogue (gate_up 4 warps; down 8 in two halves taking alternate 32-token chunks),
+//               overlapped with the next item's main loop through the second accumulator:
 //               GATE_UP  rows 0-63 of a gate_up tile are gate rows, rows 64-127 the up rows of the same
 //                        64 features: h = bf16(silu(g) * u) -> the sorted h matrix (the reference's
 //                        SwiGLU, designs/moe_batch/moe_batch.h:181-202, h rounded to bf16);
@@ -31,8 +33,9 @@
 namespace fm {
 
 // Warp roles: 0 weight producer, 1 MMA issuer, then DQ dequantiser warps (groups of 4 working alternate
-// slabs), EPI epilogue warps, and the activation producer last. gate_up (K = H = 2048, light epilogue):
-// 8 + 4, 480 threads; down (K = F = 512, a y row per token and band): 8 + 8, 576 threads.
+// slabs), EPI epilogue warps (groups of 4, "halves", taking alternate 32-token chunks), and the
+// activation producer last. gate_up (K = H = 2048, light epilogue): 8 + 4, 480 threads; down
+// (K = F = 512, a y row per token and band): 8 + 8, 608 threads.
 template <bool GATE_UP>
 struct TcRoles {
     static constexpr int DQ = 8;
@@ -206,7 +209,7 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
         // a dequantiser group (4 warps, 128 threads) consumes a raw tile and fills an A stage
         for (int i = 0; i < SR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 128); }
         for (int i = 0; i < SB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
-        // arrivals are per warp: 4 dequantiser / 8 epilogue warps per CTA, both CTAs' on the first CTA's
+        // arrivals are per warp: 4 dequantiser / 4 or 8 epilogue warps per CTA, both CTAs' on the first CTA's
         for (int i = 0; i < SA; ++i) { mbar_init(&a_full[i], (PAIR ? 2 : 1) * 4); mbar_init(&a_empty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], (PAIR ? 2 : 1) * R::EPI); }
         mbar_init(drain, 1);
@@ -373,7 +376,6 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                 const uint4 n0 = gguf_order(*reinterpret_cast<const uint4*>(raw + r * 32));
                 const uint4 n1 = gguf_order(*reinterpret_cast<const uint4*>(raw + r * 32 + 16));
                 const uint2 sc2 = *reinterpret_cast<const uint2*>(raw + kTileNibBytes + r * 8);
-                mbar_arrive(&raw_empty[rs]);
                 const float d0 = __half2float(__ushort_as_half((unsigned short)(sc2.x & 0xFFFF)));
                 const float m0 = __half2float(__ushort_as_half((unsigned short)(sc2.x >> 16)));
                 const float d1 = __half2float(__ushort_as_half((unsigned short)(sc2.y & 0xFFFF)));
@@ -381,6 +383,13 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                 uint4 ch[8];
                 deq_block(n0, d0, m0, ch);
                 deq_block(n1, d1, m1, ch + 4);
+                // The raw slot goes back to the weight producer, whose next bulk copy (async proxy)
+                // overwrites it, only after this thread's loads from it have delivered their values (the
+                // dequantised words depend on them) and a proxy fence: releasing it right after issuing
+                // the loads let the copy land under loads still in flight on B200 (wrong weights for a
+                // slab, intermittently).
+                fence_proxy_async_smem();
+                mbar_arrive(&raw_empty[rs]);
                 if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[as], aph ^ 1))) { ok = false; break; }
                 uint8_t* arow = smem + Sm::a + as * TC_A_BYTES + r * 128;
 #pragma unroll
@@ -453,10 +462,31 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
             if (!mbar_wait(&acc_full[acc], accph)) epi_abort = 1;
             named_bar(3, 32 * R::EPI);
             if (epi_abort) break;
-            if (!GATE_UP) {   // DOWN: 8 warps, 256 threads, one row each
+            if (!GATE_UP) {   // DOWN: the rows' destinations and weights, strided over the epilogue threads
                 if (et < it.n) {
                     tok[et] = tk;
                     wgt[et] = wk;
+                }
+                for (int rr = et + 32 * R::EPI; rr < it.n; rr += 32 * R::EPI) {
+                    const int rrow = it.row0 + rr;
+                    int t2;
+                    float w2;
+                    if (mode == 1) {
+                        t2 = (a.ymap && !shared_item) ? a.ymap[rrow] : rrow;
+                        w2 = 1.0f;
+                    } else if (shared_item) {
+                        t2 = rrow - a.shared_base;
+                        w2 = a.sgate[t2];
+                    } else if (mode == 2) {
+                        t2 = *reinterpret_cast<volatile const int*>(a.err) == 0 ? a.meta[rrow] : -1;
+                        w2 = 1.0f;
+                    } else {
+                        const int p = a.pair[rrow];
+                        t2 = p / a.k;
+                        w2 = a.wpair[p];
+                    }
+                    tok[rr] = t2;
+                    wgt[rr] = w2;
                 }
                 named_bar(3, 32 * R::EPI);
             }

@@ -70,21 +70,25 @@ struct GemvLaunch {
     int k;
     int shared_base;
     float* part;
-    int part_rows;
+    int part_rows, part_ld;
     int* done;
     uint16_t* h_out;
     int h_ld;
     int F_routed, F_shared;
     float* y_out;
     int H;
+    const int* dn_list;   // GATE_UP: the down list (its K-chunk count)
+    int y_rows;           // rows of y_out (cleared by GATE_UP when the down GEMM splits K)
     int* err;
 };
 int router_ksplit(int T, int H, int E);
 size_t router_scratch_bytes(int T, int H, int E);   // the logits scratch of launch_router
 int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
                           int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
-                          int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int* err,
-                          cudaStream_t st);
+                          int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int kc_cap,
+                          int* done, int* err, cudaStream_t st);
+int gemv_chunk_cap(int T);    // most K chunks per GEMV item at T tokens (sizes the partial-sum buffer)
+constexpr int kGemvWarps = 4; // consumer warps of a GEMV CTA (one completion counter per item slot each)
 int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st);
 int launch_seg_lists(const int* seg, int nseg, int shared_group, int shared_base, int shared_rows, int* gu_list,
                      int gu_bands, int gu_bands_shared, int* dn_list, int dn_bands, int bn, cudaStream_t st);

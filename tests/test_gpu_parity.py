@@ -164,6 +164,12 @@ def test_moe_block_skewed_prefill_tc(dev):
     assert counts.max() > 256 and counts.min() < 256
     ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
     assert _rel(out, ref, c["res"]) < TOL
+    # repeated calls: a race between the kernel's roles shows as a wrong item in some calls only
+    sg = layer.shared_gate_buf
+    ti, tw = torch.from_numpy(idx).to(dev), torch.from_numpy(w).to(dev)
+    for _ in range(8):
+        again = layer.moe_block(x, res, ti, tw, shared_gate=sg).cpu().numpy()
+        assert _rel(again, ref, c["res"]) < TOL
 
 
 @pytest.mark.parametrize("T", [1, 3, 32])
@@ -197,6 +203,47 @@ def test_gemv_hot_expert_many_rows(dev):
     out = layer.moe_block(x, res, idx, w).cpu().numpy()
     ref = OM.moe_block_f64(c["x"], c["res"], idx.cpu().numpy(), w.cpu().numpy(), c["gate"], c["up"], c["down"])
     assert _rel(out, ref, c["res"]) < TOL
+
+
+@pytest.mark.parametrize("shared", [False, True])
+def test_gemv_every_token_width(dev, shared):
+    """Experts with 1, 2, 3, 4, 5, 6 and 11 tokens: GEMV items of every token-column width (1, 2, 4
+    and 8 columns, i.e. 8, 4, 2 and 1 Q4_1 blocks per accumulator) and an expert split over two items;
+    K split into chunks (few items); with and without the shared expert's 16-token items."""
+    c = cases.make_case(H=2048, E=8, F=768, FS=512 if shared else 0, k=2, T=16, seed=31)
+    layer = _layer(c, dev, "gemv")
+    x = torch.from_numpy(c["x"]).to(dev).to(torch.bfloat16)
+    res = torch.from_numpy(c["res"]).to(dev)
+    flat = np.repeat(np.arange(7), [1, 2, 3, 4, 5, 6, 11])          # 32 assignments, sorted
+    idx_h = np.stack([flat[:16], flat[16:]], axis=1).astype(np.int32)  # token t: entries t and t+16 (distinct)
+    rng = np.random.default_rng(5)
+    w_h = rng.uniform(0.2, 1.0, (16, 2)).astype(np.float32)
+    w_h /= w_h.sum(axis=1, keepdims=True)
+    idx, w = torch.from_numpy(idx_h).to(dev), torch.from_numpy(w_h).to(dev)
+    sg = None
+    if shared:
+        layer.router_block(x)
+        sg = layer.shared_gate_buf
+    out = layer.moe_block(x, res, idx, w, shared_gate=sg).cpu().numpy()
+    ref = OM.moe_block_f64(c["x"], c["res"], idx_h, w_h, c["gate"], c["up"], c["down"], shared=c["shared"])
+    assert _rel(out, ref, c["res"]) < TOL
+
+
+def test_tc_headline_shape_matches_mma(dev):
+    """The headline shape (C36: 256 experts, F 512 + shared 512, T = 8192 tokens) through the tcgen05
+    path, several calls, against the mma.sync path on the same weights and routing (that path matches
+    the fp64 oracle on the small cases)."""
+    import flowmoe
+    from flowmoe.synth import C36, synth_layer, synth_tokens
+    layer = synth_layer(flowmoe.MoEConfig(**C36), seed=3)
+    x, res = synth_tokens(8192, 2048, seed=4)
+    layer.path = "mma"
+    ref = layer.forward(x, res).clone()
+    scale = (ref - res).abs().max().item()
+    layer.path = "tc"
+    for _ in range(4):
+        out = layer.forward(x, res)
+        assert (out - ref).abs().max().item() / scale < TOL
 
 
 def test_tc_matches_mma_path(dev):
