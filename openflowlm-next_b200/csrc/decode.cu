@@ -367,7 +367,8 @@ __device__ __forceinline__ bool gv_item(uint8_t* smem, uint64_t* full, uint64_t*
                         cx[0] = cx[1] = cx[2] = cx[3] = 0.f;
                     }
                 }
-                if (P == 1) {
+                if (P == 1) {   // release the stage (its next fill is an async-proxy copy)
+                    fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[st]);
                 }
@@ -395,6 +396,10 @@ __device__ __forceinline__ bool gv_item(uint8_t* smem, uint64_t* full, uint64_t*
                         }
                 }
             }
+            // release the group's stages: every load from them has delivered its value (the
+            // accumulators depend on them), and the fence orders these reads before the producer's
+            // next bulk copies (async proxy) into the same stages
+            fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0)
                 for (int q = 0; q < gs; ++q) mbar_arrive(&empty[(st0 + q) % GV_STAGES]);
