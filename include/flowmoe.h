@@ -95,6 +95,17 @@ FM_API int fm_tiles_to_q4_1(const uint8_t* tiles, int32_t rows, int32_t k, uint8
  * kernels dequantise with the narrowed scales. For bit-level agreement with the NPU's pool. */
 FM_API int fm_tiles_narrow_scales(uint8_t* tiles, int64_t n_tiles, void* stream);
 
+/* The reference's pool chunk bytes (device) -> GGUF Q4_1 blocks uint8[n, k/32, 20] (device): the
+ * inverse of its pool packers, open_kernels/q4_1_pack.py:124-142 (pack_q4_1_pool: chunk_bytes 5120,
+ * bf16 d and m planes) and gguf_pool/gguf_pool.py:191-213 (pack_q4_pool: chunk_bytes 6144, f32
+ * planes), in the pool order of q4_1_pack.py:112-121 with band row split rs (2 standard, 4 expert
+ * stripes). k % 256 == 0, n % (32 rs) == 0. Scales become fp16; *inexact (a device int32, cleared
+ * here) counts those fp16 cannot hold exactly -- zero for every pool those packers write, since they
+ * widen fp16 scales to f32 or narrow them to bf16. The blocks then go through fm_q4_1_to_tiles /
+ * fm_gate_up_to_tiles; a 5120-byte pool's bf16 scales give the NPU pool's numerics exactly. */
+FM_API int fm_pool_to_q4_1(const uint8_t* pool, int32_t n, int32_t k, int32_t rs, int32_t chunk_bytes, uint8_t* blocks,
+                           int32_t* inexact, void* stream);
+
 /* Router weight bf16 Wr [H, E] row-major (the reference's layout, block_host.cpp:775-777) and the
  * shared-expert gate bf16 sgw [H] (or NULL) -> the layer's router array bf16 [E + 1, H]. */
 FM_API int fm_router_pack(const uint16_t* wr, const uint16_t* sgw, int32_t hidden, int32_t n_experts, uint16_t* router,

@@ -102,6 +102,52 @@ __global__ void router_pack_kernel(const uint16_t* __restrict__ wr, const uint16
     }
 }
 
+// The reference's pool chunk bytes -> GGUF Q4_1 blocks: the inverse of its pool packers
+// (open_kernels/q4_1_pack.py:124-142 pack_q4_1_pool, 5120-byte chunks with bf16 d and m planes;
+// gguf_pool/gguf_pool.py:191-213 pack_q4_pool, 6144-byte chunks with f32 planes). A chunk holds 32 rows x
+// 256 K of a [n, k] matrix in the pool order of q4_1_pack.py:112-121 (chunk c: band c / per_band,
+// ci = c % per_band, rows 32 rs band + 32 (ci % rs), columns 256 (ci / rs)); its scale planes are indexed
+// kb * 32 + row, its codes p = (row / 16) * 4096 + col * 16 + row % 16 two to a byte, even p in the low
+// nibble. One thread per (row, block): the block's d and m become fp16 (exact for every scale those
+// packers write: widened fp16 values, or fp16 values narrowed to bf16); `inexact` counts the ones fp16
+// cannot hold.
+__global__ void pool_to_q4_1_kernel(const uint8_t* __restrict__ pool, int n, int k, int rs, int scale_bytes,
+                                    uint8_t* __restrict__ blocks, int* __restrict__ inexact) {
+    const int nb = k / 32;
+    const long long total = (long long)n * nb;
+    const int per_band = rs * k / 256;
+    const int plane = 256 * scale_bytes;                  // bytes of one scale plane
+    const long long chunk = 2 * plane + 4096;             // 5120 or 6144
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / nb), b = (int)(i % nb);
+        const int band = r / (32 * rs), sub = (r % (32 * rs)) / 32;
+        const long long c = (long long)band * per_band + (long long)(b / 8) * rs + sub;
+        const uint8_t* ch = pool + c * chunk;
+        const int rr = r % 32, kb = b % 8, j = kb * 32 + rr;
+        float d, m;
+        if (scale_bytes == 2) {
+            d = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ch + 2 * j));
+            m = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ch + plane + 2 * j));
+        } else {
+            d = *reinterpret_cast<const float*>(ch + 4 * j);
+            m = *reinterpret_cast<const float*>(ch + plane + 4 * j);
+        }
+        const __half hd = __float2half_rn(d), hm = __float2half_rn(m);
+        if (!(__half2float(hd) == d) || !(__half2float(hm) == m)) atomicAdd(inexact, 1);
+        // codes of row rr, columns kb*32 .. kb*32+31 of the chunk: one nibble of every 8th byte
+        const uint8_t* codes = ch + 2 * plane + ((rr >> 4) * 4096 + (rr & 15)) / 2;
+        const int shift = (rr & 1) * 4;
+        uint8_t q[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) q[t] = (codes[(kb * 32 + t) * 8] >> shift) & 0xF;
+        uint8_t* o = blocks + i * 20;
+        const unsigned short hdb = __half_as_ushort(hd), hmb = __half_as_ushort(hm);
+        o[0] = hdb & 0xFF; o[1] = hdb >> 8; o[2] = hmb & 0xFF; o[3] = hmb >> 8;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) o[4 + t] = q[t] | (q[t + 16] << 4);   // byte t: value t low, t+16 high
+    }
+}
+
 }  // namespace fm
 
 using namespace fm;
@@ -178,6 +224,27 @@ extern "C" FM_API int fm_tiles_narrow_scales(uint8_t* tiles, int64_t n_tiles, vo
     const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
     narrow_scales_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(tiles, n_tiles);
     FM_LAUNCH_CHECK("narrow_scales");
+    return FM_OK;
+}
+
+extern "C" FM_API int fm_pool_to_q4_1(const uint8_t* pool, int32_t n, int32_t k, int32_t rs, int32_t chunk_bytes,
+                                       uint8_t* blocks, int32_t* inexact, void* stream) {
+    if (!pool || !blocks || !inexact || n <= 0 || k <= 0 || rs <= 0 || k % 256 || n % (32 * rs) ||
+        (chunk_bytes != 5120 && chunk_bytes != 6144)) {
+        set_error("fm_pool_to_q4_1: needs k %% 256 == 0, n %% (32 rs) == 0 and 5120- or 6144-byte chunks "
+                  "(got n=%d k=%d rs=%d chunk=%d)", n, k, rs, chunk_bytes);
+        return FM_EINVAL_SHAPE;
+    }
+    if ((reinterpret_cast<uintptr_t>(pool) & 3) || (reinterpret_cast<uintptr_t>(inexact) & 3)) {
+        set_error("fm_pool_to_q4_1: pool and inexact must be 4-byte aligned");
+        return FM_EINVAL_SHAPE;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    if (cudaMemsetAsync(inexact, 0, sizeof(int32_t), st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
+    const long long total = (long long)n * (k / 32);
+    const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+    pool_to_q4_1_kernel<<<grid, 256, 0, st>>>(pool, n, k, rs, chunk_bytes == 5120 ? 2 : 4, blocks, inexact);
+    FM_LAUNCH_CHECK("pool_to_q4_1");
     return FM_OK;
 }
 

@@ -6,8 +6,9 @@ sigmoid-gated shared expert, as hand-written CUDA behind the C ABI of ``libflowm
 (``include/flowmoe.h``). Importing this package loads that library; there is no CPU fallback.
 """
 from . import _lib  # noqa: F401  (loads libflowmoe.so or raises)
-from .layer import MoEConfig, MoELayer, gate_up_to_tiles, q4_1_to_tiles, router_block, tiles_to_q4_1  # noqa: F401
+from .layer import (MoEConfig, MoELayer, gate_up_to_tiles, pool_to_q4_1, q4_1_to_tiles, router_block,  # noqa: F401
+                    tiles_to_q4_1)
 from .quant import dequantize_q4_1, quantize_q4_1  # noqa: F401
 
-__all__ = ["MoEConfig", "MoELayer", "router_block", "q4_1_to_tiles", "tiles_to_q4_1", "quantize_q4_1",
-           "dequantize_q4_1"]
+__all__ = ["MoEConfig", "MoELayer", "router_block", "q4_1_to_tiles", "tiles_to_q4_1", "pool_to_q4_1",
+           "quantize_q4_1", "dequantize_q4_1"]

@@ -109,6 +109,27 @@ def tiles_to_q4_1(tiles: torch.Tensor, rows: int, k: int) -> torch.Tensor:
     return dst
 
 
+def pool_to_q4_1(pool, n: int, k: int, rs: int = 2, chunk_bytes: int | None = None, device="cuda") -> torch.Tensor:
+    """The reference's pool chunk bytes of one [n, k] matrix -> GGUF Q4_1 blocks [n, k/32, 20] (device).
+
+    ``pool`` is what open_kernels/q4_1_pack.py ``pack_q4_1_pool`` (5120-byte chunks, bf16 scales) or
+    gguf_pool/gguf_pool.py ``pack_q4_pool`` (6144-byte chunks, f32 scales) wrote for the matrix with band
+    row split ``rs``; ``chunk_bytes`` is inferred from the size when not given. Raises if a scale does
+    not fit fp16 exactly (a pool those packers did not write)."""
+    src = _as_dev_u8(pool, device).reshape(-1)
+    nch = n * k // (32 * 256)
+    if chunk_bytes is None:
+        chunk_bytes = src.numel() // nch if nch and src.numel() % nch == 0 else 0
+    if src.numel() != nch * chunk_bytes:
+        raise ValueError(f"{src.numel()} pool bytes are not {nch} chunks of {chunk_bytes} B for [{n}, {k}]")
+    out = torch.empty(n, k // 32, Q4_1_BYTES, dtype=torch.uint8, device=src.device)
+    bad = torch.empty(1, dtype=torch.int32, device=src.device)
+    call("fm_pool_to_q4_1", src.data_ptr(), n, k, rs, chunk_bytes, out.data_ptr(), bad.data_ptr(), _stream(src.device))
+    if int(bad.item()):
+        raise _lib.FlowMoeError(_lib.FM_EINVAL_SHAPE, f"pool_to_q4_1: {int(bad.item())} scales do not fit fp16")
+    return out
+
+
 def narrow_scales(tiles: torch.Tensor) -> torch.Tensor:
     """In place: every d and m of a tile array rounded to bf16 precision (fm_tiles_narrow_scales)."""
     n = tiles.numel()

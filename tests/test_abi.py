@@ -75,3 +75,15 @@ def test_small_workspace_is_rejected():
 def test_tile_geometry_checked():
     from flowmoe import _lib
     assert _lib.lib.fm_q4_1_to_tiles(None, 100, 2048, None, None) == _lib.FM_EINVAL_SHAPE
+
+
+@pytest.mark.parametrize("n,k,rs,chunk", [(64, 200, 2, 5120), (48, 256, 2, 5120), (64, 256, 0, 5120), (64, 256, 2, 4096)])
+def test_pool_import_bad_geometry_is_rejected(n, k, rs, chunk):
+    """fm_pool_to_q4_1 checks k % 256, n % (32 rs) and the chunk size before any device work."""
+    from flowmoe import _lib
+    buf = (ctypes.c_uint8 * 16)()
+    bad = (ctypes.c_int32 * 1)()
+    rc = _lib.lib.fm_pool_to_q4_1(ctypes.cast(buf, ctypes.c_void_p), n, k, rs, chunk, ctypes.cast(buf, ctypes.c_void_p),
+                                  ctypes.cast(bad, ctypes.c_void_p), None)
+    assert rc == _lib.FM_EINVAL_SHAPE
+    assert "fm_pool_to_q4_1" in _lib.last_error()

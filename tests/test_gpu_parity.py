@@ -46,6 +46,28 @@ def test_tiles_round_trip_bit_exact(dev):
     assert not np.array_equal(t.cpu().numpy(), blocks.reshape(-1))   # it is a real permutation
 
 
+@pytest.mark.parametrize("chunk", [5120, 6144])
+def test_pool_import_bit_exact(dev, golden, chunk):
+    """The reference's pool bytes (its own packers' output, and the oracle's restatement of them at an
+    expert-stripe split rs = 4) -> GGUF blocks on the device, bit for bit the oracle's inverse; the f32
+    pool gives back the original blocks, the bf16 pool their bf16-scale twins; the imported blocks then
+    tile like any others."""
+    import flowmoe
+    g = golden["q4_1"]
+    pool = g["pool_bf16_rs2" if chunk == 5120 else "pool_f32_rs2"]
+    got = flowmoe.pool_to_q4_1(pool, 64, 256, rs=2, device=dev).cpu().numpy()
+    assert np.array_equal(got, OQ.pool_to_blocks(pool, 64, 256, 2, chunk))
+    blocks = OQ.random_q4_1_blocks(512, 2048, np.random.default_rng(7))
+    pool4 = OQ.blocks_to_pool(blocks, 4, chunk)
+    got4 = flowmoe.pool_to_q4_1(pool4, 512, 2048, rs=4, device=dev)
+    want4 = OQ.pool_to_blocks(pool4, 512, 2048, 4, chunk)
+    assert np.array_equal(got4.cpu().numpy(), want4)
+    if chunk == 6144:
+        assert np.array_equal(want4, blocks)
+    t = flowmoe.q4_1_to_tiles(got4, 512, 2048, dev)
+    assert np.array_equal(flowmoe.tiles_to_q4_1(t, 512, 2048).cpu().numpy().reshape(want4.shape), want4)
+
+
 def _check_router(c, probs, idx, w):
     xb = c["x"]
     p_ref, idx_ref, w_ref = OM.router_block(xb, c["Wr"], c["k"])

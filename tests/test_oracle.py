@@ -157,3 +157,17 @@ def test_dequant_bf16_scales_bit_exact(golden):
     """The q4nx numerics (d, m narrowed to bf16): the reference's dequant_q4_1(scale_dtype=bfloat16)."""
     g = golden["q4_1"]
     assert np.array_equal(OQ.dequant_q4_1(g["blocks"], bf16_scales=True), g["dequant_bf16_scales"])
+
+
+def test_pool_packers_match_reference_bytes(golden):
+    """The oracle's restatement of the reference's two pool packers writes their very bytes
+    (q4_1_pack.pack_q4_1_pool: bf16 planes; gguf_pool.pack_q4_pool: f32 planes; rs = 2), and the inverse
+    gives back the blocks exactly (f32) or with the bf16-narrowed scales the NPU pool computes with."""
+    g = golden["q4_1"]
+    b = g["blocks"]
+    assert np.array_equal(OQ.blocks_to_pool(b, 2, 5120), g["pool_bf16_rs2"])
+    assert np.array_equal(OQ.blocks_to_pool(b, 2, 6144), g["pool_f32_rs2"])
+    assert np.array_equal(OQ.pool_to_blocks(g["pool_f32_rs2"], 64, 256, 2, 6144), b)
+    b16 = OQ.pool_to_blocks(g["pool_bf16_rs2"], 64, 256, 2, 5120)
+    assert np.array_equal(b16[..., 4:], b[..., 4:])
+    assert np.array_equal(OQ.dequant_q4_1(b16), g["dequant_bf16_scales"])
