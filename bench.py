@@ -346,6 +346,36 @@ def run_reference(args):
     return 0
 
 
+def ep_stack_measure(rank, world, args, n_layers=48, T_total=64):
+    """BASELINE config 5 across the group: 48 C36 layers of x + MoE(RMSNorm(x)), T_total decode tokens
+    split over the ranks, experts sharded, the stack captured into one CUDA graph per rank and replayed;
+    ms per step is the max over ranks of the CUDA-event time of the replays."""
+    import flowmoe
+    from flowmoe.ep import expert_range
+    from flowmoe.stack import EPMoEStack
+    from flowmoe.synth import C36, synth_stack, synth_tokens
+    eb, el = expert_range(256, rank, world)
+    cfg = flowmoe.MoEConfig(**C36, e_begin=eb, e_local=el)
+    layers, norms = synth_stack(cfg, n_layers, seed=5)
+    Tr = T_total // world
+    x, _ = synth_tokens(T_total, cfg.hidden, seed=5)
+    x = x.float()[rank * Tr:(rank + 1) * Tr].contiguous()
+    stack = EPMoEStack(layers, norms, t_cap=Tr).capture(Tr)
+    st = torch.cuda.current_stream()
+    for _ in range(3):
+        stack.forward(x)
+    stack.check()
+    ms = max_over_ranks(time_steps(lambda: stack.forward(x), 10, 0, world, st), world)
+    stack.check()
+    e_bytes = 3 * cfg.hidden * cfg.ffn * 5 // 8
+    stack.close()
+    del stack, layers
+    torch.cuda.empty_cache()
+    return {"layers": n_layers, "T_total": T_total, "tokens_per_rank": Tr, "ms": round(ms, 3),
+            "tokens_per_s": round(T_total / (ms * 1e-3), 1), "experts_per_gpu": el,
+            "expert_bytes": e_bytes, "graph": "whole stack per rank, replayed"}
+
+
 def run_flowmoe(args):
     import flowmoe
     from flowmoe import _lib
@@ -446,6 +476,8 @@ def run_flowmoe(args):
     e2e = {"value": round(T * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
            "h2d_bytes_per_step": x.numel() * 2 + res.numel() * 4, "d2h_bytes_per_step": oh.numel() * 4}
 
+    ep_stack = ep_stack_measure(rank, world, args) if world > 1 and args.ep == "peer" and not args.no_sweep else None
+
     line = None
     if rank == 0:
         cpu = None
@@ -473,7 +505,8 @@ def run_flowmoe(args):
                              "frac": round(gu_tflops / tfl_sus, 4), "traffic": traffic,
                              "peak_kind": f"{peak_kind} bf16 sustained"},
                 "stages_ms": stage_ms, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
-                "cpu_baseline": cpu, "sweep": sw}
+                "cpu_baseline": cpu, "sweep": sw,
+                **({"stack_c36_T64_ep": ep_stack} if ep_stack else {})}
         print(json.dumps(line), flush=True)
     barrier(world)
     if world > 1:

@@ -147,6 +147,12 @@ FM_API int fm_moe_layer_norm(const fm_layer* L, const float* x, const uint16_t* 
                              int32_t t_real, float* out, int32_t* idx, float* w, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* The post-attention RMSNorm alone (the first stage of fm_moe_layer_norm): xb [T, H] bf16 = bf16(x / rms(x)
+ * * w), fp64 reduction, as Core::rmsnorm_host (src/open_qwen36/core.cpp:3014-3044, groups = 1). For
+ * callers that feed the normalised rows to another entry point, e.g. fm_ep_peer_layer with res = x. */
+FM_API int fm_rmsnorm_bf16(const float* x, const uint16_t* norm_w, float eps, int32_t T, int32_t H, uint16_t* xb,
+                           void* stream);
+
 /* The dispatch stage alone: per local expert counts [e_local], exclusive offsets [e_local + 1] (the
  * last = routed pair count), pos [t_real, k] = row of each (token, slot) pair in the expert-sorted
  * order (-1 for an id outside the local range) and pair [offsets[e_local]] = its inverse (t * k + s).

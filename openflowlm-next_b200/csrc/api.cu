@@ -609,6 +609,21 @@ extern "C" FM_API int fm_moe_layer_norm(const fm_layer* L, const float* x, const
     return moe_layer_xb(L, xb, x, T, t_real, out, idx, w, workspace, lo, st);
 }
 
+extern "C" FM_API int fm_rmsnorm_bf16(const float* x, const uint16_t* norm_w, float eps, int32_t T, int32_t H,
+                                       uint16_t* xb, void* stream) {
+    g_err[0] = 0;
+    if (T < 0 || H <= 0 || H % 4 || !(eps >= 0.f) || (T > 0 && (!x || !norm_w || !xb))) {
+        set_error("fm_rmsnorm_bf16: T=%d H=%d (H %% 4 == 0), eps, and non-null buffers needed", T, H);
+        return FM_EINVAL_SHAPE;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(norm_w) & 7) ||
+        (reinterpret_cast<uintptr_t>(xb) & 7)) {
+        set_error("fm_rmsnorm_bf16: x must be 16-byte aligned, norm_w and xb 8-byte aligned");
+        return FM_EINVAL_SHAPE;
+    }
+    return launch_rmsnorm_bf16(x, norm_w, eps, T, H, xb, (cudaStream_t)stream);
+}
+
 extern "C" FM_API int fm_moe_layer(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, int32_t T,
                             int32_t t_real, float* out, int32_t* idx, float* w, void* workspace, size_t workspace_bytes,
                             void* stream) {

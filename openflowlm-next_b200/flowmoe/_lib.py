@@ -54,6 +54,7 @@ SIGNATURES = {
     "fm_version": [ctypes.c_char_p, SZ],
     "fm_q4_1_to_tiles": [P, I32, I32, P, P],
     "fm_pool_to_q4_1": [P, I32, I32, I32, I32, P, P, P],
+    "fm_rmsnorm_bf16": [P, P, ctypes.c_float, I32, I32, P, P],
     "fm_tiles_to_q4_1": [P, I32, I32, P, P],
     "fm_gate_up_to_tiles": [P, P, I32, I32, P, P],
     "fm_tiles_narrow_scales": [P, ctypes.c_int64, P],

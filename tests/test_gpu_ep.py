@@ -277,3 +277,71 @@ def test_ep_peer_absent_rank_times_out(tmp_path):
     res = _run_peer("absent", tmp_path)
     assert res[0]["ok"], res[0]
     assert "FM_ETIMEOUT" in res[0]["error"], res[0]
+
+
+def _stack_worker(rank, world, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    sys.path[:0] = [str(ROOT), str(ROOT / "openflowlm-next_b200")]
+    result = {"rank": rank}
+    import torch.distributed as dist
+    stack = None
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        from flowmoe.stack import EPMoEStack
+        rng = np.random.default_rng(77)
+        cs, layers, nws = [], [], []
+        for l in range(3):
+            c = cases.make_case(H=512, E=32, F=256, FS=256, k=8, T=64, seed=400 + l)
+            c["norm_w"] = OM.bf16_round((1.0 + rng.normal(0, 0.01, c["H"])).astype(np.float32))
+            cs.append(c)
+            layers.append(_rank_layer(c, rank, world, dev).layer)
+            nws.append(torch.from_numpy(c["norm_w"]))
+        n = 64 // world
+        lo, hi = rank * n, (rank + 1) * n
+        x0 = cs[0]["res"][lo:hi]
+        want = OM.moe_stack_f64(x0, cs)
+        stack = EPMoEStack(layers, nws, t_cap=n, timeout_ms=5000)
+        x = torch.from_numpy(x0).to(dev).contiguous()
+        errs = []
+        got = stack.forward(x)
+        stack.check()
+        errs.append(float(np.abs(got.cpu().numpy() - want).max() / np.abs(want - x0).max()))
+        stack.capture(n)
+        for _ in range(2):       # graph replays: the epochs keep advancing on the device
+            got = stack.forward(x)
+            stack.check()
+            errs.append(float(np.abs(got.cpu().numpy() - want).max() / np.abs(want - x0).max()))
+        result.update(ok=True, errs=errs)
+    except Exception as e:
+        result.update(ok=False, error=f"{type(e).__name__}: {e}", tb=traceback.format_exc()[-3000:])
+    finally:
+        Path(outdir, f"rank{rank}.json").write_text(json.dumps(result))
+        try:
+            if stack is not None:
+                stack.close()
+        finally:
+            if dist.is_initialized():
+                dist.destroy_process_group()
+
+
+def test_ep_stack_two_ranks_matches_oracle(tmp_path):
+    """BASELINE config 5's form, small: three layers of x + MoE(RMSNorm(x)) across two ranks over peer
+    memory (one shared peer group), eager and then as a replayed CUDA graph, against the fp64 oracle stack
+    on each rank's tokens."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.start_processes(_stack_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    deadline = time.monotonic() + 240
+    while not ctx.join(timeout=1):
+        if time.monotonic() > deadline:
+            for p in ctx.processes:
+                p.kill()
+            pytest.fail("stack ranks did not finish within 240 s")
+    for r in range(2):
+        res = json.loads(Path(tmp_path, f"rank{r}.json").read_text())
+        assert res["ok"], res.get("tb")
+        assert max(res["errs"]) < TOL, res
