@@ -18,7 +18,11 @@ rank r holds experts [r * 256 / N, (r + 1) * 256 / N), router and shared expert 
           inside the timed region vs the measured dense bf16 peak (MEASURED_PEAKS.json);
   cpu_baseline the oracle port (NumPy fp32 + BLAS, routing by the reference's own C++ router when
           oracle/_ref is built) on a bounded token sample, rank 0 at N=1;
-  sweep   BASELINE configs 2 (decode T 1..32, HBM GB/s) and 3 (Zipf prefill T 512..8192, TFLOP/s).
+  sweep   BASELINE configs 2 (decode T 1..32, HBM GB/s, 16 token batches per graph replay so the
+          touched experts stream from HBM), 3 (Zipf prefill T 512..8192, TFLOP/s) and 5 on one GPU
+          (48-layer RMSNorm stack, decode T=64, one CUDA graph);
+  stack_c36_T64_ep (N > 1 with --ep-stack) config 5 across the group: 64 decode tokens split over the
+          ranks, each rank's experts of all 48 layers, one CUDA graph per rank, max over ranks.
 --impl reference times only the CPU implementation (rank 0), same metric and unit.
 """
 from __future__ import annotations
@@ -476,7 +480,7 @@ def run_flowmoe(args):
     e2e = {"value": round(T * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
            "h2d_bytes_per_step": x.numel() * 2 + res.numel() * 4, "d2h_bytes_per_step": oh.numel() * 4}
 
-    ep_stack = ep_stack_measure(rank, world, args) if world > 1 and args.ep == "peer" and not args.no_sweep else None
+    ep_stack = ep_stack_measure(rank, world, args) if world > 1 and args.ep == "peer" and args.ep_stack else None
 
     line = None
     if rank == 0:
@@ -545,6 +549,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="N > 1: the expert-parallel exchange (peer-memory stores, or NCCL all-to-all)")
+    ap.add_argument("--ep-stack", action="store_true",
+                    help="N > 1: also time BASELINE config 5 (48-layer stack, 64 decode tokens) across the group")
     ap.add_argument("--profile-case", choices=["decode", "decode1", "prefill"], default=None,
                     help="run a few plain layer calls for an ncu capture and exit")
     args = ap.parse_args()
