@@ -627,7 +627,9 @@ static int sm_count_decode() {
     return n;
 }
 
+// Past 32 tokens there are items enough for every CTA slot, and no K split (no partial-sum buffer).
 int gemv_chunk_cap(int T) {
+    if (T > 32) return 1;
     const int cap = T <= 4 ? 16 : 64 / T;
     return cap < 2 ? 2 : cap;
 }

@@ -204,6 +204,16 @@ def test_gemv_decode_c36(dev, T):
     assert _rel(out, ref, c["res"]) < TOL
 
 
+@pytest.mark.parametrize("T", [48, 128])
+def test_auto_path_past_32_tokens(dev, T):
+    """48 and 128 tokens on the size default: the GEMV path (up to T * k = 1024 pairs, one dispatch CTA)
+    without K chunks; 128 x 8 = 1024 pairs is the largest GEMV call; shared expert on."""
+    c = cases.make_case(H=2048, E=64, F=512, FS=512, k=8, T=T, seed=40 + T)
+    layer, x, res, idx, w, out = _run_block(c, dev, path="auto")
+    ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
+    assert _rel(out, ref, c["res"]) < TOL
+
+
 def test_gemv_split_k_small_layer(dev):
     """Few active bands: the GEMV splits K (4 chunks for gate/up, 2 for down) and the last chunk in
     reduces them; shared expert on."""
