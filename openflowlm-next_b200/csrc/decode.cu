@@ -33,41 +33,34 @@ namespace fm {
 constexpr int kGemvRows = 8;        // sorted rows (tokens) per GEMV item
 constexpr int kDispSmallThreads = 1024;
 
-// Block-wide (1024 threads) exclusive scan / sum of one int per thread; sh holds 32 ints.
-__device__ int block_exclusive_scan_1024(int v, int* sh) {
+// Block-wide (1024 threads) exclusive scan of two ints per thread (x and y scanned independently) and
+// their block totals; sh holds 64 ints.
+__device__ int2 block_exclusive_scan2_1024(int2 v, int* sh, int2* tot) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int x = v;
+    int2 x = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
+        const int ya = __shfl_up_sync(0xffffffffu, x.x, o), yb = __shfl_up_sync(0xffffffffu, x.y, o);
+        if (lane >= o) { x.x += ya; x.y += yb; }
     }
     __syncthreads();
-    if (lane == 31) sh[warp] = x;
+    if (lane == 31) { sh[warp] = x.x; sh[32 + warp] = x.y; }
     __syncthreads();
     if (warp == 0) {
-        int s = sh[lane];
+        int sa = sh[lane], sb = sh[32 + lane];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, s, o);
-            if (lane >= o) s += y;
+            const int ya = __shfl_up_sync(0xffffffffu, sa, o), yb = __shfl_up_sync(0xffffffffu, sb, o);
+            if (lane >= o) { sa += ya; sb += yb; }
         }
-        sh[lane] = s;
+        sh[lane] = sa;
+        sh[32 + lane] = sb;
     }
     __syncthreads();
-    const int r = (warp ? sh[warp - 1] : 0) + x - v;
+    const int2 r = make_int2((warp ? sh[warp - 1] : 0) + x.x - v.x, (warp ? sh[31 + warp] : 0) + x.y - v.y);
+    *tot = make_int2(sh[31], sh[63]);
     __syncthreads();
     return r;
-}
-
-__device__ int block_sum_1024(int v, int* sh) {
-    const int ex = block_exclusive_scan_1024(v, sh);
-    __shared__ int tot;
-    if (threadIdx.x == 1023) tot = ex + v;
-    __syncthreads();
-    const int t = tot;
-    __syncthreads();
-    return t;
 }
 
 // K chunks per item: the smallest divisor of the slab counts (at least two slabs per chunk, at most
@@ -94,8 +87,8 @@ __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
     extern __shared__ int sm[];
     int* cnt = sm;                                  // [e_local]
     int* wcnt = cnt + e_local;                      // [32][e_local]
-    int* scan_sh = wcnt + 32 * e_local;             // [32]
-    int* off_s = scan_sh + 32;                      // [e_local + 1] group row offsets
+    int* scan_sh = wcnt + 32 * e_local;             // [64]
+    int* off_s = scan_sh + 64;                      // [e_local + 1] group row offsets
     int* gu0 = off_s + e_local + 1;                 // [e_local + 2] first GEMV slot of each group (gate/up)
     int* dn0 = gu0 + e_local + 2;                   // [e_local + 2] (down)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -167,7 +160,7 @@ __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
         __syncthreads();
     }
     if (e >= 0) {
-        const int b = offsets[e] + wcnt[warp * e_local + e] + rank;
+        const int b = off_s[e] + wcnt[warp * e_local + e] + rank;
         pos[p] = b;
         pair[b] = p;
     } else if (p < P) {
@@ -185,10 +178,11 @@ __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
         tt = (c_g + kGemvRows - 1) / kGemvRows;
     }
     const int bgu = tt * bands_g, bdn = tt * dn_bands;
-    const int tot_gu = block_sum_1024(bgu, scan_sh), tot_dn = block_sum_1024(bdn, scan_sh);
+    int2 tot;
+    const int2 slot = block_exclusive_scan2_1024(make_int2(bgu, bdn), scan_sh, &tot);
+    const int tot_gu = tot.x, tot_dn = tot.y, slot_gu = slot.x, slot_dn = slot.y;
     const int kc_gu = choose_chunks(tot_gu, gu_slabs, 0, kc_cap, target);
     const int kc_dn = choose_chunks(tot_dn, dn_slabs, shared_rows > 0 ? dn_slabs_shared : 0, kc_cap, target);
-    const int slot_gu = block_exclusive_scan_1024(bgu, scan_sh), slot_dn = block_exclusive_scan_1024(bdn, scan_sh);
     if (gi <= G) {
         gu0[gi] = gi < G ? slot_gu : tot_gu;
         dn0[gi] = gi < G ? slot_dn : tot_dn;
@@ -638,7 +632,7 @@ int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, i
                           int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
                           int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int kc_cap,
                           int* done, int* err, cudaStream_t st) {
-    const size_t sm = (size_t)(e_local * 33 + 32 + 3 * (e_local + 2)) * 4;
+    const size_t sm = (size_t)(e_local * 33 + 64 + 3 * (e_local + 2)) * 4;
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(dispatch_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);

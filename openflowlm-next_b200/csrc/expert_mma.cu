@@ -144,42 +144,48 @@ __global__ void combine_kernel(const float* __restrict__ res, const YT* __restri
     __shared__ int srow[kMaxTopK];
     __shared__ float sw[kMaxTopK];
     __shared__ int n_sel;
-    if (threadIdx.x == 0) {
-        int n = 0;
-        if (t < t_real) {
-            // insertion order by expert id (ascending), the visit order of core.cpp:5163-5165
-            int ord[kMaxTopK], ids[kMaxTopK];
-            for (int s = 0; s < k; ++s) {
-                const int e = idx[(size_t)t * k + s];
-                int j = n;
-                while (j > 0 && ids[j - 1] > e) { ids[j] = ids[j - 1]; ord[j] = ord[j - 1]; --j; }
-                ids[j] = e;
-                ord[j] = s;
-                ++n;
-            }
-            int m = 0;
-            for (int j = 0; j < n; ++j) {
-                const int p = pos[(size_t)t * k + ord[j]];
-                if (p >= 0) { srow[m] = p; sw[m] = w[(size_t)t * k + ord[j]]; ++m; }
-            }
-            n = m;
+    const int i = blockIdx.y * blockDim.x + threadIdx.x;   // float4 column group
+    const bool col = i < H / 4;
+    // the residual and shared-expert loads are issued before the pair lists are read
+    float4 o = col ? reinterpret_cast<const float4*>(res + (size_t)t * H)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 vs = make_float4(0.f, 0.f, 0.f, 0.f);
+    float g = 0.f;
+    if (col && shared_on && t < t_real) {
+        vs = ld_y4(y, (size_t)(P + t), H, i);
+        g = sgate[t];
+    }
+    if (threadIdx.x < 32) {
+        // lane s < k holds slot s; its place in ascending expert order (ties by slot: the visit order of
+        // core.cpp:5163-5165) among the slots routed here (pos >= 0) comes from k shuffles
+        const int lane = threadIdx.x;
+        const bool on = t < t_real && lane < k;
+        const int e = on ? idx[(size_t)t * k + lane] : 0x7fffffff;
+        const int p = on ? pos[(size_t)t * k + lane] : -1;
+        const float ww = on ? w[(size_t)t * k + lane] : 0.f;
+        const bool sel = on && p >= 0;
+        int m = 0;
+        for (int j = 0; j < k; ++j) {
+            const int ej = __shfl_sync(0xffffffffu, e, j);
+            const int sj = __shfl_sync(0xffffffffu, sel ? 1 : 0, j);
+            if (sj && (ej < e || (ej == e && j < lane))) ++m;
         }
-        n_sel = n;
+        const unsigned bal = __ballot_sync(0xffffffffu, sel);
+        if (sel) {
+            srow[m] = p;
+            sw[m] = ww;
+        }
+        if (lane == 0) n_sel = __popc(bal);
     }
     __syncthreads();
     const int n = n_sel;
-    const int i = blockIdx.y * blockDim.x + threadIdx.x;   // float4 column group
-    if (i >= H / 4) return;
-    float4 o = reinterpret_cast<const float4*>(res + (size_t)t * H)[i];
+    if (!col) return;
     if (t < t_real) {
-        float4 v[kMaxTopK + 1];
+        float4 v[kMaxTopK];
 #pragma unroll
         for (int j = 0; j < kMaxTopK; ++j)
             if (j < n) v[j] = ld_y4(y, (size_t)srow[j], H, i);
-        if (shared_on) v[kMaxTopK] = ld_y4(y, (size_t)(P + t), H, i);
         if (shared_on) {
-            const float g = sgate[t];
-            o.x += g * v[kMaxTopK].x; o.y += g * v[kMaxTopK].y; o.z += g * v[kMaxTopK].z; o.w += g * v[kMaxTopK].w;
+            o.x += g * vs.x; o.y += g * vs.y; o.z += g * vs.z; o.w += g * vs.w;
         }
 #pragma unroll
         for (int j = 0; j < kMaxTopK; ++j)

@@ -217,18 +217,35 @@ __global__ void router_topk_kernel(float* __restrict__ logits, int ld, const flo
     }
 }
 
-// The same result for E <= 256 and unsplit logits, with each lane's (up to 8) probabilities kept in
-// registers: one exp per expert, then k rounds of (lane max, warp arg-max).
+// Logit e of a token row lg summed over the ks K chunks (chunk stride zs) in chunk order, every chunk's
+// load issued before the first add.
+template <bool SPLIT>
+__device__ __forceinline__ float chunk_sum(const float* lg, size_t zs, int ks, int e) {
+    if (!SPLIT) return lg[e];
+    float part[kMaxKSplit];
+#pragma unroll
+    for (int z = 0; z < kMaxKSplit; ++z) part[z] = z < ks ? lg[(size_t)z * zs + e] : 0.f;
+    float v = part[0];
+#pragma unroll
+    for (int z = 1; z < kMaxKSplit; ++z)
+        if (z < ks) v += part[z];
+    return v;
+}
+
+// The same result for E <= 256, with each lane's (up to 8) probabilities kept in registers: the ks K
+// chunks summed in chunk order (as above), one exp per expert, then k rounds of (lane max, warp arg-max).
 // gate_row (bf16 [H], or NULL): the shared-gate logit is not in the logits rows but computed here as
 // the f32 dot product of the token's bf16 row xb[t] with it (the cuBLAS path leaves the odd row out
 // of the GEMM so that its output stays 16-byte aligned).
-__global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, const float* __restrict__ bias, int T,
-                                    int E, int k, float* __restrict__ probs, int32_t* __restrict__ idx,
+template <bool SPLIT>
+__global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, int ks, const float* __restrict__ bias,
+                                    int T, int E, int k, float* __restrict__ probs, int32_t* __restrict__ idx,
                                     float* __restrict__ w, float* __restrict__ sgate, const uint16_t* __restrict__ xb,
                                     const uint16_t* __restrict__ gate_row, int H) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
     const float* lg = logits + (size_t)warp * ld;
+    const size_t zs = (size_t)T * ld;
     float gl = 0.f;
     if (gate_row) {
         if (sgate) {
@@ -245,14 +262,14 @@ __global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, co
             }
             gl = warp_sum(gl);
         }
-    } else {
-        gl = lg[E];
+    } else if (sgate) {
+        gl = chunk_sum<SPLIT>(lg, zs, ks, E);
     }
     float v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int e = lane + 32 * i;
-        v[i] = e < E ? lg[e] + (bias ? bias[e] : 0.f) : -INFINITY;
+        v[i] = e < E ? chunk_sum<SPLIT>(lg, zs, ks, e) + (bias ? bias[e] : 0.f) : -INFINITY;
     }
     float mx = v[0];
 #pragma unroll
@@ -371,7 +388,7 @@ int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias,
     const int ks = router_ksplit(T, H, E);
     const int ld = router_ld(T, E);
     // the register top-k computes the shared-gate logit itself on the cuBLAS path (E rows in the GEMM)
-    const bool topk8 = ks == 1 && E <= 256;
+    const bool topk8 = E <= 256;
     const bool gate_in_topk = topk8 && T >= kRouterBlasMinT;
     const int gemm_rows = gate_in_topk ? E : E + 1;
     if (T >= kRouterBlasMinT) {
@@ -396,8 +413,13 @@ int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias,
         FM_LAUNCH_CHECK("router_logits");
     }
     if (topk8) {
-        router_topk8_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, ld, bias, T, E, k, probs, idx, w, sgate, xb,
-                                                         gate_in_topk ? router + (size_t)E * H : nullptr, H);
+        const uint16_t* gate_row = gate_in_topk ? router + (size_t)E * H : nullptr;
+        if (ks > 1)   // one warp per CTA: each token's ks x (E + 1) partial logits stream into its own SM
+            router_topk8_kernel<true><<<T, 32, 0, st>>>(logits, ld, ks, bias, T, E, k, probs, idx, w, sgate, xb,
+                                                        gate_row, H);
+        else
+            router_topk8_kernel<false><<<(T + 7) / 8, 256, 0, st>>>(logits, ld, ks, bias, T, E, k, probs, idx, w, sgate,
+                                                                    xb, gate_row, H);
         FM_LAUNCH_CHECK("router_topk8");
     } else {
         router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, ld, bias, T, E, k, ks, probs, idx, w, sgate);

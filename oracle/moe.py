@@ -60,16 +60,16 @@ def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float = 1e-6) -> np.ndarray:
     return ((xd / rms) * np.asarray(w, np.float64)).astype(np.float32)
 
 
-def moe_stack_f64(x, layers, eps: float = 1e-6, engine_rounding: bool = True):
+def moe_stack_f64(x, layers, eps: float = 1e-6, engine_rounding: bool = True, y_bf16: bool = False):
     """x_{l+1} = x_l + MoE_l(RMSNorm_l(x_l)) over a list of layers, each a dict with ``norm_w``, ``Wr``,
     ``gate``, ``up``, ``down``, ``shared``, ``k`` (the staged_tail -> ffn_block sequence of
-    ``core.cpp:4934-4957`` repeated per layer; ``replica.py:121-143``)."""
+    ``core.cpp:4934-4957`` repeated per layer; ``replica.py:121-143``). ``y_bf16``: see ``moe_block_f64``."""
     x = np.asarray(x, np.float32)
     for L in layers:
         xm = rmsnorm(x, L["norm_w"], eps)
         _, idx, w = router_block(bf16_round(xm), L["Wr"], L["k"])
         x = moe_block_f64(xm, x, idx, w, L["gate"], L["up"], L["down"], shared=L["shared"],
-                          engine_rounding=engine_rounding).astype(np.float32)
+                          engine_rounding=engine_rounding, y_bf16=y_bf16).astype(np.float32)
     return x
 
 
@@ -152,7 +152,7 @@ def shared_gate(xm: np.ndarray, sgw: np.ndarray, round_x: bool = True) -> np.nda
 
 
 def moe_block_f64(xm, res, idx, w, gate_blocks, up_blocks, down_blocks, t_real=None, shared=None,
-                  engine_rounding: bool = True):
+                  engine_rounding: bool = True, y_bf16: bool = False):
     """out [T, H] = res + (shared) + sum over each token's experts, ascending expert order, fp64.
 
     ``gate_blocks[e]`` etc. are GGUF Q4_1 blocks (uint8[rows, K/32, 20]). ``shared`` is None or
@@ -160,6 +160,9 @@ def moe_block_f64(xm, res, idx, w, gate_blocks, up_blocks, down_blocks, t_real=N
     (``core.cpp:5155``, ``:3697``). This is ``open_kernels/model/replica.py:131-143`` over T tokens
     with the engine's dispatch order and rounding points; ``engine_rounding=False`` drops the two
     bf16 rounding points (x at the gather, h before down) and is then replica.py's fp64 math.
+    ``y_bf16=True`` adds the rounding point of this build's expert-parallel paths, whose routed y rows
+    travel between ranks as bf16 (the reference keeps them in f32, ``moe_acc.cc``): each (token, expert)
+    y row is rounded to bf16 before the weighted combine; the shared expert's row is not.
     """
     xm = np.asarray(xm, np.float32)
     T, H = xm.shape
@@ -181,6 +184,8 @@ def moe_block_f64(xm, res, idx, w, gate_blocks, up_blocks, down_blocks, t_real=N
         toks = pair[lo:hi] // k
         y_pairs[lo:hi] = expert_ffn_f64(xb[toks], dequant_q4_1(gate_blocks[e]), dequant_q4_1(up_blocks[e]),
                                         dequant_q4_1(down_blocks[e]), engine_rounding)
+    if y_bf16:
+        y_pairs = bf16_round(y_pairs.astype(np.float32)).astype(np.float64)
     wf = np.asarray(w, np.float64)
     for t in range(t_real):
         order = np.argsort(idx[t], kind="stable")          # ascending expert, as the visit order

@@ -171,3 +171,31 @@ def test_pool_packers_match_reference_bytes(golden):
     b16 = OQ.pool_to_blocks(g["pool_bf16_rs2"], 64, 256, 2, 5120)
     assert np.array_equal(b16[..., 4:], b[..., 4:])
     assert np.array_equal(OQ.dequant_q4_1(b16), g["dequant_bf16_scales"])
+
+
+def test_ep_stack_case_flips_only_through_bf16_y():
+    """The expert-parallel paths carry routed y rows between ranks as bf16, an extra rounding point the
+    oracle models with ``y_bf16``. On the two-rank stack case of tests/test_gpu_ep.py that rounding alone
+    moves rank 1's output by about 5 % of the stack's update: one token there sits 4e-6 from a top-k tie
+    in the third layer and changes an expert. Rank 0 has no such token, and one layer (no compounding)
+    stays within the rounding itself."""
+    from oracle import cases
+    rng = np.random.default_rng(77)
+    cs = []
+    for l in range(3):
+        c = cases.make_case(H=512, E=32, F=256, FS=256, k=8, T=64, seed=400 + l)
+        c["norm_w"] = OM.bf16_round((1.0 + rng.normal(0, 0.01, c["H"])).astype(np.float32))
+        cs.append(c)
+    rel = []
+    for lo, hi in ((0, 32), (32, 64)):
+        x0 = cs[0]["res"][lo:hi]
+        a, b = OM.moe_stack_f64(x0, cs), OM.moe_stack_f64(x0, cs, y_bf16=True)
+        rel.append(float(np.abs(a - b).max() / np.abs(a - x0).max()))
+    assert rel[0] < 2e-3 and rel[1] > 2e-2, rel
+    # one layer: bf16 y rows change the block output by no more than their own rounding
+    c = cs[0]
+    xm = OM.rmsnorm(c["res"], c["norm_w"])
+    _, idx, w = OM.router_block(OM.bf16_round(xm), c["Wr"], c["k"])
+    a = OM.moe_block_f64(xm, c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
+    b = OM.moe_block_f64(xm, c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"], y_bf16=True)
+    assert np.abs(a - b).max() <= 2.0 ** -8 * np.abs(a - c["res"]).max()
