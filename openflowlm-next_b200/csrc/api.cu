@@ -6,7 +6,9 @@
 #include <cstdio>
 #include <cstring>
 
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -17,6 +19,35 @@ static thread_local char g_err[512];
 static std::atomic<unsigned long long> g_launches{0};
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int device_sm_count() {
+    constexpr int kDevs = 64;
+    static std::atomic<int> cache[kDevs] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+    if (dev < kDevs) {
+        const int c = cache[dev].load(std::memory_order_relaxed);
+        if (c > 0) return c;
+    }
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    if (dev < kDevs) cache[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
+cudaError_t raise_smem_limit(const void* func, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<int, const void*>, int> limit;   // the largest limit set so far
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    int& cur = limit[std::make_pair(dev, func)];
+    if (bytes <= cur) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) cur = bytes;
+    return e;
+}
 
 // Stage profiler: pairs of timing events recorded around each stage while enabled; read back (and
 // summed per stage) by fm_profile_read. Events are created when profiling is first enabled.
@@ -101,6 +132,10 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 struct SideStream {
     cudaStream_t s = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
+    // Held while one call enqueues its side work, so that another host thread cannot re-record `fork`
+    // between this call's record and the side stream's wait on it. (A later `join` record only makes a
+    // waiter wait for more of the side stream's FIFO work, never for less.)
+    std::mutex enqueue;
 };
 
 static SideStream* side_stream() {
@@ -317,17 +352,6 @@ static int run_block_gemv(const fm_layer* L, const uint16_t* xb, const float* re
     return rc;
 }
 
-static int sm_count_api() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 // The shared expert as its own pair of tcgen05 launches on the side stream (forked from st at this
 // point): gate_up over x rows [0, t_real) straight from xb, h into h_rows, down adding
 // sgate * y into out. Leaves `spare_sms` SMs to the work that runs beside it. Records side->join.
@@ -335,6 +359,7 @@ static int launch_shared_side(const fm_layer* L, const uint16_t* xb, const float
                               int* gu_list, int* dn_list, uint16_t* h_rows, int h_ld, int bdiv, int spare_sms, int* err,
                               SideStream* side, cudaStream_t st) {
     const int H = L->hidden, El = L->e_local;
+    std::lock_guard<std::mutex> lock(side->enqueue);
     cudaStream_t s2 = side->s;
     if (cudaEventRecord(side->fork, st) != cudaSuccess || cudaStreamWaitEvent(s2, side->fork, 0) != cudaSuccess)
         return cuda_status(cudaGetLastError(), "fork the shared expert");
@@ -344,7 +369,7 @@ static int launch_shared_side(const fm_layer* L, const uint16_t* xb, const float
     const int rt = (T + kBNTc - 1) / kBNTc;
     TcLaunch g{};
     g.max_items = rt * (L->shared_ffn / 64);
-    g.max_ctas = spare_sms > 0 ? sm_count_api() - spare_sms : 0;
+    g.max_ctas = spare_sms > 0 ? device_sm_count() - spare_sms : 0;
     g.list = gu_list;
     g.act = xb;
     g.act_rows = T;
@@ -1180,7 +1205,7 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     prof_end(kStageDispatch, st);
     prof_begin(kStageGather, st);
     if ((rc = launch_ep_scatter_rows(a, xb, at<int>(workspace, lo.pair), ids, offsets, at<int>(workspace, lo.send_base), P,
-                                     0, sm_count_api(), st)))
+                                     0, device_sm_count(), st)))
         return rc;
     if ((rc = launch_ep_wait(a, 1, st))) return rc;
     prof_end(kStageGather, st);

@@ -24,6 +24,13 @@ int cuda_status(cudaError_t e, const char* what);
 // Kernel launches made by this library in this process (reported by fm_launch_count).
 void note_launch();
 
+// SMs of the current device (cached per device).
+int device_sm_count();
+
+// Raises a kernel's dynamic shared-memory limit on the current device to at least `bytes` (never
+// lowers it): the attribute is per device; a mutex makes concurrent first calls safe.
+cudaError_t raise_smem_limit(const void* func, int bytes);
+
 // Launch-error check after each kernel launch: counts the launch, returns FM_ECUDA with the message
 // of the last launch error.
 #define FM_LAUNCH_CHECK(what)                                        \

@@ -610,17 +610,6 @@ __global__ void __launch_bounds__(GV_THREADS, GV_CTAS_PER_SM) gemv_kernel(GemvAr
 }
 
 // ------------------------------------------------------------------ launchers
-static int sm_count_decode() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 // Past 32 tokens there are items enough for every CTA slot, and no K split (no partial-sum buffer).
 int gemv_chunk_cap(int T) {
     if (T > 32) return 1;
@@ -633,12 +622,8 @@ int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, i
                           int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int kc_cap,
                           int* done, int* err, cudaStream_t st) {
     const size_t sm = (size_t)(e_local * 33 + 64 + 3 * (e_local + 2)) * 4;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(dispatch_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        attr = true;
-    }
-    const int target = GV_CTAS_PER_SM * sm_count_decode();   // one item per CTA slot
+    if (cudaError_t e = raise_smem_limit((const void*)dispatch_small_kernel, (int)sm)) return cuda_status(e, "dispatch_small smem");
+    const int target = GV_CTAS_PER_SM * device_sm_count();   // one item per CTA slot
     dispatch_small_kernel<<<1, kDispSmallThreads, sm, st>>>(idx, P, e_begin, e_local, shared_base, shared_rows, counts,
                                                            offsets, pos, pair, gu_list, gu_bands, gu_bands_shared,
                                                            gu_slabs, dn_list, dn_bands, dn_slabs, dn_slabs_shared, kc_cap,
@@ -675,23 +660,14 @@ int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st) {
     a.dn_list = L.dn_list;
     a.y_rows = L.y_rows;
     a.err = L.err;
-    const int slots = GV_CTAS_PER_SM * sm_count_decode();
+    const int slots = GV_CTAS_PER_SM * device_sm_count();
     const int grid = L.max_items < slots ? L.max_items : slots;
-    if (gate_up) {
-        static bool attr = false;
-        if (!attr) {
-            cudaFuncSetAttribute(gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GvSmem::total);
-            attr = true;
-        }
+    const void* fn = gate_up ? (const void*)gemv_kernel<true> : (const void*)gemv_kernel<false>;
+    if (cudaError_t e = raise_smem_limit(fn, GvSmem::total)) return cuda_status(e, "gemv smem");
+    if (gate_up)
         gemv_kernel<true><<<grid, GV_THREADS, GvSmem::total, st>>>(a);
-    } else {
-        static bool attr = false;
-        if (!attr) {
-            cudaFuncSetAttribute(gemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GvSmem::total);
-            attr = true;
-        }
+    else
         gemv_kernel<false><<<grid, GV_THREADS, GvSmem::total, st>>>(a);
-    }
     FM_LAUNCH_CHECK(gate_up ? "gemv<gate_up>" : "gemv<down>");
     return FM_OK;
 }

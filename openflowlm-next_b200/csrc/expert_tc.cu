@@ -613,25 +613,10 @@ static int make_bmap(CUtensorMap* m, const uint16_t* base, int rows, int cols, i
     return FM_OK;
 }
 
-static int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 template <bool GATE_UP, bool PAIR>
 static cudaError_t launch_tc_variant(const CUtensorMap& bmap, const CUtensorMap& bmap_big, const TcArgs& a, int grid,
                                      int sm, cudaStream_t st) {
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(expert_tc_kernel<GATE_UP, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-        attr = true;
-    }
+    if (cudaError_t e = raise_smem_limit((const void*)expert_tc_kernel<GATE_UP, PAIR>, sm)) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(TcRoles<GATE_UP>::THREADS);
@@ -674,7 +659,7 @@ int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
     a.meta = L.meta;
     for (int i = 0; i < kMaxRanks; ++i) a.yret[i] = L.yret[i];
     a.err = L.err;
-    int sms = sm_count();
+    int sms = device_sm_count();
     if (L.max_ctas > 0 && L.max_ctas < sms) sms = L.max_ctas;
     const int sm_single = TcSmem<false>::total, sm_pair = TcSmem<true>::total;
     cudaError_t e;
