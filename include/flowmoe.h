@@ -4,6 +4,11 @@
  * Every entry point takes plain device pointers, sizes and a cudaStream_t (passed as void*), returns
  * an int status (FM_OK or an FM_E* code) and never throws. fm_last_error() returns the message of the
  * calling thread's last failure. No entry point synchronises the stream unless its comment says so.
+ * Threads: entry points may be called from several host threads; per-device library state (the
+ * shared-expert side stream, the router's cuBLAS handle) is guarded while work is enqueued. Calls on
+ * two streams of one device serialise their tensor-core shared-expert work on the device's side stream,
+ * and must not run the cuBLAS router (T >= 256 tokens) at the same time: its workspace is per device.
+ * Separate devices, and the decode path (T <= 128 tokens), have no such limit.
  *
  * Weights live on the device in the "tile" layout produced by fm_q4_1_to_tiles() from GGUF Q4_1
  * blocks (the reference's open_kernels/q4_1_pack.py:1-14 block format: fp16 d | fp16 m | 16 nibble

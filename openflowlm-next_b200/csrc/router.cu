@@ -25,13 +25,15 @@ struct BlasState {
 };
 
 // One handle per device, with a fixed 32 MiB workspace so that later calls (and stream capture) never
-// allocate. Created on the first large-T call.
-static cublasHandle_t blas_handle(cudaStream_t st) {
+// allocate. Created on the first large-T call. Returns with `lock` held: the handle's stream is set for
+// this caller, and the caller enqueues its GEMM before releasing it, so that another host thread cannot
+// retarget the shared handle in between.
+static cublasHandle_t blas_handle(cudaStream_t st, std::unique_lock<std::mutex>& lock) {
     static BlasState dev_state[64];
     static std::mutex mu;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    std::lock_guard<std::mutex> lock(mu);
+    lock = std::unique_lock<std::mutex>(mu);
     BlasState& b = dev_state[dev];
     if (!b.h) {
         constexpr size_t kWs = size_t(32) << 20;
@@ -393,7 +395,8 @@ int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias,
     const int gemm_rows = gate_in_topk ? E : E + 1;
     if (T >= kRouterBlasMinT) {
         // logits (row-major [T, E+1]) = xb [T, H] . router [E+1, H]^T, as column-major C = op(A) op(B)
-        cublasHandle_t h = blas_handle(st);
+        std::unique_lock<std::mutex> blas_lock;
+        cublasHandle_t h = blas_handle(st, blas_lock);
         if (!h) {
             set_error("cuBLAS handle for the router GEMM could not be created");
             return FM_ECUDA;
