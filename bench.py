@@ -181,13 +181,11 @@ def cpu_baseline(layer_blocks, cfg, x, res, budget_s=20.0, threads=None):
     rs = res.cpu().numpy()
     n, done, t0 = 64, 0, time.perf_counter()
     while True:
-        s0 = time.perf_counter()
         port.forward(xs[done % len(xs):done % len(xs) + n], rs[done % len(rs):done % len(rs) + n])
         done += n
         if time.perf_counter() - t0 > budget_s or done >= len(xs):
             break
     dt = time.perf_counter() - t0
-    del s0
     return done / dt, cores, f"{done} of {len(xs)} tokens of the same layer, NumPy fp32 + BLAS ({cores} threads)"
 
 
