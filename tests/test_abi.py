@@ -87,3 +87,21 @@ def test_pool_import_bad_geometry_is_rejected(n, k, rs, chunk):
                                   ctypes.cast(bad, ctypes.c_void_p), None)
     assert rc == _lib.FM_EINVAL_SHAPE
     assert "fm_pool_to_q4_1" in _lib.last_error()
+
+
+def test_empty_calls_are_no_ops():
+    # T = 0 tokens: every entry point returns FM_OK before any device work, with no workspace at all
+    from flowmoe import _lib
+    L = ctypes.byref(_layer())
+    assert _lib.lib.fm_router_topk(L, None, 0, 0, None, None, None, None, None, 0, None) == 0
+    assert _lib.lib.fm_moe_block(L, None, 0, None, None, None, None, 0, 0, None, None, 0, None) == 0
+    assert _lib.lib.fm_moe_layer(L, None, 0, None, 0, 0, None, None, None, None, 0, None) == 0
+    assert _lib.lib.fm_moe_dispatch(L, None, 0, 0, None, None, None, None, None, 0, None) == 0
+
+
+@pytest.mark.parametrize("T,t_real", [(16, 17), (16, -1), (-1, 0)])
+def test_token_counts_outside_range_are_rejected(T, t_real):
+    from flowmoe import _lib
+    rc = _lib.lib.fm_moe_block(ctypes.byref(_layer()), None, 0, None, None, None, None, T, t_real, None, None, 0, None)
+    assert rc == _lib.FM_EINVAL_SHAPE
+    assert _lib.last_error()
