@@ -143,7 +143,10 @@ def _bf16(t, device) -> torch.Tensor:
     if isinstance(t, np.ndarray):
         if t.dtype == np.uint16:
             return torch.from_numpy(t.astype(np.int16, copy=False).view(np.int16)).view(torch.bfloat16).to(device)
-        t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
+        a = np.ascontiguousarray(t, np.float32)
+        if not a.flags.writeable:   # e.g. a read-only GGUF memory map: torch wants a writable buffer
+            a = a.copy()
+        t = torch.from_numpy(a)
     return t.to(device=device, dtype=torch.bfloat16).contiguous()
 
 
@@ -211,7 +214,7 @@ class MoELayer:
         sgw_t = None if sgw is None else _bf16(sgw, device).reshape(H)
         call("fm_router_pack", wr.data_ptr(), _ptr(sgw_t), H, cfg.n_experts, router.data_ptr(), _stream(device))
         if router_bias is not None and not isinstance(router_bias, torch.Tensor):
-            router_bias = torch.from_numpy(np.asarray(router_bias, np.float32))
+            router_bias = torch.from_numpy(np.array(router_bias, np.float32))   # a writable copy
         if scales == "bf16":
             for t in (gate_up, down, sgu, sdn):
                 if t is not None:
