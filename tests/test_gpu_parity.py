@@ -160,6 +160,14 @@ def test_moe_block_shared_expert_and_padding(dev, path):
     np.testing.assert_array_equal(out[21:], c["res"][21:])
 
 
+@pytest.mark.parametrize("path", ["mma", "tc", "gemv"])
+def test_moe_block_all_rows_padding(dev, path):
+    """t_real = 0: every row is padding and is carried as res exactly (core.cpp:5155), shared expert off."""
+    c = cases.make_case(H=2048, E=16, F=512, FS=512, k=8, T=16, seed=3)
+    layer, x, res, idx, w, out = _run_block(c, dev, t_real=0, path=path)
+    np.testing.assert_array_equal(out, c["res"])
+
+
 def test_moe_layer_fused_matches_staged(dev):
     c = cases.make_case(H=2048, E=32, F=256, FS=256, k=8, T=40, seed=2)
     layer, x, res, idx, w, out = _run_block(c, dev, path="mma")
