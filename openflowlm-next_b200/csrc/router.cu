@@ -292,8 +292,9 @@ __global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, in
         v[i] *= inv;
         if (probs && lane + 32 * i < E) probs[(size_t)warp * E + lane + 32 * i] = v[i];
     }
-    float ws[kMaxTopK];
-    int ids[kMaxTopK];
+    // lane s keeps slot s's (expert, probability) in registers (k <= 16 < 32)
+    float wsel = 0.f;
+    int isel = 0;
     double wsum = 0.0;
     uint32_t taken = 0;
     for (int s = 0; s < k; ++s) {
@@ -309,16 +310,10 @@ __global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, in
             if (op > bp || (op == bp && oe < be)) { bp = op; be = oe; }
         }
         if ((be & 31) == lane) taken |= 1u << (be >> 5);
-        ids[s] = be;
-        ws[s] = bp;
+        if (lane == s) { isel = be; wsel = bp; }
         wsum += (double)bp;
     }
     if (lane < k) {   // lane s writes slot s
-        float wsel = 0.f;
-        int isel = 0;
-#pragma unroll
-        for (int s = 0; s < kMaxTopK; ++s)
-            if (s == lane) { wsel = ws[s]; isel = ids[s]; }
         idx[(size_t)warp * k + lane] = isel;
         w[(size_t)warp * k + lane] = (float)((double)wsel / wsum);
     }
