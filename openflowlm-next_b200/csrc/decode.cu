@@ -622,7 +622,10 @@ int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, i
                           int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int kc_cap,
                           int* done, int* err, cudaStream_t st) {
     const size_t sm = (size_t)(e_local * 33 + 64 + 3 * (e_local + 2)) * 4;
-    if (cudaError_t e = raise_smem_limit((const void*)dispatch_small_kernel, (int)sm)) return cuda_status(e, "dispatch_small smem");
+    // the limit for the largest group count (e_local < 1024) at once, so no later call (one being
+    // captured into a graph, say) has to raise it again
+    if (cudaError_t e = raise_smem_limit((const void*)dispatch_small_kernel, 160 * 1024))
+        return cuda_status(e, "dispatch_small smem");
     const int target = GV_CTAS_PER_SM * device_sm_count();   // one item per CTA slot
     dispatch_small_kernel<<<1, kDispSmallThreads, sm, st>>>(idx, P, e_begin, e_local, shared_base, shared_rows, counts,
                                                            offsets, pos, pair, gu_list, gu_bands, gu_bands_shared,
