@@ -64,8 +64,10 @@ typedef struct fm_layer {
     int32_t shared_ffn; /* F_s of the always-on shared expert (% 64 == 0); 0 = none */
     int32_t e_begin;    /* first expert held by this rank (expert parallel); 0 on one GPU */
     int32_t e_local;    /* experts held by this rank; E on one GPU */
-    int32_t flags;      /* 0 = pick kernels by size (GEMV up to 32 tokens, tcgen05 from 64, mma.sync between);
-                           1 = force mma.sync, 2 = force tcgen05, 3 = force the GEMV (when T <= 64),
+    int32_t flags;      /* 0 = pick kernels by size (the GEMV up to 128 tokens while T * top_k <= 1024, else
+                           tcgen05 from 64 tokens, mma.sync below);
+                           1 = force mma.sync, 2 = force tcgen05, 3 = force the GEMV (within the same
+                           limits, mma.sync past them),
                            4 = force tcgen05 as CTA pairs (M = 256 MMAs; when every matrix has an
                            even number of 128-row bands, else one CTA per item as with 2) */
     const uint8_t* gate_up;   /* tiles, e_local x (2 x F x H x 5/8 B): gate then up, per expert */

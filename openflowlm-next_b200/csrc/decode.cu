@@ -1,5 +1,5 @@
-// Decode-size path (T <= 32 tokens): single-CTA dispatch that also builds the GEMV work lists, and the
-// bandwidth-bound grouped Q4_1 GEMV.
+// Decode-size path (T <= 128 tokens, T * top_k <= 1024): single-CTA dispatch that also builds the GEMV
+// work lists, and the bandwidth-bound grouped Q4_1 GEMV.
 //
 // GEMV: a work item is (group, 128-row band, up to 8 sorted rows, K chunk). Each SM runs four
 // independent CTAs of one producer warp + four consumer warps. The producer streams the item's slabs

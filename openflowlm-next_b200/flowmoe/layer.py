@@ -170,9 +170,10 @@ class MoELayer:
 
     @property
     def path(self) -> str:
-        """Kernel choice: "auto" (GEMV up to 32 tokens, tcgen05 from 64, mma.sync between), or forced
-        "mma", "tc" (tcgen05, one CTA per item), "tc2" (tcgen05 as CTA pairs where the band counts
-        allow), "gemv" (the GEMV, up to 64 tokens)."""
+        """Kernel choice: "auto" (the GEMV up to 128 tokens while tokens x top_k <= 1024, else tcgen05
+        from 64 tokens and mma.sync below), or forced "mma", "tc" (tcgen05, one CTA per item), "tc2"
+        (tcgen05 as CTA pairs where the band counts allow), "gemv" (the GEMV, within the same limits;
+        mma.sync past them)."""
         return {v: k for k, v in self.PATHS.items()}[self._L.flags]
 
     @path.setter
