@@ -9,15 +9,16 @@ bf16 tokens per GPU. A step is one fm_moe_layer call (router, dispatch, shared +
 combine) over the step's tokens. Weights (503 MB of Q4_1) exceed the 126 MB L2, so every step
 streams them from HBM. With N > 1 GPUs (torchrun, one rank per GPU) the layer is expert parallel:
 rank r holds experts [r * 256 / N, (r + 1) * 256 / N), router and shared expert replicated, its own
-8192 tokens; a step is flowmoe.ep's dispatch -> NCCL all-to-all -> local experts -> all-to-all back
--> combine (weak scaling: the tokens per GPU stay fixed).
+8192 tokens; a step is one fm_ep_peer_layer call: the routed rows go to their experts' ranks as peer
+stores over NVLink, each rank runs its experts, the y rows come back the same way, then the combine
+(--ep nccl: the NCCL all-to-all variant instead); weak scaling, the tokens per GPU stay fixed.
   value   tokens/s of the whole job, inputs resident on the device, CUDA events, max over ranks;
   e2e     the same through the public API with pinned host buffers: x (bf16) and res (f32) copied
           in and out (f32) copied back inside each timed step;
   roofline the dominant kernel (gate_up expert GEMM): algorithmic FLOPs / its event-timed duration
           inside the timed region vs the measured dense bf16 peak (MEASURED_PEAKS.json);
-  cpu_baseline the oracle port (NumPy fp32 + BLAS, routing by the reference's own C++ router when
-          oracle/_ref is built) on a bounded token sample, rank 0 at N=1;
+  cpu_baseline the oracle port (NumPy fp32 + BLAS on all host cores) on a bounded token sample,
+          rank 0 at N=1;
   sweep   BASELINE configs 2 (decode T 1..32, HBM GB/s, 16 token batches per graph replay so the
           touched experts stream from HBM), 3 (Zipf prefill T 512..8192, TFLOP/s) and 5 on one GPU
           (48-layer RMSNorm stack, decode T=64, one CUDA graph);
