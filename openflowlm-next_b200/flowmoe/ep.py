@@ -18,6 +18,10 @@ own tokens. One layer is:
 ``ep_forward`` is the exchange logic alone, over a ``stages`` object that provides steps 1, 3 and
 5: ``DeviceStages`` (libflowmoe on the GPU) in production, a CPU stand-in in the tests, so the
 exchange runs unchanged over gloo ranks on CPU.
+
+``PeerEPMoELayer`` (over a ``PeerGroup``) is the default multi-GPU layer: one ``fm_ep_peer_layer`` call
+does all five steps on the device, the two exchanges being the library's own stores into the owners'
+IPC-mapped buffers over NVLink, synchronised by device flags (no host step, so it can be graph-captured).
 """
 from __future__ import annotations
 
