@@ -254,8 +254,8 @@ FM_API int fm_ipc_free(void* ptr);
  * (the check core.cpp:5159-5160 throws on). */
 FM_API int fm_moe_check(void* workspace, void* stream);
 
-/* Kernel launches this library has made in this process (the driver-visible proof that the device
- * path ran). */
+/* Launches of this library's own kernels in this process (the proof that the device path ran); the
+ * router's cuBLAS GEMM (T >= 256 tokens) is a library kernel and is not counted. */
 FM_API int fm_launch_count(unsigned long long* n);
 
 /* Stage profiler (the reference's OFLM_OPEN_PROFILE stage timings, core.cpp:592-600, :850-935, on

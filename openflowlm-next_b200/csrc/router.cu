@@ -400,7 +400,7 @@ int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias,
         const cublasStatus_t bs = cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, gemm_rows, T, H, &one, router, CUDA_R_16BF, H, xb,
                                                CUDA_R_16BF, H, &zero, logits, CUDA_R_32F, ld, CUBLAS_COMPUTE_32F,
                                                CUBLAS_GEMM_DEFAULT);
-        note_launch();
+        // a library GEMM: not counted by fm_launch_count, which counts this library's own kernels
         if (bs != CUBLAS_STATUS_SUCCESS) {
             set_error("router GEMM (cublasGemmEx) failed: status %d", (int)bs);
             return FM_ECUDA;
