@@ -150,6 +150,33 @@ def _bf16(t, device) -> torch.Tensor:
     return t.to(device=device, dtype=torch.bfloat16).contiguous()
 
 
+def _size(x) -> int:
+    return int(x.numel()) if isinstance(x, torch.Tensor) else int(np.asarray(x).size)
+
+
+def _check_inputs(cfg: MoEConfig, gate_blocks, up_blocks, down_blocks, router_w, shared, router_bias) -> None:
+    """Every host-side size check of MoELayer.from_q4_1, before any device work."""
+    H, F, E = cfg.hidden, cfg.ffn, cfg.local
+    if _size(gate_blocks) != E * cfg.q4_bytes(F, H) or _size(up_blocks) != E * cfg.q4_bytes(F, H):
+        raise ValueError("gate/up blocks do not match [E_local, F, H/32, 20]")
+    if _size(down_blocks) != E * cfg.down_bytes:
+        raise ValueError("down blocks do not match [E_local, H, F/32, 20]")
+    wr_shape = tuple(router_w.shape)
+    if wr_shape != (H, cfg.n_experts):
+        raise ValueError(f"router weight shape {wr_shape} != (H, E) = {(H, cfg.n_experts)}")
+    if shared is not None:
+        if cfg.shared_ffn <= 0:
+            raise ValueError("shared expert weights given but cfg.shared_ffn == 0")
+        sg, su, sd, sgw = shared
+        FS = cfg.shared_ffn
+        if _size(sg) != cfg.q4_bytes(FS, H) or _size(su) != cfg.q4_bytes(FS, H) or _size(sd) != cfg.q4_bytes(H, FS):
+            raise ValueError("shared expert blocks do not match [F_s, H/32, 20] / [H, F_s/32, 20]")
+        if sgw is not None and _size(sgw) != H:
+            raise ValueError(f"shared gate vector has {_size(sgw)} values, not H = {H}")
+    if router_bias is not None and _size(router_bias) != cfg.n_experts:
+        raise ValueError(f"router bias has {_size(router_bias)} values, not E = {cfg.n_experts}")
+
+
 class MoELayer:
     """One Qwen3.6-MoE expert block resident on a B200: router, routed experts, shared expert."""
 
@@ -191,6 +218,7 @@ class MoELayer:
         if scales not in ("fp16", "bf16"):
             raise ValueError(f"scales must be 'fp16' or 'bf16', not {scales!r}")
         H, F, E = cfg.hidden, cfg.ffn, cfg.local
+        _check_inputs(cfg, gate_blocks, up_blocks, down_blocks, router_w, shared, router_bias)
         g = _as_dev_u8(gate_blocks, device).reshape(E, -1)
         u = _as_dev_u8(up_blocks, device).reshape(E, -1)
         if g.shape[1] != cfg.q4_bytes(F, H) or u.shape[1] != cfg.q4_bytes(F, H):

@@ -1,5 +1,7 @@
-"""Host-side pieces of flowmoe checked on the CPU: the torch Q4_1 quantiser against gguf's bytes."""
+"""Host-side pieces of flowmoe checked on the CPU: the torch Q4_1 quantiser against gguf's bytes, and the
+layer's input checks."""
 import numpy as np
+import pytest
 import torch
 
 
@@ -15,3 +17,27 @@ def test_torch_dequant_matches_reference(golden):
     g = golden["q4_1"]
     got = flowmoe.dequantize_q4_1(torch.from_numpy(g["blocks"])).numpy()
     assert np.array_equal(got, g["dequant"])
+
+
+@pytest.mark.parametrize("bad", ["gate", "down", "router", "shared", "sgw", "bias"])
+def test_layer_inputs_checked_before_device_work(bad):
+    # every size check of MoELayer.from_q4_1 runs on the host first: no device is touched here
+    import flowmoe
+    from oracle import cases
+    c = cases.make_case(H=256, E=4, F=128, FS=128, k=2, T=1, seed=0)
+    cfg = flowmoe.MoEConfig(hidden=256, n_experts=4, top_k=2, ffn=128, shared_ffn=128)
+    gate, down, wr, shared, bias = c["gate"], c["down"], c["Wr"], c["shared"], np.zeros(4, np.float32)
+    if bad == "gate":
+        gate = gate[:3]
+    elif bad == "down":
+        down = down[:, :128]
+    elif bad == "router":
+        wr = wr.T
+    elif bad == "shared":
+        shared = (shared[0][:64],) + tuple(shared[1:])
+    elif bad == "sgw":
+        shared = tuple(shared[:3]) + (shared[3][:100],)
+    else:
+        bias = np.zeros(5, np.float32)
+    with pytest.raises(ValueError):
+        flowmoe.MoELayer.from_q4_1(cfg, gate, c["up"], down, wr, shared=shared, device="cpu", router_bias=bias)
