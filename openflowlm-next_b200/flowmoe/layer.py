@@ -221,24 +221,16 @@ class MoELayer:
         _check_inputs(cfg, gate_blocks, up_blocks, down_blocks, router_w, shared, router_bias)
         g = _as_dev_u8(gate_blocks, device).reshape(E, -1)
         u = _as_dev_u8(up_blocks, device).reshape(E, -1)
-        if g.shape[1] != cfg.q4_bytes(F, H) or u.shape[1] != cfg.q4_bytes(F, H):
-            raise ValueError("gate/up blocks do not match [E_local, F, H/32, 20]")
         gate_up = gate_up_to_tiles(g, u, F, H, device)
         down = q4_1_to_tiles(_as_dev_u8(down_blocks, device), H, F, device).reshape(E, -1)
-        if down.shape[1] != cfg.down_bytes:
-            raise ValueError("down blocks do not match [E_local, H, F/32, 20]")
         sgu = sdn = None
         sgw = None
         if shared is not None:
-            if cfg.shared_ffn <= 0:
-                raise ValueError("shared expert weights given but cfg.shared_ffn == 0")
             sg, su, sd, sgw = shared
             FS = cfg.shared_ffn
             sgu = gate_up_to_tiles(sg, su, FS, H, device).reshape(-1)
             sdn = q4_1_to_tiles(sd, H, FS, device)
         wr = _bf16(router_w, device)
-        if tuple(wr.shape) != (H, cfg.n_experts):
-            raise ValueError(f"router weight shape {tuple(wr.shape)} != (H, E) = {(H, cfg.n_experts)}")
         router = torch.empty(cfg.n_experts + 1, H, dtype=torch.bfloat16, device=device)
         sgw_t = None if sgw is None else _bf16(sgw, device).reshape(H)
         call("fm_router_pack", wr.data_ptr(), _ptr(sgw_t), H, cfg.n_experts, router.data_ptr(), _stream(device))
