@@ -266,6 +266,19 @@ class MoELayer:
         if xm.device != self.device or xm.dim() != 2 or xm.shape[1] != self.cfg.hidden or not xm.is_contiguous():
             raise ValueError(f"xm must be a contiguous [T, {self.cfg.hidden}] tensor on {self.device}")
 
+    def _check_bufs(self, T: int, **bufs):
+        """Device buffers handed to the library as raw pointers: a host tensor or a wrong size would be
+        read or written out of bounds by the kernels, so each is checked here (None = not given)."""
+        H, k = self.cfg.hidden, self.cfg.top_k
+        want = {"res": (torch.float32, (T, H)), "out": (torch.float32, (T, H)), "idx": (torch.int32, (T, k)),
+                "w": (torch.float32, (T, k)), "shared_gate": (torch.float32, (T,))}
+        for name, t in bufs.items():
+            if t is None:
+                continue
+            dt, shape = want[name]
+            if t.dtype != dt or tuple(t.shape) != shape or not t.is_contiguous() or t.device != self.device:
+                raise ValueError(f"{name} must be a contiguous {dt} tensor of shape {shape} on {self.device}")
+
     # ---- the reference's entry points
     def router_block(self, xm: torch.Tensor, want_probs: bool = True):
         """(probs [T, E] f32, idx [T, k] int32, w [T, k] f32): softmax top-k, lowest index on a tie."""
@@ -294,11 +307,9 @@ class MoELayer:
         self._check_x(xm)
         T = xm.shape[0]
         t_real = T if t_real is None else t_real
-        for name, t, dt, shape in (("res", res, torch.float32, (T, self.cfg.hidden)),
-                                   ("idx", idx, torch.int32, (T, self.cfg.top_k)),
-                                   ("w", w, torch.float32, (T, self.cfg.top_k))):
-            if t.dtype != dt or tuple(t.shape) != shape or not t.is_contiguous() or t.device != self.device:
-                raise ValueError(f"{name} must be a contiguous {dt} tensor of shape {shape} on {self.device}")
+        if res is None or idx is None or w is None:
+            raise ValueError("moe_block needs res, idx and w")
+        self._check_bufs(T, res=res, idx=idx, w=w, out=out, shared_gate=shared_gate)
         out = torch.empty_like(res) if out is None else out
         ws = self.workspace(T)
         st = _stream(self.device)
@@ -329,6 +340,7 @@ class MoELayer:
         """Router + shared expert + routed experts (fm_moe_layer)."""
         self._check_x(xm)
         T = xm.shape[0]
+        self._check_bufs(T, res=res, out=out, idx=idx, w=w)
         t_real = T if t_real is None else t_real
         out = torch.empty(T, self.cfg.hidden, dtype=torch.float32, device=self.device) if out is None else out
         ws = self.workspace(T)
@@ -346,6 +358,7 @@ class MoELayer:
         if x.dtype != torch.float32 or x.device != self.device or x.dim() != 2 or not x.is_contiguous():
             raise ValueError(f"x must be a contiguous f32 [T, {self.cfg.hidden}] tensor on {self.device}")
         T = x.shape[0]
+        self._check_bufs(T, out=out, idx=idx, w=w)
         t_real = T if t_real is None else t_real
         out = torch.empty_like(x) if out is None else out
         if out.data_ptr() == x.data_ptr():

@@ -41,3 +41,32 @@ def test_layer_inputs_checked_before_device_work(bad):
         bias = np.zeros(5, np.float32)
     with pytest.raises(ValueError):
         flowmoe.MoELayer.from_q4_1(cfg, gate, c["up"], down, wr, shared=shared, device="cpu", router_bias=bias)
+
+
+@pytest.mark.parametrize("which", ["res_dtype", "out_shape", "idx_dtype", "w_device", "gate_shape"])
+def test_buffers_checked_before_the_library_sees_their_pointers(which):
+    # a layer object over host tensors (its constructor makes no library call); every wrong buffer must be
+    # refused in Python, since the kernels would read or write through the raw pointer
+    import flowmoe
+    cfg = flowmoe.MoEConfig(hidden=256, n_experts=4, top_k=2, ffn=128, shared_ffn=0)
+    dummy = torch.empty(16, dtype=torch.uint8)
+    layer = flowmoe.MoELayer(cfg, dummy, dummy, torch.empty(5, 256, dtype=torch.bfloat16))
+    T = 3
+    x = torch.zeros(T, 256, dtype=torch.bfloat16)
+    res, out = torch.zeros(T, 256), torch.zeros(T, 256)
+    idx, w, sg = torch.zeros(T, 2, dtype=torch.int32), torch.zeros(T, 2), torch.zeros(T)
+    if which == "res_dtype":
+        res = res.double()
+    elif which == "out_shape":
+        out = torch.zeros(T + 1, 256)
+    elif which == "idx_dtype":
+        idx = idx.long()
+    elif which == "w_device":
+        w = w.to("meta")
+    else:
+        sg = torch.zeros(T + 2)
+    with pytest.raises(ValueError):
+        if which == "gate_shape":
+            layer.moe_block(x, res, idx, w, shared_gate=sg)
+        else:
+            layer.forward(x, res, out=out, idx=idx, w=w)
