@@ -228,6 +228,7 @@ class PeerEPMoELayer:
         layer = self.layer
         layer._check_x(x)
         T = x.shape[0]
+        layer._check_bufs(T, res=res, out=out, idx=idx, w=w)
         t_real = T if t_real is None else t_real
         out = torch.empty(T, self.cfg.hidden, dtype=torch.float32, device=layer.device) if out is None else out
         ws = self.peers.ws
