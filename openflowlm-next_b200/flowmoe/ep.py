@@ -271,6 +271,8 @@ class EPMoELayer:
                 timings: dict | None = None) -> torch.Tensor:
         if x.shape[0] > self.stages.max_tokens:
             raise ValueError(f"{x.shape[0]} tokens on this rank, more than max_tokens={self.stages.max_tokens}")
+        self.stages.layer._check_x(x)
+        self.stages.layer._check_bufs(x.shape[0], res=res)
         return ep_forward(self.stages, x, res, t_real, self.group, timings)
 
     __call__ = forward
