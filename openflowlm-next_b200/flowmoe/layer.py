@@ -70,12 +70,24 @@ def _as_dev_u8(blocks, device) -> torch.Tensor:
     return blocks.to(device=device, dtype=torch.uint8).contiguous()
 
 
+def _check_dev_u8(t, name: str, numel: int | None = None) -> None:
+    """A byte buffer whose pointer goes to a kernel: a contiguous uint8 tensor on a GPU (of `numel` bytes)."""
+    if not isinstance(t, torch.Tensor) or t.dtype != torch.uint8 or not t.is_cuda or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous uint8 tensor on a GPU")
+    if numel is not None and t.numel() != numel:
+        raise ValueError(f"{name} holds {t.numel()} bytes, not {numel}")
+
+
 def q4_1_to_tiles(blocks, rows: int, k: int, device="cuda", out: torch.Tensor | None = None) -> torch.Tensor:
     """GGUF Q4_1 blocks (numpy or torch, any leading expert dims) -> the device tile layout, per matrix."""
     src = _as_dev_u8(blocks, device).reshape(-1)
     per = rows * k // 32 * Q4_1_BYTES
     if src.numel() % per:
         raise ValueError(f"{src.numel()} block bytes is not a whole number of [{rows}, {k}] matrices")
+    if out is not None:
+        _check_dev_u8(out, "out", src.numel())
+        if out.device != src.device:
+            raise ValueError(f"out is on {out.device}, the blocks on {src.device}")
     dst = torch.empty_like(src) if out is None else out.reshape(-1)
     st = _stream(src.device)
     for i in range(src.numel() // per):
@@ -100,8 +112,11 @@ def gate_up_to_tiles(gate_blocks, up_blocks, F: int, k: int, device="cuda") -> t
 
 def tiles_to_q4_1(tiles: torch.Tensor, rows: int, k: int) -> torch.Tensor:
     """The inverse permutation (tile layout -> GGUF blocks), per matrix."""
+    _check_dev_u8(tiles, "tiles")
     src = tiles.reshape(-1)
     per = rows * k // 32 * Q4_1_BYTES
+    if per <= 0 or src.numel() % per:
+        raise ValueError(f"{src.numel()} tile bytes is not a whole number of [{rows}, {k}] matrices")
     dst = torch.empty_like(src)
     st = _stream(src.device)
     for i in range(src.numel() // per):
@@ -132,6 +147,7 @@ def pool_to_q4_1(pool, n: int, k: int, rs: int = 2, chunk_bytes: int | None = No
 
 def narrow_scales(tiles: torch.Tensor) -> torch.Tensor:
     """In place: every d and m of a tile array rounded to bf16 precision (fm_tiles_narrow_scales)."""
+    _check_dev_u8(tiles, "tiles")
     n = tiles.numel()
     if n % 5120:
         raise ValueError("not a whole number of 5120-byte tiles")

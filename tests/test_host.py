@@ -70,3 +70,16 @@ def test_buffers_checked_before_the_library_sees_their_pointers(which):
             layer.moe_block(x, res, idx, w, shared_gate=sg)
         else:
             layer.forward(x, res, out=out, idx=idx, w=w)
+
+
+def test_tile_wrappers_refuse_host_buffers():
+    # the tile kernels take raw device pointers: host tensors and short outputs are refused in Python
+    import flowmoe
+    from flowmoe.layer import narrow_scales
+    host = torch.zeros(5120, dtype=torch.uint8)
+    with pytest.raises(ValueError):
+        flowmoe.tiles_to_q4_1(host, 128, 64)
+    with pytest.raises(ValueError):
+        narrow_scales(host)
+    with pytest.raises(ValueError):
+        flowmoe.q4_1_to_tiles(host, 128, 64, device="cpu", out=torch.zeros(100, dtype=torch.uint8))
