@@ -107,6 +107,10 @@ class EPMoEStack:
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's tokens x f32 [T, H] -> their stack output (the graph's buffer when replayed)."""
+        L0 = self.layers[0]
+        L0._check_x(x)
+        if x.dtype != torch.float32:
+            raise ValueError(f"x must be float32, not {x.dtype}")
         if self._graph is not None and x.shape == self._x.shape:
             self._x.copy_(x)
             self._graph.replay()
