@@ -262,7 +262,9 @@ FM_API int fm_launch_count(unsigned long long* n);
  * CUDA events): while enabled, each call records a timing event pair around every stage on its
  * stream. Stages: 0 to_bf16, 1 router, 2 dispatch, 3 gather, 4 gate_up, 5 down, 6 combine.
  * fm_profile(1) creates the events on first use; call it before any stream capture. Inside a captured
- * graph the records become event-record nodes, so fm_profile_read then reports the last replay. */
+ * graph the records become event-record nodes, so fm_profile_read then reports the last replay. The
+ * profiler is one process-wide record for one device: enable it only while a single host thread makes
+ * calls (a measurement tool, not for production). */
 FM_API int fm_profile(int32_t enable);
 
 /* Waits for the recorded events and writes the summed milliseconds per stage into ms[0..n_stages),
