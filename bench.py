@@ -46,6 +46,13 @@ METRIC = "MoE-layer tokens/s"
 T_HEADLINE = 8192
 
 
+def headline_config(world: int) -> dict:
+    """The workload both arms name (identical dicts): the C36 layer over 8192 tokens per GPU."""
+    return {"workload": WORKLOAD, "hidden": 2048, "experts": 256, "top_k": 8, "ffn": 512, "shared_ffn": 512,
+            "tokens_per_gpu": T_HEADLINE, "weights": "q4_1", "parallelism": f"ep{world}" if world > 1 else "single",
+            "l2": "expert weights 503 MB > 126 MB L2 streamed every step"}
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -163,31 +170,6 @@ def gate_up_flops(cfg, pairs, T):
     if cfg.shared_ffn:
         f += 2.0 * T * 2 * cfg.hidden * cfg.shared_ffn
     return f
-
-
-# ------------------------------------------------------------------ CPU baseline (oracle port)
-def cpu_baseline(layer_blocks, cfg, x, res, budget_s=20.0, threads=None):
-    """Oracle port on host cores, a bounded token sample; returns (tokens/s, cores, sample text)."""
-    from oracle.moe import MoeLayerF32
-    cores = threads or len(os.sched_getaffinity(0))
-    torch.set_num_threads(cores)
-    os.environ["OMP_NUM_THREADS"] = str(cores)
-    gate, up, down, wr, shared = layer_blocks
-    sh = None
-    if shared is not None:
-        sh = tuple(s.cpu().numpy() for s in shared[:3]) + (shared[3].float().cpu().numpy(),)
-    port = MoeLayerF32(wr.float().cpu().numpy(), gate.cpu().numpy(), up.cpu().numpy(), down.cpu().numpy(),
-                       shared=sh, topk=cfg.top_k)
-    xs = x.float().cpu().numpy()
-    rs = res.cpu().numpy()
-    n, done, t0 = 64, 0, time.perf_counter()
-    while True:
-        port.forward(xs[done % len(xs):done % len(xs) + n], rs[done % len(rs):done % len(rs) + n])
-        done += n
-        if time.perf_counter() - t0 > budget_s or done >= len(xs):
-            break
-    dt = time.perf_counter() - t0
-    return done / dt, cores, f"{done} of {len(xs)} tokens of the same layer, NumPy fp32 + BLAS ({cores} threads)"
 
 
 # ------------------------------------------------------------------ sweep (configs 2 and 3)
@@ -319,31 +301,108 @@ def sweep(hbm, tfl_burst):
 
 
 # ------------------------------------------------------------------ arms
+def ref_router_lib():
+    """The reference's own host router (src/open_qwen36/block_host.cpp:766-803, OpenMP), compiled from its
+    sources by oracle/Makefile into oracle/_ref/, or None when it was not built."""
+    import ctypes
+    p = ROOT / "oracle" / "_ref" / "libref_router.so"
+    if not p.exists():
+        return None
+    lib = ctypes.CDLL(str(p))
+    lib.ref_router_block.restype = ctypes.c_int
+    return lib
+
+
+class CpuLayer:
+    """The CPU implementation of the headline layer on the host cores: the router stage is the reference's
+    own C++ host::router_block when oracle/_ref holds it (else the NumPy port's router), the experts, the
+    shared expert and the combine are the NumPy fp32 + BLAS port of replica.py / Core::moe_block
+    (oracle.moe.MoeLayerF32). Weights: seeded GGUF Q4_1 blocks of the C36 shapes (the reference's block
+    generator; the timing does not depend on their values)."""
+
+    def __init__(self, seed=0, threads=None):
+        from oracle.moe import MoeLayerF32, bf16_round
+        from oracle.q4_1 import random_q4_1_blocks
+        self.cores = threads or len(os.sched_getaffinity(0))
+        torch.set_num_threads(self.cores)
+        os.environ["OMP_NUM_THREADS"] = str(self.cores)
+        rng = np.random.default_rng(seed)
+        H, E, F, FS, k = 2048, 256, 512, 512, 8
+        gate = [random_q4_1_blocks(F, H, rng) for _ in range(E)]
+        up = [random_q4_1_blocks(F, H, rng) for _ in range(E)]
+        down = [random_q4_1_blocks(H, F, rng) for _ in range(E)]
+        shared = (random_q4_1_blocks(FS, H, rng), random_q4_1_blocks(FS, H, rng), random_q4_1_blocks(H, FS, rng),
+                  bf16_round(rng.normal(0, 0.02, H).astype(np.float32)))
+        self.Wr = bf16_round(rng.normal(0, 0.02, (H, E)).astype(np.float32))
+        self.port = MoeLayerF32(self.Wr, gate, up, down, shared=shared, topk=k)
+        self.x = bf16_round(rng.standard_normal((T_HEADLINE, H), dtype=np.float32))
+        self.res = rng.standard_normal((T_HEADLINE, H)).astype(np.float32)
+        self.ref = ref_router_lib()
+        if self.ref is not None:   # the reference router replaces the port's own
+            self.port.route = self._route_ref
+
+    def _route_ref(self, xm):
+        import ctypes
+        xm = np.ascontiguousarray(xm, np.float32)
+        T, H = xm.shape
+        E, k = self.Wr.shape[1], self.port.topk
+        probs = np.empty((T, E), np.float32)
+        idx = np.empty((T, k), np.int32)
+        w = np.empty((T, k), np.float32)
+        f = ctypes.POINTER(ctypes.c_float)
+        rc = self.ref.ref_router_block(ctypes.c_size_t(T), ctypes.c_size_t(H), ctypes.c_size_t(E), ctypes.c_size_t(k),
+                                       xm.ctypes.data_as(f), self.Wr.ctypes.data_as(f), probs.ctypes.data_as(f),
+                                       idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), w.ctypes.data_as(f))
+        if rc:
+            raise RuntimeError("reference router_block raised")
+        return probs, idx, w
+
+    @property
+    def kind_text(self):
+        r = ("router: the reference's own host::router_block (block_host.cpp, built from its sources by "
+             "oracle/Makefile, OpenMP)" if self.ref is not None else "router: NumPy port")
+        return f"{r}; experts, shared expert and combine: NumPy fp32 + BLAS port ({self.cores} threads)"
+
+    def step(self, t0, n):
+        """One step over tokens [t0, t0 + n) of the 8192-token batch; returns the seconds it took."""
+        a = time.perf_counter()
+        self.port.forward(self.x[t0:t0 + n], self.res[t0:t0 + n])
+        return time.perf_counter() - a
+
+    def router_rate(self, n=T_HEADLINE):
+        """Tokens/s of the router stage alone over n tokens (the reference's C++ when built)."""
+        xm = self.x[:n]
+        a = time.perf_counter()
+        self.port.route(xm)
+        return n / (time.perf_counter() - a)
+
+
 def run_reference(args):
-    """The CPU implementation of the path on the host cores (rank 0 only)."""
+    """The CPU implementation of the path on the host cores, rank 0 only (the other ranks exit without
+    work). Same metric, unit and config dict as the flowmoe arm; each step is a bounded sample of the
+    headline batch (its first tokens onwards), timed whole, so ms_per_step is the measured step time."""
     rank = int(os.environ.get("RANK", 0))
     if rank != 0:
         return 0
-    import flowmoe
-    from flowmoe.synth import C36, synth_blocks, synth_tokens
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
-    cfg = flowmoe.MoEConfig(**C36)
-    blocks = synth_blocks(cfg, seed=0, device=dev)
-    x, res = synth_tokens(T_HEADLINE, cfg.hidden, seed=0, device=dev)
-    per_step = max(1.0, min(8.0, 150.0 / max(1, args.steps + args.warmup)))
-    vals = []
+    cpu = CpuLayer(seed=0)
+    # size the sample so that warm-up + timed steps take about two minutes
+    probe = cpu.step(0, 16)
+    n = int(max(16, min(1024, 16 * 120.0 / max(1e-3, probe * (args.steps + args.warmup)))))
+    times = []
     for i in range(args.warmup + args.steps):
-        v, cores, sample = cpu_baseline(blocks, cfg, x, res, budget_s=per_step)
+        dt = cpu.step((i * n) % (T_HEADLINE - n + 1), n)
         if i >= args.warmup:
-            vals.append(v)
-    val = float(np.median(vals))
+            times.append(dt)
+    step_s = float(np.median(times))
+    val = n / step_s
+    router = cpu.router_rate(min(T_HEADLINE, 2048))
     line = {"impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(T_HEADLINE / val * 1e3, 3),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "hidden": 2048, "experts": 256, "top_k": 8, "ffn": 512, "shared_ffn": 512,
-                       "tokens_per_gpu": T_HEADLINE, "weights": "q4_1"},
-            "cpu_baseline": {"value": round(val, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": sample + "; each step a bounded sample"},
+            "config": headline_config(args.gpus),
+            "cpu_baseline": {"value": round(val, 3), "unit": "tokens/s", "cores": cpu.cores, "kind": "port",
+                             "sample": f"each step {n} of the 8192 tokens of the headline layer; {cpu.kind_text}",
+                             "router_only_tokens_per_s": round(router, 1)},
             "e2e": {"value": round(val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -485,28 +544,34 @@ def run_flowmoe(args):
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
-            v, cores, sample = cpu_baseline(blocks, cfg, x, res, budget_s=args.cpu_seconds)
-            cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+            cl = CpuLayer(seed=0)
+            n = 64
+            dts = [cl.step((i * n) % (T_HEADLINE - n), n) for i in range(max(1, int(args.cpu_seconds / max(1e-3, cl.step(0, 16) * n / 16))))]
+            v = n / float(np.median(dts))
+            cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": cl.cores, "kind": "port",
+                   "sample": f"{len(dts)} steps of {n} of the 8192 tokens of the same layer; {cl.kind_text}",
+                   "router_only_tokens_per_s": round(cl.router_rate(2048), 1)}
+            del cl
         sw = None if args.no_sweep or world > 1 else sweep(hbm, tfl_burst)
         prof = ROOT / "profiles"
         traffic = None
         tf = prof / "traffic_gate_up.json"
         if tf.exists():
             traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+        # the burst peak for a timed region shorter than a second (the clocks stay at their maximum), the
+        # sustained one (the power cap's clocks) for a longer one
+        region_s = ms * args.steps / 1e3
+        peak, peak_kind_txt = (tfl_burst, "burst") if region_s < 1.0 else (tfl_sus, "sustained")
         line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "hidden": cfg.hidden, "experts": cfg.n_experts, "top_k": cfg.top_k,
-                           "ffn": cfg.ffn, "shared_ffn": cfg.shared_ffn, "tokens_per_gpu": T, "weights": "q4_1",
-                           "parallelism": f"ep{world}" if world > 1 else "single",
-                           **({"ep_exchange": "peer stores over NVLink" if args.ep == "peer" else "nccl all_to_all"}
-                              if world > 1 else {}),
-                           "l2": "expert weights 503 MB > 126 MB L2 streamed every step",
-                           **({"experts_per_gpu": cfg.local, "recv_rows_rank0": pairs} if world > 1 else {})},
+                "config": headline_config(world),
+                **({"ep": {"exchange": "peer stores over NVLink" if args.ep == "peer" else "nccl all_to_all",
+                           "experts_per_gpu": cfg.local, "recv_rows_rank0": pairs}} if world > 1 else {}),
                 "roofline": {"bound": "tensor", "kernel": "expert_tc<gate_up> (routed items)",
-                             "achieved": round(gu_tflops, 2), "peak": tfl_sus, "unit": "TFLOP/s",
-                             "frac": round(gu_tflops / tfl_sus, 4), "traffic": traffic,
-                             "peak_kind": f"{peak_kind} bf16 sustained"},
+                             "achieved": round(gu_tflops, 2), "peak": peak, "unit": "TFLOP/s",
+                             "frac": round(gu_tflops / peak, 4), "traffic": traffic,
+                             "peak_kind": f"{peak_kind} bf16 {peak_kind_txt} (timed region {region_s:.3f} s)"},
                 "stages_ms": stage_ms, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
                 "cpu_baseline": cpu, "sweep": sw,
                 **({"stack_c36_T64_ep": ep_stack} if ep_stack else {})}
@@ -520,14 +585,15 @@ def run_flowmoe(args):
     return 0
 
 
-def profile_case(name: str, calls: int = 6) -> int:
+def profile_case(name: str, calls: int = 6, path: str = "auto") -> int:
     """A few plain layer calls for an ncu capture (no timing, no JSON): "decode" = C30 T=32 (GEMV path),
-    "decode1" = C30 T=1, "prefill" = the headline C36 T=8192 layer."""
+    "decode1" = C30 T=1, "prefill" = the headline C36 T=8192 layer; ``path`` forces a kernel choice."""
     import flowmoe
     from flowmoe.synth import C30, C36, synth_layer, synth_tokens
     cfg = flowmoe.MoEConfig(**(C36 if name == "prefill" else C30))
     T = {"decode": 32, "decode1": 1}.get(name, T_HEADLINE)
     layer = synth_layer(cfg, seed=0)
+    layer.path = path
     x, res = synth_tokens(T, cfg.hidden, seed=T)
     out = torch.empty_like(res)
     for _ in range(calls):
@@ -552,9 +618,11 @@ def main():
                     help="N > 1: also time BASELINE config 5 (48-layer stack, 64 decode tokens) across the group")
     ap.add_argument("--profile-case", choices=["decode", "decode1", "prefill"], default=None,
                     help="run a few plain layer calls for an ncu capture and exit")
+    ap.add_argument("--profile-path", default="auto", choices=["auto", "tc", "tc2", "gemv"],
+                    help="--profile-case: the kernel choice (MoELayer.path)")
     args = ap.parse_args()
     if args.profile_case:
-        return profile_case(args.profile_case)
+        return profile_case(args.profile_case, path=args.profile_path)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -5,10 +5,10 @@
  * an int status (FM_OK or an FM_E* code) and never throws. fm_last_error() returns the message of the
  * calling thread's last failure. No entry point synchronises the stream unless its comment says so.
  * Threads: entry points may be called from several host threads; per-device library state (the
- * shared-expert side stream, the router's cuBLAS handle) is guarded while work is enqueued. Calls on
- * two streams of one device serialise their tensor-core shared-expert work on the device's side stream,
- * and must not run the cuBLAS router (T >= 256 tokens) at the same time: its workspace is per device.
- * Separate devices, and the decode path (T <= 128 tokens), have no such limit.
+ * shared-expert side stream and its events) is guarded while work is enqueued. Calls on two streams of
+ * one device serialise their tensor-core shared-expert work on the device's side stream. Separate
+ * devices, and the decode path (T <= 128 tokens), have no such limit. No entry point calls a library
+ * kernel (cuBLAS or other): every kernel launched is this library's own.
  *
  * Weights live on the device in the "tile" layout produced by fm_q4_1_to_tiles() from GGUF Q4_1
  * blocks (the reference's open_kernels/q4_1_pack.py:1-14 block format: fp16 d | fp16 m | 16 nibble
@@ -17,7 +17,7 @@
  * tile (band b, slab s) sits at byte ((b * K/64) + s) * 5120 and holds
  *     [0, 4096)    row r (0..127): 32 nibble bytes = the 16 nibble bytes of block 2s, then of block 2s+1,
  *                  each block's bytes b0..b15 stored as the four words [b(2c) b(2c+1) b(2c+8) b(2c+9)],
- *                  c = 0..3 (one mma.sync A fragment per word)
+ *                  c = 0..3 (one 16x16 MMA A fragment per word, the GEMV's operand order)
  *     [4096, 5120) row r: 8 bytes = d(2s) m(2s) d(2s+1) m(2s+1), fp16
  * The down matrix [H, F] of each expert uses these 128-row bands ("down" array). Its gate and up
  * matrices [F, H] are interleaved by fm_gate_up_to_tiles() into 128-row bands of 64 features: band c
@@ -64,12 +64,12 @@ typedef struct fm_layer {
     int32_t shared_ffn; /* F_s of the always-on shared expert (% 64 == 0); 0 = none */
     int32_t e_begin;    /* first expert held by this rank (expert parallel); 0 on one GPU */
     int32_t e_local;    /* experts held by this rank; E on one GPU */
-    int32_t flags;      /* 0 = pick kernels by size (the GEMV up to 128 tokens while T * top_k <= 1024, else
-                           tcgen05 from 64 tokens, mma.sync below);
-                           1 = force mma.sync, 2 = force tcgen05, 3 = force the GEMV (within the same
-                           limits, mma.sync past them),
-                           4 = force tcgen05 as CTA pairs (M = 256 MMAs; when every matrix has an
-                           even number of 128-row bands, else one CTA per item as with 2) */
+    int32_t flags;      /* 0 = pick kernels by size (the GEMV up to 128 tokens while T * top_k <= 1024 and
+                           e_local < 1024, else the tcgen05 grouped GEMM);
+                           2 = force tcgen05, 3 = force the GEMV (within the same limits, tcgen05 past
+                           them), 4 = force tcgen05 as CTA pairs (M = 256 MMAs; when every matrix has an
+                           even number of 128-row bands, else one CTA per item as with 2); any other
+                           value is rejected (FM_EINVAL_SHAPE) */
     const uint8_t* gate_up;   /* tiles, e_local x (2 x F x H x 5/8 B): gate then up, per expert */
     const uint8_t* down;      /* tiles, e_local x (H x F x 5/8 B) */
     const uint8_t* shared_gate_up; /* tiles of the shared expert, or NULL */
@@ -169,13 +169,18 @@ FM_API int fm_moe_dispatch(const fm_layer* L, const int32_t* idx, int32_t T, int
                            int32_t* offsets, int32_t* pos, int32_t* pair, void* workspace, size_t workspace_bytes,
                            void* stream);
 
-/* fm_moe_layer for callers that cannot allocate device memory -- a decode loop being captured into a
- * CUDA graph, or a host engine that plans every device buffer up front -- so it takes no workspace.
- * No counterpart in the reference. The scratch space is a static 16 MiB device array in this library,
- * held on every GPU that loads it until exit; calls needing more (fm_workspace_size > 16 MiB, about
- * 128 tokens for the BASELINE layers) return FM_EWORKSPACE. All calls on a device share the array:
- * calls that overlap on the GPU race and must be serialised by the caller. The first call on each
- * device looks the array's address up; make it before any stream capture. */
+/* fm_moe_layer for callers that cannot allocate device memory, so it takes no workspace: an engine that
+ * reserves all of its device memory when it loads a model (as the reference's engine does with fixed
+ * per-layer buffers) and has no hook for a call-sized workspace, or a decode loop that cannot afford the
+ * device synchronisation a cudaMalloc may cause. No counterpart in the reference.
+ * The scratch space is a static 24 MiB device array in this library, held on every GPU that loads it
+ * until exit; calls needing more (fm_workspace_size > 24 MiB: for 2048-wide top-8 layers more than 456
+ * tokens with 128 experts of F 768, more than 497 with 256 experts of F 512 and a shared expert of 512)
+ * return FM_EWORKSPACE. All calls on a device share the array, which keeps the last call's contents:
+ * calls that overlap on the GPU race and must be serialised by the caller. The first call on each device
+ * does a one-time set-up (it looks the array's address up and creates the side stream and events the
+ * shared expert uses); make it before any stream capture. Every kernel on this path is the library's
+ * own: no cudaMalloc, cudaFree or allocating library routine is called. */
 FM_API int fm_moe_layer_noalloc(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, int32_t T,
                                 int32_t t_real, float* out, int32_t* idx, float* w, void* stream);
 
@@ -254,8 +259,7 @@ FM_API int fm_ipc_free(void* ptr);
  * (the check core.cpp:5159-5160 throws on). */
 FM_API int fm_moe_check(void* workspace, void* stream);
 
-/* Launches of this library's own kernels in this process (the proof that the device path ran); the
- * router's cuBLAS GEMM (T >= 256 tokens) is a library kernel and is not counted. */
+/* Launches of this library's own kernels in this process (the proof that the device path ran). */
 FM_API int fm_launch_count(unsigned long long* n);
 
 /* Stage profiler (the reference's OFLM_OPEN_PROFILE stage timings, core.cpp:592-600, :850-935, on

@@ -44,7 +44,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return OUT
     cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--shared", "-Xcompiler", "-fPIC",
            "-Xcompiler", "-fvisibility=hidden", "-I", str(ROOT / "include"), "-I", str(CSRC),
-           "-o", str(OUT) + ".tmp", *map(str, sources()), "-lcuda", "-lcublas",
+           "-o", str(OUT) + ".tmp", *map(str, sources()), "-lcuda",
            "-Xlinker", "-rpath=" + str(Path(nvcc()).resolve().parent.parent / "lib64")]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")

@@ -102,10 +102,9 @@ int cuda_status(cudaError_t e, const char* what) {
 
 // kernels: see kernels.cuh
 
-constexpr int kBN = 64;        // rows per expert work item (expert_mma)
+constexpr int kBN = 64;        // rows per work item the list sizes assume (>= the real items' rows)
 constexpr int kBNTc = 256;     // rows per expert work item (expert_tc)
-constexpr int kTcMinTokens = 64;   // the tcgen05 path from this many tokens (below: the mma.sync path)
-constexpr int kFlagLegacy = 1, kFlagTc = 2, kFlagGemv = 3, kFlagTcPair = 4;
+constexpr int kFlagTc = 2, kFlagGemv = 3, kFlagTcPair = 4;   // 1 was the retired mma.sync path
 
 // Flag kFlagTcPair runs the tcgen05 GEMMs as CTA pairs (M = 256 MMAs over band pairs) when every
 // matrix has an even number of 128-row bands. One CTA per item is the default: measured faster on
@@ -157,6 +156,15 @@ static SideStream* side_stream() {
 }
 
 
+// Creates this device's side stream and its events now (fm_moe_layer_noalloc's first-call set-up), so
+// that no later call creates them.
+int prepare_side_stream() {
+    if (!side_stream()) {
+        set_error("could not create the side stream");
+        return FM_ECUDA;
+    }
+    return FM_OK;
+}
 
 struct Layout {
     size_t err, xb, logits, counts, offsets, blk_hist, pos, pair, gu_list, dn_list, xperm, hperm, yperm, sgate, idx, w;
@@ -177,6 +185,10 @@ static int validate(const fm_layer* L, int T) {
     }
     if (k <= 0 || k > E || k > kMaxTopK) {
         set_error("router_block: topk %d past the expert count %d (or > %d)", k, E, kMaxTopK);
+        return FM_EINVAL_SHAPE;
+    }
+    if (L->flags != 0 && L->flags != kFlagTc && L->flags != kFlagGemv && L->flags != kFlagTcPair) {
+        set_error("flags %d is not a kernel choice (0 size default, 2 tcgen05, 3 GEMV, 4 tcgen05 CTA pairs)", L->flags);
         return FM_EINVAL_SHAPE;
     }
     if (L->e_begin < 0 || L->e_local < 0 || L->e_begin + L->e_local > E) {
@@ -223,7 +235,7 @@ static Layout make_layout(const fm_layer* L, int T) {
     o.dn_list = take((size_t)(4 + 4 * o.max_dn) * 4);
     o.xperm = take((size_t)o.rows * H * 2);
     o.hperm = take((size_t)o.rows * o.fmax * 2);
-    o.yperm = take((size_t)o.rows * H * 4);
+    o.yperm = take(decode ? (size_t)o.rows * H * 4 : 0);   // f32 y rows: the GEMV path only
     o.sgate = take((size_t)T * 4);
     o.idx = take((size_t)o.P * 4);
     o.w = take((size_t)o.P * 4);
@@ -252,6 +264,13 @@ static int check_ws(const Layout& lo, void* ws, size_t bytes) {
     return FM_OK;
 }
 
+// Clears the call's status words (expert ids out of range, device waits that gave up) before its first
+// kernel on the tcgen05 path; on the GEMV path the dispatch kernel clears them itself.
+static int clear_status(void* ws, const Layout& lo, cudaStream_t st) {
+    if (cudaMemsetAsync(at<int>(ws, lo.err), 0, 16, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
+    return FM_OK;
+}
+
 static int xm_to_bf16(const fm_layer* L, const void* xm, int dtype, int T, void* ws, const Layout& lo,
                       const uint16_t** xb, cudaStream_t st) {
     if (dtype == FM_BF16) {
@@ -269,19 +288,19 @@ static int xm_to_bf16(const fm_layer* L, const void* xm, int dtype, int T, void*
     return rc;
 }
 
-enum class Path { Mma, Tc, Gemv };
+enum class Path { Tc, Gemv };
 
+// The GEMV up to kDecodeMaxT tokens (while T * top_k <= 1024, the single-CTA dispatch, and fewer than
+// 1024 local experts), the tcgen05 grouped GEMM otherwise; flags force either (the GEMV only within its
+// limits).
 static Path pick_path(const fm_layer* L, int T) {
     const bool gemv_ok = T <= gemv_max_t(L) && L->e_local < 1024 && T * L->top_k <= 1024;
     switch (L->flags) {
-        case kFlagLegacy: return Path::Mma;
         case kFlagTc:
         case kFlagTcPair: return Path::Tc;
-        case kFlagGemv: return gemv_ok ? Path::Gemv : Path::Mma;
         default: break;
     }
-    if (gemv_ok) return Path::Gemv;
-    return T >= kTcMinTokens ? Path::Tc : Path::Mma;
+    return gemv_ok ? Path::Gemv : Path::Tc;
 }
 
 static int run_block_gemv(const fm_layer* L, const uint16_t* xb, const float* res, const int32_t* idx, const float* w,
@@ -416,38 +435,32 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
                      const float* sgate, int T, int t_real, float* out, void* ws, const Layout& lo, cudaStream_t st) {
     const int H = L->hidden, k = L->top_k, E = L->n_experts;
     const bool shared_on = L->shared_ffn > 0 && sgate && L->shared_gate_up && L->shared_down && t_real > 0;
-    const Path path = pick_path(L, T);
-    if (path == Path::Gemv) return run_block_gemv(L, xb, res, idx, w, sgate, T, t_real, out, ws, lo, st);
+    if (pick_path(L, T) == Path::Gemv) return run_block_gemv(L, xb, res, idx, w, sgate, T, t_real, out, ws, lo, st);
     const int P = t_real * k;
-    const bool tc = path == Path::Tc;
-    const int bn = tc ? kBNTc : kBN;
-    const int bdiv = (tc && tc_pair(L)) ? 2 : 1;   // list entries are band pairs for the CTA-pair kernel
-    if (cudaMemsetAsync(at<int>(ws, lo.err), 0, 16, st) != cudaSuccess) return cuda_status(cudaGetLastError(), "memset");
+    const int bdiv = tc_pair(L) ? 2 : 1;   // list entries are band pairs for the CTA-pair kernel
+    // (the caller cleared the status words before this call's first kernel: clear_status)
     const int nblk = (P + kChunk - 1) / kChunk;
     // rows of the sorted space: routed [0, P), shared [P_cap, P_cap + t_real) with P_cap = T * k
     const int Pcap = lo.P;
-    // tcgen05 path: the shared expert reads x directly and runs on a side stream while the routed rows
-    // are dispatched and gathered (those kernels leave most SMs idle); out = res must precede it
-    SideStream* side = (tc && shared_on) ? side_stream() : nullptr;
-    if (tc && shared_on && !side) {
+    // the shared expert reads x directly and runs on a side stream while the routed rows are dispatched
+    // and gathered (those kernels leave most SMs idle); out = res must precede it
+    SideStream* side = shared_on ? side_stream() : nullptr;
+    if (shared_on && !side) {
         set_error("could not create the side stream");
         return FM_ECUDA;
     }
     int rc = FM_OK;
-    if (tc) {
-        if (cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-            return cuda_status(cudaGetLastError(), "out = res");
-        if (side && (rc = launch_shared_side(L, xb, sgate, T, t_real, out, at<int>(ws, lo.gu_list_sh),
-                                             at<int>(ws, lo.dn_list_sh), at<uint16_t>(ws, lo.hperm) + (size_t)Pcap * lo.fmax,
-                                             lo.fmax, bdiv, 0, at<int>(ws, lo.err) + 1, side, st)))
-            return rc;
-    }
-    const bool shared_in_lists = shared_on && !side;
+    if (cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "out = res");
+    if (side && (rc = launch_shared_side(L, xb, sgate, T, t_real, out, at<int>(ws, lo.gu_list_sh),
+                                         at<int>(ws, lo.dn_list_sh), at<uint16_t>(ws, lo.hperm) + (size_t)Pcap * lo.fmax,
+                                         lo.fmax, bdiv, 0, at<int>(ws, lo.err) + 1, side, st)))
+        return rc;
     prof_begin(kStageDispatch, st);
-    rc = launch_dispatch(idx, P, L->e_begin, L->e_local, E, Pcap, shared_in_lists ? t_real : 0, at<int>(ws, lo.blk_hist),
-                         nblk, at<int>(ws, lo.counts), at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
-                         at<int>(ws, lo.gu_list), L->ffn / 64 / bdiv, shared_in_lists ? L->shared_ffn / 64 / bdiv : 0,
-                         at<int>(ws, lo.dn_list), H / kTileRows / bdiv, bn, at<int>(ws, lo.err), st);
+    rc = launch_dispatch(idx, P, L->e_begin, L->e_local, E, Pcap, 0, at<int>(ws, lo.blk_hist), nblk,
+                         at<int>(ws, lo.counts), at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
+                         at<int>(ws, lo.gu_list), L->ffn / 64 / bdiv, 0, at<int>(ws, lo.dn_list), H / kTileRows / bdiv,
+                         kBNTc, at<int>(ws, lo.err), st);
     if (rc) return rc;
     prof_end(kStageDispatch, st);
     prof_begin(kStageGather, st);
@@ -455,75 +468,33 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
                             k, H, lo.rows, at<uint16_t>(ws, lo.xperm), st)))
         return rc;
     prof_end(kStageGather, st);
-    if (tc) {
-        // out = res was set above (rows past t_real stay res); the down GEMM adds w * y into it
-        TcLaunch g{};
-        g.max_items = lo.max_gu;
-        g.list = at<int>(ws, lo.gu_list);
-        g.act = at<uint16_t>(ws, lo.xperm);
-        g.act_rows = lo.rows;
-        g.act_cols = H;
-        g.act_ld = H;
-        g.w_routed = L->gate_up;
-        g.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
-        g.w_shared = L->shared_gate_up;
-        g.shared_group = L->e_local;
-        g.K_routed = H;
-        g.K_shared = H;
-        g.h_out = at<uint16_t>(ws, lo.hperm);
-        g.h_ld = lo.fmax;
-        g.err = at<int>(ws, lo.err) + 1;
-        g.cta_pair = bdiv == 2;
-        prof_begin(kStageGateUp, st);
-        if ((rc = launch_expert_tc(true, g, st))) return rc;
-        prof_end(kStageGateUp, st);
-        TcLaunch d{};
-        d.max_items = lo.max_dn;
-        d.list = at<int>(ws, lo.dn_list);
-        d.act = at<uint16_t>(ws, lo.hperm);
-        d.act_rows = lo.rows;
-        d.act_cols = lo.fmax;
-        d.act_ld = lo.fmax;
-        d.w_routed = L->down;
-        d.w_routed_stride = (size_t)H * L->ffn / 32 * 20;
-        d.w_shared = L->shared_down;
-        d.shared_group = L->e_local;
-        d.K_routed = L->ffn;
-        d.K_shared = L->shared_ffn;
-        d.out = out;
-        d.H = H;
-        d.pair = at<int>(ws, lo.pair);
-        d.wpair = w;
-        d.k = k;
-        d.shared_base = Pcap;
-        d.sgate = sgate;
-        d.err = at<int>(ws, lo.err) + 1;
-        d.cta_pair = bdiv == 2;
-        prof_begin(kStageDown, st);
-        if ((rc = launch_expert_tc(false, d, st))) return rc;
-        prof_end(kStageDown, st);
-        if (side && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
-            return cuda_status(cudaGetLastError(), "join the shared expert");
-        return FM_OK;
-    }
-    GroupedArgs a{};
-    a.list = at<int>(ws, lo.gu_list);
-    a.act = at<uint16_t>(ws, lo.xperm);
-    a.act_ld = H;
-    a.w_routed = L->gate_up;
-    a.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
-    a.w_shared = L->shared_gate_up;
-    a.shared_group = L->e_local;
-    a.K_routed = H;
-    a.K_shared = H;
-    a.out = at<uint16_t>(ws, lo.hperm);
-    a.out_ld = lo.fmax;
+    // out = res was set above (rows past t_real stay res); the down GEMM adds w * y into it
+    TcLaunch g{};
+    g.max_items = lo.max_gu;
+    g.list = at<int>(ws, lo.gu_list);
+    g.act = at<uint16_t>(ws, lo.xperm);
+    g.act_rows = lo.rows;
+    g.act_cols = H;
+    g.act_ld = H;
+    g.w_routed = L->gate_up;
+    g.w_routed_stride = (size_t)2 * L->ffn * H / 32 * 20;
+    g.w_shared = L->shared_gate_up;
+    g.shared_group = L->e_local;
+    g.K_routed = H;
+    g.K_shared = H;
+    g.h_out = at<uint16_t>(ws, lo.hperm);
+    g.h_ld = lo.fmax;
+    g.err = at<int>(ws, lo.err) + 1;
+    g.cta_pair = bdiv == 2;
     prof_begin(kStageGateUp, st);
-    if ((rc = launch_expert_mma(true, a, lo.max_gu, st))) return rc;
+    if ((rc = launch_expert_tc(true, g, st))) return rc;
     prof_end(kStageGateUp, st);
-    GroupedArgs d{};
+    TcLaunch d{};
+    d.max_items = lo.max_dn;
     d.list = at<int>(ws, lo.dn_list);
     d.act = at<uint16_t>(ws, lo.hperm);
+    d.act_rows = lo.rows;
+    d.act_cols = lo.fmax;
     d.act_ld = lo.fmax;
     d.w_routed = L->down;
     d.w_routed_stride = (size_t)H * L->ffn / 32 * 20;
@@ -531,16 +502,21 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     d.shared_group = L->e_local;
     d.K_routed = L->ffn;
     d.K_shared = L->shared_ffn;
-    d.out = at<float>(ws, lo.yperm);
-    d.out_ld = H;
+    d.out = out;
+    d.H = H;
+    d.pair = at<int>(ws, lo.pair);
+    d.wpair = w;
+    d.k = k;
+    d.shared_base = Pcap;
+    d.sgate = sgate;
+    d.err = at<int>(ws, lo.err) + 1;
+    d.cta_pair = bdiv == 2;
     prof_begin(kStageDown, st);
-    if ((rc = launch_expert_mma(false, d, lo.max_dn, st))) return rc;
+    if ((rc = launch_expert_tc(false, d, st))) return rc;
     prof_end(kStageDown, st);
-    prof_begin(kStageCombine, st);
-    rc = launch_combine(res, at<float>(ws, lo.yperm), at<int>(ws, lo.pos), idx, w, sgate, shared_on ? 1 : 0, T,
-                        t_real, k, H, Pcap, out, st);
-    prof_end(kStageCombine, st);
-    return rc;
+    if (side && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
+        return cuda_status(cudaGetLastError(), "join the shared expert");
+    return FM_OK;
 }
 
 }  // namespace fm
@@ -576,10 +552,11 @@ extern "C" FM_API int fm_router_topk(const fm_layer* L, const void* xm, int32_t 
     const Layout lo = make_layout(L, T);
     if (int rc = check_ws(lo, workspace, workspace_bytes)) return rc;
     cudaStream_t st = (cudaStream_t)stream;
+    if (int rc = clear_status(workspace, lo, st)) return rc;
     const uint16_t* xb = nullptr;
     if (int rc = xm_to_bf16(L, xm, xm_dtype, T, workspace, lo, &xb, st)) return rc;
     return launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k, at<float>(workspace, lo.logits), probs,
-                         idx, w, shared_gate, st);
+                         idx, w, shared_gate, at<int>(workspace, lo.err), st);
 }
 
 extern "C" FM_API int fm_moe_block(const fm_layer* L, const void* xm, int32_t xm_dtype, const float* res, const int32_t* idx,
@@ -596,6 +573,8 @@ extern "C" FM_API int fm_moe_block(const fm_layer* L, const void* xm, int32_t xm
     if (int rc = check_ws(lo, workspace, workspace_bytes)) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     const uint16_t* xb = nullptr;
+    if (pick_path(L, T) == Path::Tc)
+        if (int rc = clear_status(workspace, lo, st)) return rc;
     if (int rc = xm_to_bf16(L, xm, xm_dtype, T, workspace, lo, &xb, st)) return rc;
     return run_block(L, xb, res, idx, w, shared_gate, T, t_real, out, workspace, lo, st);
 }
@@ -608,9 +587,11 @@ static int moe_layer_xb(const fm_layer* L, const uint16_t* xb, const float* res,
     int32_t* ids = idx ? idx : at<int32_t>(workspace, lo.idx);
     float* ws_w = w ? w : at<float>(workspace, lo.w);
     float* sg = at<float>(workspace, lo.sgate);
+    if (pick_path(L, T) == Path::Tc)
+        if (int rc = clear_status(workspace, lo, st)) return rc;
     prof_begin(kStageRouter, st);
     if (int rc = launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k,
-                               at<float>(workspace, lo.logits), nullptr, ids, ws_w, sg, st))
+                               at<float>(workspace, lo.logits), nullptr, ids, ws_w, sg, at<int>(workspace, lo.err), st))
         return rc;
     prof_end(kStageRouter, st);
     return run_block(L, xb, res, ids, ws_w, sg, T, t_real, out, workspace, lo, st);
@@ -887,7 +868,7 @@ extern "C" FM_API int fm_ep_dispatch(const fm_layer* L, const void* xm, int32_t 
         return cuda_status(cudaGetLastError(), "memset");
     prof_begin(kStageRouter, st);
     if (int rc = launch_router(xb, L->router, L->router_bias, T, H, E, k, at<float>(workspace, lo.logits), nullptr, idx, w,
-                               shared_gate, st))
+                               shared_gate, at<int>(workspace, lo.err), st))
         return rc;
     prof_end(kStageRouter, st);
     const int P = t_real * k;
@@ -1170,7 +1151,7 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     int rc = FM_OK;
     prof_begin(kStageRouter, st);
     if (T > 0 && (rc = launch_router(xb, L->router, L->router_bias, T, H, E, k, at<float>(workspace, lo.logits), nullptr,
-                                     ids, wts, sg, st)))
+                                     ids, wts, sg, a.err, st)))
         return rc;
     prof_end(kStageRouter, st);
     prof_begin(kStageDispatch, st);

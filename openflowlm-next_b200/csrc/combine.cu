@@ -1,126 +1,10 @@
-// Grouped Q4_1 expert GEMM on the warp-level tensor-core path (mma.sync m16n8k16 bf16).
-//
-// The small-batch kernel (decode-sized token counts) and the correctness baseline of the tcgen05
-// kernel: one CTA per work item (group, 128-row band, up to 64 sorted rows), K walked in 64-wide
-// slabs. Each slab's weight tile (5120 B) is staged in shared memory and dequantised in registers
-// straight into mma A fragments: w = q * d + m in f32 with the fp16 d/m widened exactly, rounded
-// once to bf16 (the reference's "Q4_1 nibble -> bf16" of designs/moe_batch/moe_batch.h:98-137,
-// with exact scales).
-//   GATE_UP: a gate_up tile holds gate rows 0-63 and up rows 64-127 of 64 features; warp w's mma
-//            rows g / g+8 are gate / up of feature 8w+g, so h = bf16(silu(g) * u) is thread-local
-//            (moe_batch.h:181-202, designs/moe_batch/make_test.py:96).
-//   DOWN:    y rows in f32 (the reference's C tiles, core.cpp:5230-5255 reads them back as f32).
+// Combine kernels: the ordered weighted sum of each token's expert rows (the scatter of
+// src/open_qwen36/core.cpp:5236-5255: a token's expert terms added in ascending expert order), for the
+// decode GEMV path (f32 y rows) and the expert-parallel paths (bf16 y rows returned by the expert ranks).
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace fm {
-
-constexpr int XM_BN = 64;               // sorted rows per work item
-constexpr int XM_LDB = kTileK + 8;      // padded bf16 row of the activation tile
-
-__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Two K values of one row from two code bytes (bits 0-3 and 8-11 of u): w = q * d + m, bf16x2.
-__device__ __forceinline__ uint32_t deq_pair(uint32_t u, float d, float m) {
-    const float q0 = (float)(u & 0xF), q1 = (float)((u >> 8) & 0xF);
-    return pack_bf16x2(fmaf(q0, d, m), fmaf(q1, d, m));
-}
-
-// A fragments (m16n8k16 row-major), k16 step kk of the slab; fragment rows g and g+8 come from tile
-// rows rA and rB. Step kk covers block kk/2, values 16*(kk&1) + {2c, 2c+1, 2c+8, 2c+9}: in the tile's
-// fragment order those are the low (kk even) or high (kk odd) nibbles of word c of the block.
-__device__ __forceinline__ void load_a_frag(const uint8_t* tile, int rA, int rB, int c, int kk, uint32_t* a) {
-    const int blk = kk >> 1, sh = (kk & 1) * 4;
-    const uint32_t ua = *reinterpret_cast<const uint32_t*>(tile + rA * 32 + blk * 16 + c * 4) >> sh;
-    const uint32_t ub = *reinterpret_cast<const uint32_t*>(tile + rB * 32 + blk * 16 + c * 4) >> sh;
-    const __half2 scA = *reinterpret_cast<const __half2*>(tile + kTileNibBytes + rA * 8 + blk * 4);
-    const __half2 scB = *reinterpret_cast<const __half2*>(tile + kTileNibBytes + rB * 8 + blk * 4);
-    const float dA = __low2float(scA), mA = __high2float(scA);
-    const float dB = __low2float(scB), mB = __high2float(scB);
-    a[0] = deq_pair(ua, dA, mA);          // values 2c, 2c+1
-    a[1] = deq_pair(ub, dB, mB);
-    a[2] = deq_pair(ua >> 16, dA, mA);    // values 2c+8, 2c+9
-    a[3] = deq_pair(ub >> 16, dB, mB);
-}
-
-template <bool GATE_UP>
-__global__ void __launch_bounds__(256) expert_mma_kernel(GroupedArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    uint8_t* wt = smem;                                                   // the slab's weight tile
-    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + kTileBytes);       // [64][72]
-    const int n_items = a.list[0];
-    if ((int)blockIdx.x >= n_items) return;
-    const int4 it = reinterpret_cast<const int4*>(a.list + 4)[blockIdx.x];
-    const int g = it.x, band = it.y, row0 = it.z, nrows = it.w;
-    const bool sh = g == a.shared_group;
-    const int K = sh ? a.K_shared : a.K_routed;
-    const uint8_t* wbase = sh ? a.w_shared : a.w_routed + (size_t)g * a.w_routed_stride;
-    const int slabs = K / kTileK;
-    const uint8_t* wg = wbase + (size_t)band * slabs * kTileBytes;              // the band's tiles
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, cq = lane & 3;
-    // tile rows of this warp's fragment rows g and g+8
-    const int rA = GATE_UP ? warp * 8 + gq : warp * 16 + gq;
-    const int rB = GATE_UP ? 64 + warp * 8 + gq : warp * 16 + gq + 8;
-    float accg[8][4] = {};
-    for (int s = 0; s < slabs; ++s) {
-        const uint4* src_g = reinterpret_cast<const uint4*>(wg + (size_t)s * kTileBytes);
-        for (int i = threadIdx.x; i < kTileBytes / 16; i += 256) reinterpret_cast<uint4*>(wt)[i] = src_g[i];
-        for (int i = threadIdx.x; i < XM_BN * 8; i += 256) {
-            const int r = i >> 3, q = i & 7;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (r < nrows) v = *reinterpret_cast<const uint4*>(a.act + (size_t)(row0 + r) * a.act_ld + s * kTileK + q * 8);
-            *reinterpret_cast<uint4*>(xs + r * XM_LDB + q * 8) = v;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            uint32_t ag[4];
-            load_a_frag(wt, rA, rB, cq, kk, ag);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const uint16_t* xr = xs + (j * 8 + gq) * XM_LDB + kk * 16 + 2 * cq;
-                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xr);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(xr + 8);
-                mma16816(accg[j], ag, b0, b1);
-            }
-        }
-        __syncthreads();
-    }
-    // C fragment: c0,c1 = (fragment row gq, cols 2cq, 2cq+1), c2,c3 = (row gq+8, same cols); col =
-    // sorted activation row.
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int n = j * 8 + 2 * cq + h;
-            if (n >= nrows) continue;
-            if (GATE_UP) {
-                const int f = band * 64 + warp * 8 + gq;
-                const float v = silu_f(accg[j][h]) * accg[j][h + 2];
-                reinterpret_cast<uint16_t*>(a.out)[(size_t)(row0 + n) * a.out_ld + f] = f32_to_bf16_bits(v);
-            } else {
-                const int f = band * kTileRows + warp * 16 + gq;
-                float* o = reinterpret_cast<float*>(a.out) + (size_t)(row0 + n) * a.out_ld + f;
-                o[0] = accg[j][h];
-                o[8] = accg[j][h + 2];
-            }
-        }
-    }
-}
-
-int launch_expert_mma(bool gate_up, const GroupedArgs& a, int max_items, cudaStream_t st) {
-    if (max_items <= 0) return FM_OK;
-    const size_t sm = kTileBytes + XM_BN * XM_LDB * 2;
-    if (gate_up) expert_mma_kernel<true><<<max_items, 256, sm, st>>>(a);
-    else expert_mma_kernel<false><<<max_items, 256, sm, st>>>(a);
-    FM_LAUNCH_CHECK(gate_up ? "expert_mma<gate_up>" : "expert_mma<down>");
-    return FM_OK;
-}
 
 // Four consecutive y values of row `row` as floats: f32 rows, or bf16 rows (the tcgen05 path).
 __device__ __forceinline__ float4 ld_y4(const float* y, size_t row, int H, int i) {

@@ -592,8 +592,9 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// bf16 matrix [rows, cols] with row stride ld elements -> map with a {64, 32} box, 128-byte swizzle.
-static int make_bmap(CUtensorMap* m, const uint16_t* base, int rows, int cols, int ld, int box_rows) {
+// bf16 matrix [rows, cols] with row stride ld elements -> map with a {64, box_rows} box, 128-byte swizzle
+// (rows past `rows` read as zeros).
+int make_bmap(CUtensorMap* m, const uint16_t* base, int rows, int cols, int ld, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) {
         set_error("cuTensorMapEncodeTiled unavailable");

@@ -1,33 +1,31 @@
-// Host-side launch wrappers of the kernels (router.cu, dispatch.cu, expert_mma.cu). Each returns an
+// Host-side launch wrappers of the kernels (router.cu, dispatch.cu, combine.cu, decode.cu, expert_tc.cu). Each returns an
 // FM_* status and records the message with set_error on failure.
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace fm {
 
 int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st);
 int launch_rmsnorm_bf16(const float* x, const uint16_t* w, float eps, int T, int H, uint16_t* xb, cudaStream_t st);
+// The router of T tokens (idx, w, sgate, optional probs). From kRouterTcMinT tokens with E + 1 <= 272
+// the fused tcgen05 kernel (router_tc.cu; logits stay on chip, bounded waits report FM_ETIMEOUT in
+// err[1]), else the logits kernel (split-K at small T, into `logits`) and a top-k kernel.
+constexpr int kRouterTcMinT = 256;
+// The per-device side stream of the tcgen05 path (shared expert), created now if it does not exist yet.
+int prepare_side_stream();
+bool router_tc_ok(int T, int E, int k);
 int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
-                  float* logits, float* probs, int32_t* idx, float* w, float* sgate, cudaStream_t st);
+                  float* logits, float* probs, int32_t* idx, float* w, float* sgate, int* err, cudaStream_t st);
+int launch_router_tc(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
+                     float* probs, int32_t* idx, float* w, float* sgate, int* err, cudaStream_t st);
 int launch_dispatch(const int32_t* idx, int P, int e_begin, int e_local, int E, int shared_base, int shared_rows,
                     int* blk_hist, int nblk,
                     int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
                     int* dn_list, int dn_bands, int bn, int* err, cudaStream_t st);
 int launch_gather(const uint16_t* xb, const int* pair, const int* counts, const int* offsets, int e_local, int shared_base,
                   int k, int H, int max_rows, uint16_t* xperm, cudaStream_t st);
-struct GroupedArgs {
-    const int* list;
-    const uint16_t* act;
-    int act_ld;
-    const uint8_t* w_routed;
-    size_t w_routed_stride;
-    const uint8_t* w_shared;
-    int shared_group;
-    int K_routed, K_shared;
-    void* out;
-    int out_ld;
-};
-int launch_expert_mma(bool gate_up, const GroupedArgs& a, int max_items, cudaStream_t st);
 struct TcLaunch {
     int max_items;
     const int* list;
@@ -56,6 +54,8 @@ struct TcLaunch {
     int max_ctas;                    // grid cap (0: one CTA per SM); leaves SMs to concurrent work
 };
 int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st);
+// bf16 matrix [rows, cols] (row stride ld elements) -> a TMA map with {64, box_rows} boxes, 128-byte swizzle.
+int make_bmap(CUtensorMap* m, const uint16_t* base, int rows, int cols, int ld, int box_rows);
 struct GemvLaunch {
     int max_items;
     const int* list;

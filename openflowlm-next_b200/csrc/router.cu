@@ -1,52 +1,16 @@
-// Router: logits GEMM (bf16 x bf16 -> f32 on the tensor cores: cuBLAS from 256 tokens, a split-K
-// mma.sync kernel below) and the per-token softmax / top-k.
+// Router below the prefill sizes: a split-K logits kernel (bf16 x bf16 -> f32 on the warp-level tensor
+// cores; the decode sizes are bound by reading the router weights, so the K split spreads that read
+// over the SMs) and the per-token softmax / top-k. From kRouterTcMinT tokens (E + 1 <= 272) the fused
+// tcgen05 kernel of router_tc.cu takes over; larger routers run the logits kernel unsplit.
 //
 // Follows host::router_block (src/open_qwen36/block_host.cpp:766-803): float logits, max
 // subtraction, float exp with a double denominator, p = e * float(1/denom), top-k by probability
 // (strictly greater wins, so the lowest index wins a tie), weights renormalised by a double sum.
 // The shared-expert gate (core.cpp:4370-4373) rides along as router row E.
-#include <cublas_v2.h>
-
-#include <mutex>
-
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace fm {
-
-// From this many tokens the logits are one cuBLAS bf16 GEMM (a plain library GEMM: [T, H] x [H, E+1]
-// with f32 accumulation and output); below it, the split-K mma.sync kernel here, which needs no
-// library state (the no-allocation entry point and decode graphs use it).
-constexpr int kRouterBlasMinT = 256;
-
-struct BlasState {
-    cublasHandle_t h = nullptr;
-    void* ws = nullptr;
-};
-
-// One handle per device, with a fixed 32 MiB workspace so that later calls (and stream capture) never
-// allocate. Created on the first large-T call. Returns with `lock` held: the handle's stream is set for
-// this caller, and the caller enqueues its GEMM before releasing it, so that another host thread cannot
-// retarget the shared handle in between.
-static cublasHandle_t blas_handle(cudaStream_t st, std::unique_lock<std::mutex>& lock) {
-    static BlasState dev_state[64];
-    static std::mutex mu;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    lock = std::unique_lock<std::mutex>(mu);
-    BlasState& b = dev_state[dev];
-    if (!b.h) {
-        constexpr size_t kWs = size_t(32) << 20;
-        if (cublasCreate(&b.h) != CUBLAS_STATUS_SUCCESS) { b.h = nullptr; return nullptr; }
-        if (cudaMalloc(&b.ws, kWs) != cudaSuccess || cublasSetWorkspace(b.h, b.ws, kWs) != CUBLAS_STATUS_SUCCESS) {
-            cublasDestroy(b.h);
-            b.h = nullptr;
-            return nullptr;
-        }
-    }
-    if (cublasSetStream(b.h, st) != CUBLAS_STATUS_SUCCESS) return nullptr;
-    return b.h;
-}
 
 // xb[t][h] = bf16(xm[t][h]) for f32 input (the rounding the reference applies at the device
 // boundary, core.cpp:5204).
@@ -236,37 +200,16 @@ __device__ __forceinline__ float chunk_sum(const float* lg, size_t zs, int ks, i
 
 // The same result for E <= 256, with each lane's (up to 8) probabilities kept in registers: the ks K
 // chunks summed in chunk order (as above), one exp per expert, then k rounds of (lane max, warp arg-max).
-// gate_row (bf16 [H], or NULL): the shared-gate logit is not in the logits rows but computed here as
-// the f32 dot product of the token's bf16 row xb[t] with it (the cuBLAS path leaves the odd row out
-// of the GEMM so that its output stays 16-byte aligned).
+// The shared-gate logit is the logits row's column E.
 template <bool SPLIT>
 __global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, int ks, const float* __restrict__ bias,
                                     int T, int E, int k, float* __restrict__ probs, int32_t* __restrict__ idx,
-                                    float* __restrict__ w, float* __restrict__ sgate, const uint16_t* __restrict__ xb,
-                                    const uint16_t* __restrict__ gate_row, int H) {
+                                    float* __restrict__ w, float* __restrict__ sgate) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
     const float* lg = logits + (size_t)warp * ld;
     const size_t zs = (size_t)T * ld;
-    float gl = 0.f;
-    if (gate_row) {
-        if (sgate) {
-            const uint4* xr = reinterpret_cast<const uint4*>(xb + (size_t)warp * H);
-            const uint4* gr = reinterpret_cast<const uint4*>(gate_row);
-            for (int i = lane; i < H / 8; i += 32) {
-                const uint4 a = xr[i], b = gr[i];
-                const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    gl = fmaf(__uint_as_float(av[j] << 16), __uint_as_float(bv[j] << 16), gl);
-                    gl = fmaf(__uint_as_float(av[j] & 0xFFFF0000u), __uint_as_float(bv[j] & 0xFFFF0000u), gl);
-                }
-            }
-            gl = warp_sum(gl);
-        }
-    } else if (sgate) {
-        gl = chunk_sum<SPLIT>(lg, zs, ks, E);
-    }
+    const float gl = sgate ? chunk_sum<SPLIT>(lg, zs, ks, E) : 0.f;
     float v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -364,16 +307,15 @@ int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st) {
     return FM_OK;
 }
 
-// K chunks of the router GEMM: enough CTAs to cover the SMs when few tokens give few tiles.
-// Row stride of the logits: E + 1, padded to 8 floats for the cuBLAS path (an aligned output).
-static int router_ld(int T, int E) { return T >= kRouterBlasMinT ? (E + 1 + 7) / 8 * 8 : E + 1; }
-
+// K chunks of the router GEMM: enough CTAs to cover the SMs when few tokens give few tiles. The logits
+// rows hold E + 1 values (the last is the shared-gate logit).
 size_t router_scratch_bytes(int T, int H, int E) {
-    return (size_t)router_ksplit(T, H, E) * T * router_ld(T, E) * 4;
+    if (router_tc_ok(T, E, 1)) return 0;   // the fused kernel keeps its logits in TMEM
+    return (size_t)router_ksplit(T, H, E) * T * (E + 1) * 4;
 }
 
 int router_ksplit(int T, int H, int E) {
-    if (T >= kRouterBlasMinT) return 1;
+    if (T >= kRouterTcMinT) return 1;
     const int tiles = ((E + 1 + RG_BN - 1) / RG_BN) * ((T + RG_BM - 1) / RG_BM);
     int ks = 1;
     while (ks < kMaxKSplit && tiles * ks < 148 && H % (2 * ks * RG_BK) == 0) ks *= 2;
@@ -381,43 +323,18 @@ int router_ksplit(int T, int H, int E) {
 }
 
 int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
-                  float* logits, float* probs, int32_t* idx, float* w, float* sgate, cudaStream_t st) {
+                  float* logits, float* probs, int32_t* idx, float* w, float* sgate, int* err, cudaStream_t st) {
+    if (router_tc_ok(T, E, k)) return launch_router_tc(xb, router, bias, T, H, E, k, probs, idx, w, sgate, err, st);
     const int ks = router_ksplit(T, H, E);
-    const int ld = router_ld(T, E);
-    // the register top-k computes the shared-gate logit itself on the cuBLAS path (E rows in the GEMM)
-    const bool topk8 = E <= 256;
-    const bool gate_in_topk = topk8 && T >= kRouterBlasMinT;
-    const int gemm_rows = gate_in_topk ? E : E + 1;
-    if (T >= kRouterBlasMinT) {
-        // logits (row-major [T, E+1]) = xb [T, H] . router [E+1, H]^T, as column-major C = op(A) op(B)
-        std::unique_lock<std::mutex> blas_lock;
-        cublasHandle_t h = blas_handle(st, blas_lock);
-        if (!h) {
-            set_error("cuBLAS handle for the router GEMM could not be created");
-            return FM_ECUDA;
-        }
-        const float one = 1.0f, zero = 0.0f;
-        const cublasStatus_t bs = cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, gemm_rows, T, H, &one, router, CUDA_R_16BF, H, xb,
-                                               CUDA_R_16BF, H, &zero, logits, CUDA_R_32F, ld, CUBLAS_COMPUTE_32F,
-                                               CUBLAS_GEMM_DEFAULT);
-        // a library GEMM: not counted by fm_launch_count, which counts this library's own kernels
-        if (bs != CUBLAS_STATUS_SUCCESS) {
-            set_error("router GEMM (cublasGemmEx) failed: status %d", (int)bs);
-            return FM_ECUDA;
-        }
-    } else {
-        dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM, ks);
-        router_logits_kernel<<<grid, 128, 0, st>>>(xb, router, logits, T, E + 1, H);
-        FM_LAUNCH_CHECK("router_logits");
-    }
-    if (topk8) {
-        const uint16_t* gate_row = gate_in_topk ? router + (size_t)E * H : nullptr;
+    const int ld = E + 1;
+    dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM, ks);
+    router_logits_kernel<<<grid, 128, 0, st>>>(xb, router, logits, T, E + 1, H);
+    FM_LAUNCH_CHECK("router_logits");
+    if (E <= 256) {
         if (ks > 1)   // one warp per CTA: each token's ks x (E + 1) partial logits stream into its own SM
-            router_topk8_kernel<true><<<T, 32, 0, st>>>(logits, ld, ks, bias, T, E, k, probs, idx, w, sgate, xb,
-                                                        gate_row, H);
+            router_topk8_kernel<true><<<T, 32, 0, st>>>(logits, ld, ks, bias, T, E, k, probs, idx, w, sgate);
         else
-            router_topk8_kernel<false><<<(T + 7) / 8, 256, 0, st>>>(logits, ld, ks, bias, T, E, k, probs, idx, w, sgate,
-                                                                    xb, gate_row, H);
+            router_topk8_kernel<false><<<(T + 7) / 8, 256, 0, st>>>(logits, ld, ks, bias, T, E, k, probs, idx, w, sgate);
         FM_LAUNCH_CHECK("router_topk8");
     } else {
         router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, ld, bias, T, E, k, ks, probs, idx, w, sgate);

@@ -28,7 +28,9 @@ Q4_1_BYTES = 20
 
 @dataclass(frozen=True)
 class MoEConfig:
-    """The layer geometry (C30 = 2048/128/8/768/0, C36 = 2048/256/8/512/512)."""
+    """The layer geometry: hidden size, router width, top-k, routed and shared expert intermediate sizes, and
+    the expert range this rank holds (e.g. 2048/128/8/768/0 for a Qwen3-30B-A3B-shaped layer,
+    2048/256/8/512/512 for a Qwen3.6-MoE-shaped one)."""
     hidden: int = 2048
     n_experts: int = 128
     top_k: int = 8
@@ -209,14 +211,13 @@ class MoELayer:
                           router.data_ptr(), _ptr(self.router_bias))
         self._ws: torch.Tensor | None = None
 
-    PATHS = {"auto": 0, "mma": 1, "tc": 2, "gemv": 3, "tc2": 4}
+    PATHS = {"auto": 0, "tc": 2, "gemv": 3, "tc2": 4}
 
     @property
     def path(self) -> str:
-        """Kernel choice: "auto" (the GEMV up to 128 tokens while tokens x top_k <= 1024, else tcgen05
-        from 64 tokens and mma.sync below), or forced "mma", "tc" (tcgen05, one CTA per item), "tc2"
-        (tcgen05 as CTA pairs where the band counts allow), "gemv" (the GEMV, within the same limits;
-        mma.sync past them)."""
+        """Kernel choice: "auto" (the GEMV up to 128 tokens while tokens x top_k <= 1024, else the tcgen05
+        grouped GEMM), or forced "tc" (tcgen05, one CTA per item), "tc2" (tcgen05 as CTA pairs where the
+        band counts allow), "gemv" (the GEMV, within the same limits; tcgen05 past them)."""
         return {v: k for k, v in self.PATHS.items()}[self._L.flags]
 
     @path.setter

@@ -194,6 +194,44 @@ def moe_block_f64(xm, res, idx, w, gate_blocks, up_blocks, down_blocks, t_real=N
     return out
 
 
+def moe_rows_f64(rows, xm, res, idx, w, gate_blocks, up_blocks, down_blocks, shared=None, e_begin: int = 0):
+    """``moe_block_f64`` for the token rows ``rows`` only (out f64 [len(rows), H]).
+
+    The block is per token once the routing is fixed (``core.cpp:5236-5255`` adds each token's own expert
+    terms into its own row; the shared expert and its gate are per token, ``core.cpp:4342-4380``), so a
+    sample of rows of a full-size call is checked exactly as the whole call would be, at the cost of the
+    experts those rows touch. ``gate_blocks[e]`` etc. may be any indexable of per-expert GGUF Q4_1 blocks
+    (numpy arrays or device tensors, fetched and dequantised once per touched expert); expert e of the
+    routing is entry ``e - e_begin``.
+    """
+    rows = np.asarray(rows, np.int64)
+    xm = np.asarray(xm, np.float32)[rows]
+    out = np.asarray(res, np.float64)[rows].copy()
+    idx = np.asarray(idx)[rows]
+    wf = np.asarray(w, np.float64)[rows]
+    xb = bf16_round(xm)
+
+    def host(b):
+        if hasattr(b, "cpu"):   # a torch tensor: bf16 values widen to f32 exactly, bytes stay bytes
+            return (b.float() if str(b.dtype) == "torch.bfloat16" else b).cpu().numpy()
+        return np.asarray(b)
+
+    if shared is not None:
+        sg_b, su_b, sd_b, sgw = shared
+        sh = expert_ffn_f64(xb, dequant_q4_1(host(sg_b)), dequant_q4_1(host(su_b)), dequant_q4_1(host(sd_b)))
+        out += shared_gate(xm, host(sgw).astype(np.float32))[:, None] * sh
+    # y of every sampled (row, slot) pair, one expert at a time (each touched expert dequantised once)
+    y = np.zeros(idx.shape + (xm.shape[1],), np.float64)
+    for e in sorted(set(int(v) for v in idx.reshape(-1))):
+        ri, si = np.nonzero(idx == e)
+        g, u, d = (dequant_q4_1(host(b[e - e_begin])) for b in (gate_blocks, up_blocks, down_blocks))
+        y[ri, si] = expert_ffn_f64(xb[ri], g, u, d)
+    for i in range(len(rows)):
+        for s in np.argsort(idx[i], kind="stable"):       # ascending expert, the visit order
+            out[i] += wf[i, s] * y[i, s]
+    return out
+
+
 class MoeLayerF32:
     """The timed CPU baseline: NumPy fp32 + BLAS restatement of the block.
 

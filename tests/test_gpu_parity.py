@@ -143,14 +143,15 @@ def _run_block(c, dev, t_real=None, path="auto"):
 
 @pytest.mark.parametrize("T,path", [(16, "auto"), (1, "auto"), (32, "auto"), (16, "tc"), (1, "tc")])
 def test_moe_block_config1(dev, T, path):
-    """BASELINE config 1 geometry (C30: H 2048, E 128, F 768, top-8, no shared), both kernel paths."""
-    c = cases.make_case(T=T, seed=0)
+    """Config 1 (C30: H 2048, E 128, F 768, top-8, no shared) with its weight recipe (f32 N(0, 0.02)
+    quantised to Q4_1), both kernel paths."""
+    c = cases.make_case(T=T, seed=0, weights="normal")
     layer, x, res, idx, w, out = _run_block(c, dev, path=path)
     ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"])
     assert _rel(out, ref, c["res"]) < TOL
 
 
-@pytest.mark.parametrize("path", ["mma", "tc", "gemv"])
+@pytest.mark.parametrize("path", ["tc", "tc2", "gemv"])
 def test_moe_block_shared_expert_and_padding(dev, path):
     """C36-shaped (shared expert + sigmoid gate) at small E, with rows past t_real carried."""
     c = cases.make_case(H=2048, E=16, F=512, FS=512, k=8, T=24, seed=1)
@@ -160,7 +161,7 @@ def test_moe_block_shared_expert_and_padding(dev, path):
     np.testing.assert_array_equal(out[21:], c["res"][21:])
 
 
-@pytest.mark.parametrize("path", ["mma", "tc", "gemv"])
+@pytest.mark.parametrize("path", ["tc", "tc2", "gemv"])
 def test_moe_block_all_rows_padding(dev, path):
     """t_real = 0: every row is padding and is carried as res exactly (core.cpp:5155), shared expert off."""
     c = cases.make_case(H=2048, E=16, F=512, FS=512, k=8, T=16, seed=3)
@@ -170,12 +171,12 @@ def test_moe_block_all_rows_padding(dev, path):
 
 def test_moe_layer_fused_matches_staged(dev):
     c = cases.make_case(H=2048, E=32, F=256, FS=256, k=8, T=40, seed=2)
-    layer, x, res, idx, w, out = _run_block(c, dev, path="mma")
+    layer, x, res, idx, w, out = _run_block(c, dev, path="gemv")   # a fixed summation order: bit-comparable
     fused = layer.forward(x, res).cpu().numpy()
     np.testing.assert_allclose(fused, out, rtol=0, atol=0)
 
 
-@pytest.mark.parametrize("path", ["mma", "tc"])
+@pytest.mark.parametrize("path", ["tc", "tc2"])
 def test_moe_block_prefill_sized(dev, path):
     """T=512 over several dispatch chunks and 256-row work items (C30 prefill shape, fewer experts to
     keep the oracle fast)."""
@@ -267,33 +268,6 @@ def test_gemv_every_token_width(dev, shared):
     out = layer.moe_block(x, res, idx, w, shared_gate=sg).cpu().numpy()
     ref = OM.moe_block_f64(c["x"], c["res"], idx_h, w_h, c["gate"], c["up"], c["down"], shared=c["shared"])
     assert _rel(out, ref, c["res"]) < TOL
-
-
-def test_tc_headline_shape_matches_mma(dev):
-    """The headline shape (C36: 256 experts, F 512 + shared 512, T = 8192 tokens) through the tcgen05
-    path, several calls, against the mma.sync path on the same weights and routing (that path matches
-    the fp64 oracle on the small cases)."""
-    import flowmoe
-    from flowmoe.synth import C36, synth_layer, synth_tokens
-    layer = synth_layer(flowmoe.MoEConfig(**C36), seed=3)
-    x, res = synth_tokens(8192, 2048, seed=4)
-    layer.path = "mma"
-    ref = layer.forward(x, res).clone()
-    scale = (ref - res).abs().max().item()
-    layer.path = "tc"
-    for _ in range(4):
-        out = layer.forward(x, res)
-        assert (out - ref).abs().max().item() / scale < TOL
-
-
-def test_tc_matches_mma_path(dev):
-    """The two kernel paths agree with each other far inside the oracle tolerance."""
-    c = cases.make_case(H=2048, E=8, F=128, FS=128, k=2, T=300, seed=7)
-    outs = []
-    for path in ("mma", "tc"):
-        layer, x, res, idx, w, out = _run_block(c, dev, path=path)
-        outs.append(out)
-    assert _rel(outs[1], outs[0], c["res"]) < 2e-3
 
 
 @pytest.mark.parametrize("H,F,FS,T,seed", [(2048, 128, 128, 300, 7), (256, 256, 128, 700, 8), (512, 192, 0, 90, 9)])

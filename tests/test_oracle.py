@@ -110,6 +110,22 @@ def test_dispatch_stable_and_checked():
         OM.dispatch(np.array([[3]], np.int32), 3)
 
 
+def test_sampled_rows_equal_whole_block():
+    """moe_rows_f64 (the checker of the full-size GPU calls) gives the whole-block oracle's rows exactly,
+    shared expert and an expert offset (expert-parallel weights) included."""
+    from oracle import cases
+    c = cases.make_case(H=256, E=8, F=128, FS=128, k=3, T=20, seed=4)
+    _, idx, w = OM.router_block(c["x"], c["Wr"], c["k"])
+    whole = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
+    rows = np.array([17, 0, 5, 11])
+    got = OM.moe_rows_f64(rows, c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
+    np.testing.assert_allclose(got, whole[rows], rtol=0, atol=1e-12)
+    keep = np.nonzero((idx >= 2).all(axis=1))[0]   # tokens whose experts are all >= 2
+    got2 = OM.moe_rows_f64(keep, c["x"], c["res"], idx, w, c["gate"][2:], c["up"][2:], c["down"][2:],
+                           shared=c["shared"], e_begin=2)
+    np.testing.assert_allclose(got2, whole[keep], rtol=0, atol=1e-12)
+
+
 def test_cpu_baseline_matches_fp64():
     rng = np.random.default_rng(3)
     H, E, F, T = 256, 8, 128, 12
