@@ -13,8 +13,9 @@ rank r holds experts [r * 256 / N, (r + 1) * 256 / N), router and shared expert 
 stores over NVLink, each rank runs its experts, the y rows come back the same way, then the combine
 (--ep nccl: the NCCL all-to-all variant instead); weak scaling, the tokens per GPU stay fixed.
   value   tokens/s of the whole job, inputs resident on the device, CUDA events, max over ranks;
-  e2e     the same through the public API with pinned host buffers: x (bf16) and res (f32) copied
-          in and out (f32) copied back inside each timed step;
+  e2e     the same through the public API with pinned host buffers (flowmoe.HostPipeline): every step
+          copies x (bf16) and res (f32) in and out (f32) back inside the timed region, the copies of
+          neighbouring steps overlapping the kernels on their own streams;
   roofline the dominant kernel (gate_up expert GEMM): algorithmic FLOPs / its event-timed duration
           inside the timed region vs the measured dense bf16 peak (MEASURED_PEAKS.json);
   cpu_baseline the oracle port (NumPy fp32 + BLAS on all host cores) on a bounded token sample,
@@ -468,16 +469,17 @@ def run_flowmoe(args):
             def step():
                 layer(x, res, out=out, idx=idx)
 
-            def forward_into(xd, rd):
-                return layer(xd, rd, out=out, idx=idx)
+            def forward_into(xd, rd, od):
+                return layer(xd, rd, out=od, idx=idx)
         else:
             layer = EPMoELayer(base, max_tokens=T)
 
             def step():
                 layer(x, res, timings=ep_info)
 
-            def forward_into(xd, rd):
-                return layer(xd, rd)
+            def forward_into(xd, rd, od):
+                od.copy_(layer(xd, rd))
+                return od
     else:
         blocks = synth_blocks(cfg, seed=0)
         gate, up, down, wr, shared = blocks
@@ -487,8 +489,8 @@ def run_flowmoe(args):
         w = torch.empty(T, cfg.top_k, device="cuda")
         step = lambda: layer.forward(x, res, out=out, idx=idx, w=w)  # noqa: E731
 
-        def forward_into(xd, rd):
-            return layer.forward(xd, rd, out=out, idx=idx, w=w)
+        def forward_into(xd, rd, od):
+            return layer.forward(xd, rd, out=od, idx=idx, w=w)
 
     # device-resident timing, with the stage events recorded live in the timed region
     for _ in range(args.warmup):
@@ -523,20 +525,31 @@ def run_flowmoe(args):
     # beside the dispatch (one GPU) or the row exchange (expert parallel)
     gu_tflops = gate_up_flops(cfg, pairs, 0) / (gu_ms * 1e-3) / 1e12
 
-    # end to end through the public API with host buffers
+    # end to end through the public API with host buffers: flowmoe.HostPipeline streams each step's inputs
+    # from pinned host memory and its output back, the copies of neighbouring steps overlapping the kernels
     xh = x.cpu().pin_memory()
     rh = res.cpu().pin_memory()
     oh = torch.empty(T, cfg.hidden, dtype=torch.float32).pin_memory()
-    xd, rd = torch.empty_like(x), torch.empty_like(res)
-
-    def e2e_step():
-        xd.copy_(xh, non_blocking=True)
-        rd.copy_(rh, non_blocking=True)
-        oh.copy_(forward_into(xd, rd), non_blocking=True)
-
-    e2e_ms = max_over_ranks(time_steps(e2e_step, args.steps, 2, world, st), world)
+    pipe = flowmoe.HostPipeline(layer if world == 1 else base, T,
+                                call=lambda xd, rd, od, t_real: forward_into(xd, rd, od))
+    for _ in range(2):
+        pipe.submit(xh, rh, oh)
+    pipe.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record(st)
+    pipe.wait_on(st)
+    for _ in range(args.steps):
+        pipe.submit(xh, rh, oh)
+    pipe.join(st)
+    eb.record(st)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(ea.elapsed_time(eb) / args.steps, world)
     e2e = {"value": round(T * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
-           "h2d_bytes_per_step": x.numel() * 2 + res.numel() * 4, "d2h_bytes_per_step": oh.numel() * 4}
+           "h2d_bytes_per_step": x.numel() * 2 + res.numel() * 4, "d2h_bytes_per_step": oh.numel() * 4,
+           "api": "flowmoe.HostPipeline (host->device, layer, device->host on three streams, two slots)"}
 
     ep_stack = ep_stack_measure(rank, world, args) if world > 1 and args.ep == "peer" and args.ep_stack else None
 

@@ -55,26 +55,33 @@ constexpr int TC_EPI_LD = 132;             // padded f32 row of the DOWN staging
 constexpr int TC_HALF_BYTES = 32 * TC_EPI_LD * 4;            // one epilogue half's staging area
 constexpr int TC_EPI_BYTES = 2 * TC_HALF_BYTES + 2 * 256 * 4;   // two halves + token / weight lists
 
-// Shared-memory layout: 2 dequantised A stages, 6 raw weight tiles, and 128 KB of activation stages
-// (4 of 256 rows for one CTA per item, 8 of 128 rows for a CTA-pair member).
-template <bool PAIR>
+// Shared-memory layout. gate_up (K = 2048: 32 slabs per item, a light epilogue): 4 dequantised A stages,
+// 4 raw weight tiles, the gate/up exchange and h staging of one epilogue half (12 KB); down (K = 512, two
+// epilogue halves with 32 x 132 f32 staging each and the token / weight lists): 2 A stages, 6 raw tiles.
+// Both: 128 KB of activation stages (4 of 256 rows for one CTA per item, 8 of 128 rows for a CTA-pair
+// member). Two dequantiser groups take alternate slabs, so with 4 A stages each group has a second
+// stage to fill while the tensor core still reads its first.
+template <bool GATE_UP, bool PAIR>
 struct TcSmem {
-    static constexpr int SA = 2;
+    static constexpr int SA = GATE_UP ? 4 : 2;
     static constexpr int SB = PAIR ? 8 : 4;
-    static constexpr int SR = 6;                  // raw weight tiles in flight (streamed from HBM)
+    static constexpr int SR = GATE_UP ? 4 : 6;    // raw weight tiles in flight (streamed from HBM)
     static constexpr int B_STAGE = PAIR ? TC_B_BYTES / 2 : TC_B_BYTES;
+    static constexpr int EPI = GATE_UP ? 3 * 16 * 64 * 4 : TC_EPI_BYTES;
     // offsets from the 1024-aligned dynamic smem base
     static constexpr int a = 0;
     static constexpr int b = a + SA * TC_A_BYTES;
     static constexpr int raw = b + SB * B_STAGE;
     static constexpr int epi = raw + SR * kTileBytes;
-    static constexpr int bars = epi + TC_EPI_BYTES;
+    static constexpr int bars = epi + EPI;
     // raw, activation, A and accumulator rings + drain
     static constexpr int nbars = 2 * SR + 2 * SB + 2 * SA + 4 + 1;
     static constexpr int tmem = bars + nbars * 8;
     static constexpr int total = tmem + 16 + 1024;   // + alignment slack
 };
-static_assert(TcSmem<true>::total <= 232448 && TcSmem<false>::total <= 232448, "shared memory per CTA");
+static_assert(TcSmem<true, true>::total <= 232448 && TcSmem<true, false>::total <= 232448 &&
+                  TcSmem<false, true>::total <= 232448 && TcSmem<false, false>::total <= 232448,
+              "shared memory per CTA");
 
 struct TcArgs {
     const int* list;
@@ -181,7 +188,7 @@ template <bool GATE_UP, bool PAIR>
 __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel(const __grid_constant__ CUtensorMap bmap,
                                                                   const __grid_constant__ CUtensorMap bmap_big, TcArgs a) {
     using R = TcRoles<GATE_UP>;
-    using Sm = TcSmem<PAIR>;
+    using Sm = TcSmem<GATE_UP, PAIR>;
     constexpr int SA = Sm::SA, SB = Sm::SB, SR = Sm::SR, B_STAGE = Sm::B_STAGE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -372,10 +379,10 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                 const int rs = sc % SR, as = sc % SA;
                 const uint32_t rph = (sc / SR) & 1, aph = (sc / SA) & 1;
                 if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[rs], rph))) { ok = false; break; }
-                const uint8_t* raw = smem + Sm::raw + rs * kTileBytes;
-                const uint4 n0 = gguf_order(*reinterpret_cast<const uint4*>(raw + r * 32));
-                const uint4 n1 = gguf_order(*reinterpret_cast<const uint4*>(raw + r * 32 + 16));
-                const uint2 sc2 = *reinterpret_cast<const uint2*>(raw + kTileNibBytes + r * 8);
+                const uint32_t raw = smem_u32(smem + Sm::raw + rs * kTileBytes);
+                const uint4 n0 = gguf_order(lds128(raw + r * 32));
+                const uint4 n1 = gguf_order(lds128(raw + r * 32 + 16));
+                const uint2 sc2 = lds64(raw + kTileNibBytes + r * 8);
                 const float d0 = __half2float(__ushort_as_half((unsigned short)(sc2.x & 0xFFFF)));
                 const float m0 = __half2float(__ushort_as_half((unsigned short)(sc2.x >> 16)));
                 const float d1 = __half2float(__ushort_as_half((unsigned short)(sc2.y & 0xFFFF)));
@@ -391,9 +398,9 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                 fence_proxy_async_smem();
                 mbar_arrive(&raw_empty[rs]);
                 if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[as], aph ^ 1))) { ok = false; break; }
-                uint8_t* arow = smem + Sm::a + as * TC_A_BYTES + r * 128;
+                const uint32_t arow = smem_u32(smem + Sm::a + as * TC_A_BYTES + r * 128);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = ch[c];
+                for (int c = 0; c < 8; ++c) sts128(arow + ((c ^ (r & 7)) << 4), ch[c]);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {   // the warp's 32 rows are in place (on the first CTA's barrier)
@@ -662,7 +669,8 @@ int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
     a.err = L.err;
     int sms = device_sm_count();
     if (L.max_ctas > 0 && L.max_ctas < sms) sms = L.max_ctas;
-    const int sm_single = TcSmem<false>::total, sm_pair = TcSmem<true>::total;
+    const int sm_single = gate_up ? TcSmem<true, false>::total : TcSmem<false, false>::total;
+    const int sm_pair = gate_up ? TcSmem<true, true>::total : TcSmem<false, true>::total;
     cudaError_t e;
     if (L.cta_pair) {
         // one pair per two SMs; items are band pairs

@@ -9,10 +9,16 @@ namespace fm {
 
 int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st);
 int launch_rmsnorm_bf16(const float* x, const uint16_t* w, float eps, int T, int H, uint16_t* xb, cudaStream_t st);
-// The router of T tokens (idx, w, sgate, optional probs). From kRouterTcMinT tokens with E + 1 <= 272
-// the fused tcgen05 kernel (router_tc.cu; logits stay on chip, bounded waits report FM_ETIMEOUT in
-// err[1]), else the logits kernel (split-K at small T, into `logits`) and a top-k kernel.
+// The router of T tokens (idx, w, sgate, optional probs): the logits into `logits`, from kRouterTcMinT
+// tokens (E <= 496) by the tcgen05 kernel of router_tc.cu (row stride router_tc_ld(E); bounded waits
+// report FM_ETIMEOUT in err[1]), below by the split-K logits kernel; then a top-k kernel.
 constexpr int kRouterTcMinT = 256;
+bool router_tc_ok(int T, int E, int k);
+int router_tc_ld(int E);
+int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
+                  float* logits, float* probs, int32_t* idx, float* w, float* sgate, int* err, cudaStream_t st);
+int launch_router_tc_logits(const uint16_t* xb, const uint16_t* router, int T, int H, int E, float* logits, int* err,
+                            cudaStream_t st);
 // The per-device side stream of the tcgen05 path (shared expert), created now if it does not exist yet.
 int prepare_side_stream();
 bool router_tc_ok(int T, int E, int k);

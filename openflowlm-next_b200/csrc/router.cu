@@ -1,7 +1,7 @@
-// Router below the prefill sizes: a split-K logits kernel (bf16 x bf16 -> f32 on the warp-level tensor
-// cores; the decode sizes are bound by reading the router weights, so the K split spreads that read
-// over the SMs) and the per-token softmax / top-k. From kRouterTcMinT tokens (E + 1 <= 272) the fused
-// tcgen05 kernel of router_tc.cu takes over; larger routers run the logits kernel unsplit.
+// Router: the logits GEMM and the per-token softmax / top-k. Below the prefill sizes the logits come from
+// a split-K kernel (bf16 x bf16 -> f32 on the warp-level tensor cores; the decode sizes are bound by
+// reading the router weights, so the K split spreads that read over the SMs); from kRouterTcMinT tokens
+// from the tcgen05 kernel of router_tc.cu (routers of more than 496 experts: the logits kernel unsplit).
 //
 // Follows host::router_block (src/open_qwen36/block_host.cpp:766-803): float logits, max
 // subtraction, float exp with a double denominator, p = e * float(1/denom), top-k by probability
@@ -310,7 +310,7 @@ int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st) {
 // K chunks of the router GEMM: enough CTAs to cover the SMs when few tokens give few tiles. The logits
 // rows hold E + 1 values (the last is the shared-gate logit).
 size_t router_scratch_bytes(int T, int H, int E) {
-    if (router_tc_ok(T, E, 1)) return 0;   // the fused kernel keeps its logits in TMEM
+    if (router_tc_ok(T, E, 1)) return (size_t)T * router_tc_ld(E) * 4;
     return (size_t)router_ksplit(T, H, E) * T * (E + 1) * 4;
 }
 
@@ -324,12 +324,16 @@ int router_ksplit(int T, int H, int E) {
 
 int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
                   float* logits, float* probs, int32_t* idx, float* w, float* sgate, int* err, cudaStream_t st) {
-    if (router_tc_ok(T, E, k)) return launch_router_tc(xb, router, bias, T, H, E, k, probs, idx, w, sgate, err, st);
-    const int ks = router_ksplit(T, H, E);
-    const int ld = E + 1;
-    dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM, ks);
-    router_logits_kernel<<<grid, 128, 0, st>>>(xb, router, logits, T, E + 1, H);
-    FM_LAUNCH_CHECK("router_logits");
+    const bool tc = router_tc_ok(T, E, k);
+    const int ks = tc ? 1 : router_ksplit(T, H, E);
+    const int ld = tc ? router_tc_ld(E) : E + 1;
+    if (tc) {
+        if (int rc = launch_router_tc_logits(xb, router, T, H, E, logits, err, st)) return rc;
+    } else {
+        dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM, ks);
+        router_logits_kernel<<<grid, 128, 0, st>>>(xb, router, logits, T, E + 1, H);
+        FM_LAUNCH_CHECK("router_logits");
+    }
     if (E <= 256) {
         if (ks > 1)   // one warp per CTA: each token's ks x (E + 1) partial logits stream into its own SM
             router_topk8_kernel<true><<<T, 32, 0, st>>>(logits, ld, ks, bias, T, E, k, probs, idx, w, sgate);

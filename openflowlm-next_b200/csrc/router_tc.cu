@@ -1,19 +1,18 @@
-// Prefill-size router on the 5th-generation tensor cores, fused with the softmax top-k: one CTA per 128
-// tokens computes the [128 x (E + 1)] logits of its tokens (the E router rows and the shared-expert gate
-// row) into TMEM and turns them into the routing in the same kernel, so the logits never leave the SM.
+// Prefill-size router logits on the 5th-generation tensor cores: logits[t][0..E] = xb[t] . router[0..E]
+// (the E router rows and the shared-expert gate row) in f32, for the router_topk8 kernel that follows.
+// CTA (token tile of 128, column half): a tile's two CTAs each take half of the E + 1 columns (rounded
+// to 16), so a 8192-token call runs on 128 CTAs, and the second reads the tile's activations from L2.
 //
-//   warp 0     TMA producer: per 64-wide K slab, the 128 token rows of xb and the E + 1 router rows
-//              (rows past E + 1, up to a multiple of 16, read as zeros), 4 stages;
-//   warp 1     TMEM owner and MMA issuer: tcgen05.mma M = 128 tokens, N = E + 1 rounded up to 16 (two
-//              MMAs when that is more than 256), K = 16, bf16 in, f32 accumulation;
-//   warps 2-5  one thread per token (TMEM lane): max, softmax denominator and top-k over the token's
-//              accumulator row, read back from TMEM 32 columns at a time.
+//   warp 0     TMA producer: per 64-wide K slab, the 128 token rows of xb and the CTA's router rows (rows
+//              past E + 1 read as zeros), 4 stages;
+//   warp 1     TMEM owner and MMA issuer: tcgen05.mma M = 128 tokens, N = the CTA's columns, K = 16, bf16
+//              in, f32 accumulation;
+//   warps 2-5  epilogue: thread = token (TMEM lane), 32 columns per tcgen05.ld, 16-byte stores of its
+//              logits row segment (row stride ld, a multiple of 4).
 //
-// The routing follows host::router_block (src/open_qwen36/block_host.cpp:766-803) as the other router
-// kernels do: logits + bias, max subtraction, float exp with a double denominator, p = e * float(1/den),
-// top-k by probability with the lowest index on a tie (experts are taken in ascending order and a later
-// one must be strictly larger to pass an earlier one), weights renormalised by a double sum; the
-// shared-expert gate is sigmoid of the gate row's logit (core.cpp:4370-4373).
+// The top-k of each token (softmax, lowest index on a tie, renormalised; host::router_block,
+// src/open_qwen36/block_host.cpp:766-803) runs in router_topk8 with one warp per token: routing 128
+// tokens inside this CTA would serialise 128 dependent shuffle chains on four warps.
 // Every mbarrier wait is bounded: a give-up records FM_ETIMEOUT in err[1] and the CTA drains and exits.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -27,56 +26,22 @@ constexpr int RT_A_BYTES = RT_BM * 128;    // 128 token rows x 64 bf16
 constexpr int RT_THREADS = 192;
 
 struct RouterTcArgs {
-    const float* bias;
-    int T, E, k;
-    int ntot;        // MMA columns: E + 1 rounded up to 16 (<= 272)
-    int nbox;        // router boxes per stage (1, or 2 when ntot > 256)
-    int box_rows;    // rows per router box (ntot / nbox)
+    int T, E;
+    int ncols;       // MMA columns of one CTA (a multiple of 16, <= 256)
     int slabs;       // H / 64
-    float* probs;
-    int32_t* idx;
-    float* w;
-    float* sgate;
+    float* logits;   // [T, ld] f32
+    int ld;
     int* err;
 };
 
 __host__ __device__ constexpr int rt_stage_bytes(int ntot) { return RT_A_BYTES + ntot * 128; }
 
-// One (p, e) offered to a descending top list of k entries (ties: the earlier expert first). Experts
-// arrive in ascending order, so the new one passes an entry only when strictly larger; once it has
-// displaced an entry, the displaced one (earlier than every entry after it) passes equal entries.
-// kth tracks tv[k - 1] (kept apart so that no register array is indexed at run time).
-template <int KMAX>
-__device__ __forceinline__ void topk_offer(float (&tv)[KMAX], int (&ti)[KMAX], float& kth, int k, float p, int e) {
-    if (!(p > kth)) return;
-    float cv = p;
-    int ci = e;
-    bool carried = false;
-#pragma unroll
-    for (int j = 0; j < KMAX; ++j) {
-        if (j < k && (carried ? cv >= tv[j] : cv > tv[j])) {
-            const float t = tv[j];
-            const int u = ti[j];
-            tv[j] = cv;
-            ti[j] = ci;
-            cv = t;
-            ci = u;
-            carried = true;
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < KMAX; ++j)
-        if (j == k - 1) kth = tv[j];
-}
-
-template <int KMAX>
 __global__ void __launch_bounds__(RT_THREADS, 1) router_tc_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                    const __grid_constant__ CUtensorMap wmap, RouterTcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int stage_bytes = rt_stage_bytes(a.ntot);
-    float* sbias = reinterpret_cast<float*>(smem + RT_STAGES * stage_bytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sbias + ((a.E + 3) & ~3));
+    const int stage_bytes = rt_stage_bytes(a.ncols);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + RT_STAGES * stage_bytes);
     uint64_t* full = bars;
     uint64_t* empty = full + RT_STAGES;
     uint64_t* acc_full = empty + RT_STAGES;
@@ -84,8 +49,8 @@ __global__ void __launch_bounds__(RT_THREADS, 1) router_tc_kernel(const __grid_c
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * RT_BM;
-    for (int e = threadIdx.x; e < a.E; e += RT_THREADS) sbias[e] = a.bias ? a.bias[e] : 0.f;
+    const int m0 = (blockIdx.x >> 1) * RT_BM;           // the token tile
+    const int n0 = (blockIdx.x & 1) * a.ncols;          // the CTA's first column
     if (threadIdx.x == 0) {
         for (int i = 0; i < RT_STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
         mbar_init(acc_full, 1);
@@ -95,7 +60,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1) router_tc_kernel(const __grid_c
         prefetch_tmap(&wmap);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 512);
+        tmem_alloc(tmem_slot, 256);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -114,8 +79,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1) router_tc_kernel(const __grid_c
                 mbar_expect_tx(&full[st], stage_bytes);
                 uint8_t* A = smem + st * stage_bytes;
                 tma_load_2d(A, &xmap, s * 64, m0, &full[st]);
-                for (int j = 0; j < a.nbox; ++j)
-                    tma_load_2d(A + RT_A_BYTES + j * a.box_rows * 128, &wmap, s * 64, j * a.box_rows, &full[st]);
+                tma_load_2d(A + RT_A_BYTES, &wmap, s * 64, n0, &full[st]);
                 issued |= 1u << st;
                 if (++st == RT_STAGES) { st = 0; ph ^= 1; }
             }
@@ -130,9 +94,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1) router_tc_kernel(const __grid_c
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            const int n1 = a.ntot < 256 ? a.ntot : 256;
-            const uint32_t id1 = idesc_bf16(RT_BM, n1);
-            const uint32_t id2 = a.ntot > 256 ? idesc_bf16(RT_BM, a.ntot - 256) : 0u;
+            const uint32_t idesc = idesc_bf16(RT_BM, a.ncols);
             int st = 0;
             uint32_t ph = 0;
             bool ok = true, any = false;
@@ -142,13 +104,9 @@ __global__ void __launch_bounds__(RT_THREADS, 1) router_tc_kernel(const __grid_c
                 const uint32_t sa = smem_u32(smem + st * stage_bytes);
                 const uint32_t sb = sa + RT_A_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint32_t acc = (s > 0 || kk > 0) ? 1u : 0u;
-                    tc_mma_f16(tmem_base, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), id1, acc);
-                    if (a.ntot > 256)
-                        tc_mma_f16(tmem_base + 256, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + 256 * 128 + kk * 32), id2,
-                                   acc);
-                }
+                for (int kk = 0; kk < 4; ++kk)
+                    tc_mma_f16(tmem_base, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc,
+                               (s > 0 || kk > 0) ? 1u : 0u);
                 any = true;
                 tc_commit(&empty[st]);
                 if (++st == RT_STAGES) { st = 0; ph ^= 1; }
@@ -161,76 +119,32 @@ __global__ void __launch_bounds__(RT_THREADS, 1) router_tc_kernel(const __grid_c
             }
         }
     } else {
-        // ---------------------------------------------------------------- epilogue: one thread per token
+        // ---------------------------------------------------------------- epilogue: thread = token
         const int lg = warp & 3;                     // the TMEM lane quarter this warp may read
-        const int row = lg * 32 + lane;
-        const int t = m0 + row;
-        const bool live = t < a.T;
+        const int t = m0 + lg * 32 + lane;
         const bool ok = mbar_wait(acc_full, 0);
         if (!ok) atomicCAS(a.err + 1, 0, FM_ETIMEOUT);
         if (__all_sync(0xffffffffu, ok)) {
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(lg * 32) << 16);
-            const int E = a.E, k = a.k;
-            float mx = -INFINITY;
-            for (int c0 = 0; c0 < E; c0 += 32) {
+            const int ncols = min(a.ncols, a.E + 1 - n0);   // this CTA's real columns
+            float* row = a.logits + (size_t)t * a.ld + n0;
+            for (int c0 = 0; c0 < ncols; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld32(taddr + c0, v);
                 tmem_ld_wait();
+                if (t < a.T) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (c0 + j < E) mx = fmaxf(mx, __uint_as_float(v[j]) + sbias[c0 + j]);
-            }
-            double den = 0.0;
-            for (int c0 = 0; c0 < E; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(taddr + c0, v);
-                tmem_ld_wait();
+                    for (int j = 0; j < 32; j += 4) {
+                        if (c0 + j + 4 <= ncols) {
+                            *reinterpret_cast<float4*>(row + c0 + j) = make_float4(
+                                __uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                __uint_as_float(v[j + 3]));
+                        } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (c0 + j < E) den += (double)expf(__uint_as_float(v[j]) + sbias[c0 + j] - mx);
-            }
-            const float inv = (float)(1.0 / den);
-            float tv[KMAX];
-            int ti[KMAX];
-#pragma unroll
-            for (int j = 0; j < KMAX; ++j) { tv[j] = -1.0f; ti[j] = 0x7fffffff; }
-            float kth = -1.0f;
-            float* prow = (a.probs && live) ? a.probs + (size_t)t * E : nullptr;
-            for (int c0 = 0; c0 < E; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(taddr + c0, v);
-                tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int e = c0 + j;
-                    if (e < E) {
-                        const float p = expf(__uint_as_float(v[j]) + sbias[e] - mx) * inv;
-                        topk_offer<KMAX>(tv, ti, kth, k, p, e);
-                        if (prow) prow[e] = p;
-                    }
-                }
-            }
-            if (a.sgate) {   // the gate row's logit: column E
-                uint32_t v[32];
-                tmem_ld32(taddr + (E & ~31), v);
-                tmem_ld_wait();
-                float gl = 0.f;
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (j == (E & 31)) gl = __uint_as_float(v[j]);
-                if (live) a.sgate[t] = 1.0f / (1.0f + expf(-gl));
-            }
-            if (live) {
-                double wsum = 0.0;
-#pragma unroll
-                for (int s = 0; s < KMAX; ++s)
-                    if (s < k) wsum += (double)tv[s];
-#pragma unroll
-                for (int s = 0; s < KMAX; ++s) {
-                    if (s < k) {
-                        a.idx[(size_t)t * k + s] = ti[s];
-                        a.w[(size_t)t * k + s] = (float)((double)tv[s] / wsum);
+                            for (int q = 0; q < 4; ++q)
+                                if (c0 + j + q < ncols) row[c0 + j + q] = __uint_as_float(v[j + q]);
+                        }
                     }
                 }
             }
@@ -240,41 +154,31 @@ __global__ void __launch_bounds__(RT_THREADS, 1) router_tc_kernel(const __grid_c
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, 512);
+        tmem_dealloc(tmem_base, 256);
     }
 }
 
-bool router_tc_ok(int T, int E, int k) { return T >= kRouterTcMinT && E + 1 <= 272 && k <= kMaxTopK; }
+bool router_tc_ok(int T, int E, int k) { return T >= kRouterTcMinT && E <= 496 && k <= kMaxTopK; }
 
-int launch_router_tc(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
-                     float* probs, int32_t* idx, float* w, float* sgate, int* err, cudaStream_t st) {
+int router_tc_ld(int E) { return (E + 1 + 3) & ~3; }
+
+int launch_router_tc_logits(const uint16_t* xb, const uint16_t* router, int T, int H, int E, float* logits, int* err,
+                            cudaStream_t st) {
     RouterTcArgs a{};
-    a.bias = bias;
     a.T = T;
     a.E = E;
-    a.k = k;
-    a.ntot = (E + 1 + 15) / 16 * 16;
-    a.nbox = (a.ntot + 255) / 256;
-    a.box_rows = a.ntot / a.nbox;
+    a.ncols = ((E + 1 + 1) / 2 + 15) / 16 * 16;   // half of E + 1, rounded up to 16
     a.slabs = H / 64;
-    a.probs = probs;
-    a.idx = idx;
-    a.w = w;
-    a.sgate = sgate;
+    a.logits = logits;
+    a.ld = router_tc_ld(E);
     a.err = err;
     CUtensorMap xmap, wmap;
     if (int rc = make_bmap(&xmap, xb, T, H, H, RT_BM)) return rc;
-    if (int rc = make_bmap(&wmap, router, E + 1, H, H, a.box_rows)) return rc;
-    const int smem = RT_STAGES * rt_stage_bytes(a.ntot) + ((E + 3) & ~3) * 4 + 8 * (2 * RT_STAGES + 2) + 16 + 1024;
-    const int grid = (T + RT_BM - 1) / RT_BM;
-    cudaError_t e;
-    if (k <= 8) {
-        if ((e = raise_smem_limit((const void*)router_tc_kernel<8>, smem))) return cuda_status(e, "router_tc smem");
-        router_tc_kernel<8><<<grid, RT_THREADS, smem, st>>>(xmap, wmap, a);
-    } else {
-        if ((e = raise_smem_limit((const void*)router_tc_kernel<16>, smem))) return cuda_status(e, "router_tc smem");
-        router_tc_kernel<16><<<grid, RT_THREADS, smem, st>>>(xmap, wmap, a);
-    }
+    if (int rc = make_bmap(&wmap, router, E + 1, H, H, a.ncols)) return rc;
+    const int smem = RT_STAGES * rt_stage_bytes(a.ncols) + 8 * (2 * RT_STAGES + 2) + 16 + 1024;
+    const int grid = 2 * ((T + RT_BM - 1) / RT_BM);
+    if (cudaError_t e = raise_smem_limit((const void*)router_tc_kernel, smem)) return cuda_status(e, "router_tc smem");
+    router_tc_kernel<<<grid, RT_THREADS, smem, st>>>(xmap, wmap, a);
     FM_LAUNCH_CHECK("router_tc");
     return FM_OK;
 }

@@ -147,6 +147,38 @@ def pool_to_q4_1(pool, n: int, k: int, rs: int = 2, chunk_bytes: int | None = No
     return out
 
 
+def experts_from_pool(gate_up_pool, down_pool, E: int, F: int, H: int, chunk_bytes: int | None = None,
+                      device="cuda"):
+    """The reference engine's MoE expert pool regions -> per-expert GGUF Q4_1 blocks on the device:
+    (gate [E, F, H/32, 20], up [E, F, H/32, 20], down [E, H, F/32, 20]).
+
+    ``gate_up_pool`` is what the engine's ``expert_stripes`` op writes (src/open_qwen36/pools.cpp:927-950):
+    per expert, per 128-row stripe k, the up stripe then the gate stripe (``[up_k | gate_k]``), each stripe's
+    32-row x 256-column chunks in ``stripe_transpose`` order (open_kernels/recipes/pack.py:525-530), i.e.
+    the chunk law of q4_1_pack.chunk_geometry with band row split 4. ``down_pool`` is what ``expert_down``
+    writes (pools.cpp:951-962): one slice per expert in ``down_perm`` order (recipes/pack.py:515-522), the
+    same law for the F = 512 the reference packs. Chunks are 5120 bytes (bf16 d and m, the q4nx pool) or
+    6144 (f32 d and m); ``chunk_bytes`` is inferred from the sizes when not given."""
+    if F % 128 or H % 256 or F % 256 or H % 128:
+        raise ValueError(f"expert pool geometry needs F % 256 == 0 and H % 256 == 0 (F={F}, H={H})")
+    gu = _as_dev_u8(gate_up_pool, device).reshape(-1)
+    dn = _as_dev_u8(down_pool, device).reshape(-1)
+    nch = E * 2 * F * H // (32 * 256)
+    if chunk_bytes is None:
+        chunk_bytes = gu.numel() // nch if nch and gu.numel() % nch == 0 else 0
+    if gu.numel() != nch * chunk_bytes or dn.numel() * 2 != gu.numel():
+        raise ValueError(f"pool regions of {gu.numel()} and {dn.numel()} bytes are not {E} experts of "
+                         f"[{F}, {H}] up/gate and [{H}, {F}] down in {chunk_bytes}-byte chunks")
+    st = gu.reshape(E, F // 128, 2, -1)
+    dnv = dn.reshape(E, -1)
+    gate, up, down = [], [], []
+    for e in range(E):
+        up.append(pool_to_q4_1(st[e, :, 0].contiguous(), F, H, rs=4, chunk_bytes=chunk_bytes, device=gu.device))
+        gate.append(pool_to_q4_1(st[e, :, 1].contiguous(), F, H, rs=4, chunk_bytes=chunk_bytes, device=gu.device))
+        down.append(pool_to_q4_1(dnv[e], H, F, rs=4, chunk_bytes=chunk_bytes, device=gu.device))
+    return torch.stack(gate), torch.stack(up), torch.stack(down)
+
+
 def narrow_scales(tiles: torch.Tensor) -> torch.Tensor:
     """In place: every d and m of a tile array rounded to bf16 precision (fm_tiles_narrow_scales)."""
     _check_dev_u8(tiles, "tiles")
@@ -258,6 +290,15 @@ class MoELayer:
                 if t is not None:
                     narrow_scales(t)
         return cls(cfg, gate_up.reshape(-1), down.reshape(-1), router, sgu, sdn, router_bias)
+
+    @classmethod
+    def from_expert_pool(cls, cfg: MoEConfig, gate_up_pool, down_pool, router_w, shared=None, device="cuda",
+                         router_bias=None, chunk_bytes: int | None = None):
+        """A layer from the reference engine's expert pool regions (``experts_from_pool``) for this rank's
+        cfg.local experts; router, shared expert and bias as in ``from_q4_1``. 5120-byte chunks carry bf16
+        scales, so the layer computes with the q4nx pool's numerics."""
+        gate, up, down = experts_from_pool(gate_up_pool, down_pool, cfg.local, cfg.ffn, cfg.hidden, chunk_bytes, device)
+        return cls.from_q4_1(cfg, gate, up, down, router_w, shared=shared, device=device, router_bias=router_bias)
 
     # ---- workspace
     def workspace_bytes(self, T: int) -> int:

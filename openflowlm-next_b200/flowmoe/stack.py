@@ -1,10 +1,12 @@
-"""A stack of MoE layers with the post-attention RMSNorm and residual between them:
+"""A stack of MoE layers with the post-attention RMSNorm and residual between them (e.g. the 48 MoE layers
+of a Qwen3.6-MoE-shaped model at a decode batch):
 x_{l+1} = x_l + MoE_l(RMSNorm_l(x_l)), the engine's staged_tail -> ffn_block sequence repeated per layer
 (src/open_qwen36/core.cpp:4934-4957; open_kernels/model/replica.py:121-143). Attention and the rest of a
 transformer block are not part of this path; the stack isolates the MoE half of each layer.
 
 Each layer is one ``fm_moe_layer_norm`` call; ``capture()`` records the whole stack for a fixed token
-count into one CUDA graph (the decode loop of config 5), replayed by ``forward``.
+count into one CUDA graph (a decode loop), replayed by ``forward``. ``flowmoe.profile.StageProfile`` records
+per-layer stage times of an eager pass (``forward(x, layer_hook=...)``) as the reference's JSONL profile.
 """
 from __future__ import annotations
 
@@ -26,22 +28,25 @@ class MoEStack:
         self._graph = None
         self._bufs = None
 
-    def _run(self, x: torch.Tensor, bufs) -> torch.Tensor:
+    def _run(self, x: torch.Tensor, bufs, layer_hook=None) -> torch.Tensor:
         cur = x
         for i, (layer, nw) in enumerate(zip(self.layers, self.norm_ws)):
             nxt = bufs[i & 1]
             layer.forward_norm(cur, nw, self.eps, out=nxt)
+            if layer_hook is not None:
+                layer_hook(i)
             cur = nxt
         return cur
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """x f32 [T, H] -> the stack's output (a new tensor unless a captured graph is replayed)."""
-        if self._graph is not None and x.shape == self._x.shape:
+    def forward(self, x: torch.Tensor, layer_hook=None) -> torch.Tensor:
+        """x f32 [T, H] -> the stack's output (a new tensor unless a captured graph is replayed).
+        ``layer_hook(i)`` (eager passes only) is called after layer i is enqueued."""
+        if self._graph is not None and x.shape == self._x.shape and layer_hook is None:
             self._x.copy_(x)
             self._graph.replay()
             return self._y
         bufs = [torch.empty_like(x), torch.empty_like(x)]
-        return self._run(x, bufs)
+        return self._run(x, bufs, layer_hook)
 
     __call__ = forward
 
@@ -63,8 +68,8 @@ class MoEStack:
 
 
 class EPMoEStack:
-    """The stack across an expert-parallel group (48 layers, decode, experts sharded over
-    the node's GPUs). Each rank holds its expert range of every layer and runs its own tokens; a layer is
+    """The stack across an expert-parallel group (e.g. 48 layers at a decode batch, experts sharded over the
+    node's GPUs). Each rank holds its expert range of every layer and runs its own tokens; a layer is
     ``fm_rmsnorm_bf16`` (xb = RMSNorm_l(x)) then ``fm_ep_peer_layer`` (x <- x + MoE_l(xb) over peer memory).
     All layers share one peer group -- one symmetric buffer, its epochs advancing call by call, since the
     layers have one geometry and run in sequence -- and ``capture()`` records the whole stack into one CUDA

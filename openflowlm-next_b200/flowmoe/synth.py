@@ -1,4 +1,4 @@
-"""Seeded synthetic layers and tokens of the BASELINE configs, generated on the device.
+"""Seeded synthetic layers and tokens of the benchmarked shapes, generated on the device.
 
 Expert weights fp32 N(0, 0.02) quantised to GGUF Q4_1 (``quantize_q4_1``, gguf's algorithm); router
 weight and shared gate bf16 N(0, 0.02); activations bf16 N(0, 1); residual f32 N(0, 1). The prefill
@@ -13,8 +13,8 @@ import torch
 from .layer import MoEConfig, MoELayer
 from .quant import quantize_q4_1
 
-C30 = dict(hidden=2048, n_experts=128, top_k=8, ffn=768, shared_ffn=0)    # Qwen3-30B-A3B-shaped (configs 1-3)
-C36 = dict(hidden=2048, n_experts=256, top_k=8, ffn=512, shared_ffn=512)  # Qwen3.6-MoE-shaped (configs 4-5)
+C30 = dict(hidden=2048, n_experts=128, top_k=8, ffn=768, shared_ffn=0)    # Qwen3-30B-A3B-shaped MoE layer
+C36 = dict(hidden=2048, n_experts=256, top_k=8, ffn=512, shared_ffn=512)  # Qwen3.6-MoE-shaped, shared expert
 
 
 def _gen(seed: int, device) -> torch.Generator:

@@ -1,6 +1,6 @@
 """Writes the golden vectors under tests/golden/ by running the REFERENCE's own Python code.
 
-    python tests/golden/make_golden.py [--ref /path/to/OpenFlowLM-Next]
+    python tests/golden/make_golden.py --ref /path/to/OpenFlowLM-Next    (or OFLM_REFERENCE=/path ...)
 
 Needs the reference tree (read in place; nothing is copied) and ``gguf`` 0.19.0. The GPU box has
 neither, so the fixtures are committed and the tests read only the ``.npz`` files. Each fixture
@@ -18,11 +18,15 @@ Fixtures:
   moe.npz     ``replica.moe_decode`` (fp64, HF-faithful) over 4 tokens of a small Qwen3.6-shaped
               block (H=2048 as replica.py fixes it, E=16, F=128, shared F=128, top-8) whose Q4_1
               experts come from the reference's block generator (seed 0).
+  expert_pool.npz  the SHA-256 of the MoE expert pool regions (gate_up stripes and down slices) the
+              engine's pack ops write for 2 seeded experts (F=512, H=256), built from the reference's
+              own pack_q4_1_pool, stripe_transpose and down_perm, and of their source blocks.
 """
 from __future__ import annotations
 
 import argparse
 import hashlib
+import os
 import sys
 from pathlib import Path
 
@@ -42,8 +46,11 @@ def bf16_vals(a: np.ndarray) -> np.ndarray:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("OFLM_REFERENCE"),
+                    help="the reference tree (required; default: $OFLM_REFERENCE)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("--ref (or OFLM_REFERENCE) must name the reference tree")
     ref = Path(a.ref)
     sys.path[:0] = [str(ref / "open_kernels"), str(ref / "open_kernels" / "model"), str(ref)]
     import gguf
@@ -121,7 +128,35 @@ def main() -> int:
     np.savez_compressed(HERE / "moe.npz", H=H, E=E, F=F, FS=FS, T=T, blocks_sha=sha(allb),
                         postln=postln, Wr=Wr, sgw=sgw, xres=xres, xm=np.array(xms, np.float32),
                         top=np.array(tops, np.int32), probs=np.array(probs), out=np.array(outs))
-    for f in ("q4_1.npz", "router.npz", "moe.npz"):
+    # ---- the MoE expert pool regions the engine packs (pools.cpp:927-962 expert_stripes / expert_down over
+    # recipes/pack.py's stripe_transpose and down_perm), built from the reference's own functions: the
+    # container's plain chunk raster of each matrix (chunk (row block, k-tile) at rb * ncol + kt, which is
+    # pack_q4_1_pool with a row split of 1), then the ops' chunk orders and the [up_k | gate_k] interleave
+    from open_kernels.recipes import pack as RPK
+    Ep, Fp, Hp = 2, 512, 256
+    rng = np.random.default_rng(7)
+    pu = [QP.random_q4_1_blocks(Fp, Hp, rng) for _ in range(Ep)]
+    pg = [QP.random_q4_1_blocks(Fp, Hp, rng) for _ in range(Ep)]
+    pd = [QP.random_q4_1_blocks(Hp, Fp, rng) for _ in range(Ep)]
+    CHB = QP.CH
+    ns, ncol = Fp // 128, Hp // 256
+    tp = RPK.stripe_transpose(Hp)
+    gu_pool, dn_pool = [], []
+    for e in range(Ep):
+        fu = QP.pack_q4_1_pool(pu[e], 1).reshape(-1, CHB)
+        fg = QP.pack_q4_1_pool(pg[e], 1).reshape(-1, CHB)
+        for k in range(ns):
+            for f in (fu, fg):   # [up_k | gate_k]
+                stripe = f[k * 4 * ncol:(k + 1) * 4 * ncol]
+                gu_pool.append(stripe[tp].reshape(-1))
+        fd = QP.pack_q4_1_pool(pd[e], 1).reshape(-1, CHB)
+        dn_pool.append(fd[RPK.down_perm(fd.shape[0])].reshape(-1))
+    gu_pool, dn_pool = np.concatenate(gu_pool), np.concatenate(dn_pool)
+    np.savez_compressed(HERE / "expert_pool.npz", E=Ep, F=Fp, H=Hp, seed=7,
+                        blocks_sha=sha(np.concatenate([b.reshape(-1) for b in pu + pg + pd])),
+                        gate_up_sha=sha(gu_pool), down_sha=sha(dn_pool),
+                        gate_up_bytes=gu_pool.size, down_bytes=dn_pool.size)
+    for f in ("q4_1.npz", "router.npz", "moe.npz", "expert_pool.npz"):
         print(f"wrote {HERE / f} ({(HERE / f).stat().st_size} B)")
     return 0
 

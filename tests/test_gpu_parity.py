@@ -343,3 +343,59 @@ def test_bf16_scales_narrowing(dev, golden):
     ref = OM.moe_block_f64(c["x"], c["res"], idx.cpu().numpy(), w.cpu().numpy(), narrow(c["gate"]), narrow(c["up"]),
                            narrow(c["down"]))
     assert _rel(out, ref, c["res"]) < TOL
+
+
+def test_host_pipeline_matches_direct_calls(dev):
+    """flowmoe.HostPipeline (host->device copy, layer, device->host copy on their own streams, two device
+    slots): five batches from pinned host memory give the direct calls' results bit for bit, each batch in
+    its own host output buffer and in one shared one."""
+    import flowmoe
+    c = cases.make_case(H=2048, E=16, F=512, FS=512, k=8, T=40, seed=14)
+    layer = _layer(c, dev, "gemv")
+    T, H = 40, 2048
+    rng = np.random.default_rng(1)
+    xs = [torch.from_numpy(OM.bf16_round(rng.standard_normal((T, H), dtype=np.float32))).to(torch.bfloat16).pin_memory()
+          for _ in range(5)]
+    rs = [torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).pin_memory() for _ in range(5)]
+    outs = [torch.empty(T, H).pin_memory() for _ in range(5)]
+    pipe = flowmoe.HostPipeline(layer, T)
+    for x, r, o in zip(xs, rs, outs):
+        pipe.submit(x, r, o)
+    pipe.synchronize()
+    for x, r, o in zip(xs, rs, outs):
+        want = layer.forward(x.to(dev), r.to(dev)).cpu()
+        assert torch.equal(o, want)
+    shared = torch.empty(T, H).pin_memory()
+    for x, r in zip(xs, rs):
+        pipe.submit(x, r, shared)
+    pipe.synchronize()
+    assert torch.equal(shared, outs[-1])
+    with pytest.raises(ValueError, match="pinned"):
+        pipe.submit(xs[0], rs[0], torch.empty(T, H))
+
+
+def test_expert_pool_import_bit_exact(dev, golden):
+    """The reference engine's expert pool regions (expert_stripes / expert_down, pools.cpp:927-962; bytes
+    pinned to the reference's own packers by test_expert_pool_matches_reference_bytes) -> per-expert GGUF
+    blocks on the device, bit for bit the oracle's inverse (bf16 scales), and a layer built straight from
+    the pool equals one built from those blocks."""
+    import flowmoe
+    g = golden["expert_pool"]
+    E, F, H = int(g["E"]), int(g["F"]), int(g["H"])
+    rng = np.random.default_rng(int(g["seed"]))
+    up = [OQ.random_q4_1_blocks(F, H, rng) for _ in range(E)]
+    gate = [OQ.random_q4_1_blocks(F, H, rng) for _ in range(E)]
+    down = [OQ.random_q4_1_blocks(H, F, rng) for _ in range(E)]
+    gu, dn = OQ.expert_pool(up, gate, down)
+    gb, ub, db = flowmoe.experts_from_pool(gu, dn, E, F, H, device=dev)
+    per = gu.size // E
+    for e in range(E):
+        st = gu[e * per:(e + 1) * per].reshape(F // 128, 2, -1)
+        assert np.array_equal(ub[e].cpu().numpy(), OQ.pool_to_blocks(st[:, 0].reshape(-1), F, H, 4))
+        assert np.array_equal(gb[e].cpu().numpy(), OQ.pool_to_blocks(st[:, 1].reshape(-1), F, H, 4))
+        assert np.array_equal(db[e].cpu().numpy(), OQ.pool_to_blocks(dn[e * dn.size // E:(e + 1) * dn.size // E], H, F, 4))
+    cfg = flowmoe.MoEConfig(hidden=H, n_experts=E, top_k=1, ffn=F)
+    Wr = OM.bf16_round(rng.normal(0, 0.02, (H, E)).astype(np.float32))
+    a = flowmoe.MoELayer.from_expert_pool(cfg, gu, dn, Wr, device=dev)
+    b = flowmoe.MoELayer.from_q4_1(cfg, gb, ub, db, Wr, device=dev)
+    assert torch.equal(a.gate_up, b.gate_up) and torch.equal(a.down, b.down)

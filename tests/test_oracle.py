@@ -215,3 +215,28 @@ def test_ep_stack_case_flips_only_through_bf16_y():
     a = OM.moe_block_f64(xm, c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
     b = OM.moe_block_f64(xm, c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"], y_bf16=True)
     assert np.abs(a - b).max() <= 2.0 ** -8 * np.abs(a - c["res"]).max()
+
+
+def _expert_pool_case(golden):
+    g = golden["expert_pool"]
+    E, F, H = int(g["E"]), int(g["F"]), int(g["H"])
+    rng = np.random.default_rng(int(g["seed"]))
+    up = [OQ.random_q4_1_blocks(F, H, rng) for _ in range(E)]
+    gate = [OQ.random_q4_1_blocks(F, H, rng) for _ in range(E)]
+    down = [OQ.random_q4_1_blocks(H, F, rng) for _ in range(E)]
+    assert _sha(np.concatenate([b.reshape(-1) for b in up + gate + down])) == str(g["blocks_sha"])
+    return g, E, F, H, up, gate, down
+
+
+def test_expert_pool_matches_reference_bytes(golden):
+    """The oracle's restatement of the engine's expert_stripes / expert_down ops (pools.cpp:927-962 over
+    recipes/pack.py:498-530) writes the very pool bytes the reference's own packers and chunk orders
+    produce for the same seeded experts, and its inverse gives the experts back (bf16 scales)."""
+    g, E, F, H, up, gate, down = _expert_pool_case(golden)
+    gu, dn = OQ.expert_pool(up, gate, down)
+    assert _sha(gu) == str(g["gate_up_sha"]) and _sha(dn) == str(g["down_sha"])
+    per = gu.size // E
+    for e in range(E):
+        st = gu[e * per:(e + 1) * per].reshape(F // 128, 2, -1)
+        u_back = OQ.pool_to_blocks(st[:, 0].reshape(-1), F, H, 4)
+        assert np.array_equal(OQ.dequant_q4_1(u_back), OQ.dequant_q4_1(up[e], bf16_scales=True))
