@@ -631,7 +631,7 @@ def main():
                     help="N > 1: also time BASELINE config 5 (48-layer stack, 64 decode tokens) across the group")
     ap.add_argument("--profile-case", choices=["decode", "decode1", "prefill"], default=None,
                     help="run a few plain layer calls for an ncu capture and exit")
-    ap.add_argument("--profile-path", default="auto", choices=["auto", "tc", "tc2", "gemv"],
+    ap.add_argument("--profile-path", default="auto", choices=["auto", "tc", "gemv"],
                     help="--profile-case: the kernel choice (MoELayer.path)")
     args = ap.parse_args()
     if args.profile_case:

@@ -67,9 +67,7 @@ typedef struct fm_layer {
     int32_t flags;      /* 0 = pick kernels by size (the GEMV up to 128 tokens while T * top_k <= 1024 and
                            e_local < 1024, else the tcgen05 grouped GEMM);
                            2 = force tcgen05, 3 = force the GEMV (within the same limits, tcgen05 past
-                           them), 4 = force tcgen05 as CTA pairs (M = 256 MMAs; when every matrix has an
-                           even number of 128-row bands, else one CTA per item as with 2); any other
-                           value is rejected (FM_EINVAL_SHAPE) */
+                           them); any other value is rejected (FM_EINVAL_SHAPE) */
     const uint8_t* gate_up;   /* tiles, e_local x (2 x F x H x 5/8 B): gate then up, per expert */
     const uint8_t* down;      /* tiles, e_local x (H x F x 5/8 B) */
     const uint8_t* shared_gate_up; /* tiles of the shared expert, or NULL */

@@ -103,17 +103,9 @@ int cuda_status(cudaError_t e, const char* what) {
 // kernels: see kernels.cuh
 
 constexpr int kBN = 64;        // rows per work item the list sizes assume (>= the real items' rows)
-constexpr int kBNTc = 256;     // rows per expert work item (expert_tc)
-constexpr int kFlagTc = 2, kFlagGemv = 3, kFlagTcPair = 4;   // 1 was the retired mma.sync path
+constexpr int kBNTc = kTcItemRows;   // rows per expert work item (expert_tc)
+constexpr int kFlagTc = 2, kFlagGemv = 3;   // 1 and 4 were retired kernel variants
 
-// Flag kFlagTcPair runs the tcgen05 GEMMs as CTA pairs (M = 256 MMAs over band pairs) when every
-// matrix has an even number of 128-row bands. One CTA per item is the default: measured faster on
-// B200 for these shapes (the pair's cross-SM barrier hand-offs cost more than the halved activation
-// traffic saves).
-static bool tc_pair(const fm_layer* L) {
-    return L->flags == kFlagTcPair && (L->ffn / 64) % 2 == 0 && (L->shared_ffn / 64) % 2 == 0 &&
-           (L->hidden / kTileRows) % 2 == 0;
-}
 // The GEMV path up to this many tokens, auto or forced (flags = 3), while T * top_k <= 1024 (the
 // single-CTA dispatch). Measured on B200 from 48 to 128 tokens (C30 and C36 layers): 2.2-2.5x faster
 // than the tcgen05 path, which needs more rows per expert to amortise its dequantisation.
@@ -187,8 +179,8 @@ static int validate(const fm_layer* L, int T) {
         set_error("router_block: topk %d past the expert count %d (or > %d)", k, E, kMaxTopK);
         return FM_EINVAL_SHAPE;
     }
-    if (L->flags != 0 && L->flags != kFlagTc && L->flags != kFlagGemv && L->flags != kFlagTcPair) {
-        set_error("flags %d is not a kernel choice (0 size default, 2 tcgen05, 3 GEMV, 4 tcgen05 CTA pairs)", L->flags);
+    if (L->flags != 0 && L->flags != kFlagTc && L->flags != kFlagGemv) {
+        set_error("flags %d is not a kernel choice (0 size default, 2 tcgen05, 3 GEMV)", L->flags);
         return FM_EINVAL_SHAPE;
     }
     if (L->e_begin < 0 || L->e_local < 0 || L->e_begin + L->e_local > E) {
@@ -296,8 +288,7 @@ enum class Path { Tc, Gemv };
 static Path pick_path(const fm_layer* L, int T) {
     const bool gemv_ok = T <= gemv_max_t(L) && L->e_local < 1024 && T * L->top_k <= 1024;
     switch (L->flags) {
-        case kFlagTc:
-        case kFlagTcPair: return Path::Tc;
+        case kFlagTc: return Path::Tc;
         default: break;
     }
     return gemv_ok ? Path::Gemv : Path::Tc;
@@ -375,15 +366,15 @@ static int run_block_gemv(const fm_layer* L, const uint16_t* xb, const float* re
 // point): gate_up over x rows [0, t_real) straight from xb, h into h_rows, down adding
 // sgate * y into out. Leaves `spare_sms` SMs to the work that runs beside it. Records side->join.
 static int launch_shared_side(const fm_layer* L, const uint16_t* xb, const float* sgate, int T, int t_real, float* out,
-                              int* gu_list, int* dn_list, uint16_t* h_rows, int h_ld, int bdiv, int spare_sms, int* err,
+                              int* gu_list, int* dn_list, uint16_t* h_rows, int h_ld, int spare_sms, int* err,
                               SideStream* side, cudaStream_t st) {
     const int H = L->hidden, El = L->e_local;
     std::lock_guard<std::mutex> lock(side->enqueue);
     cudaStream_t s2 = side->s;
     if (cudaEventRecord(side->fork, st) != cudaSuccess || cudaStreamWaitEvent(s2, side->fork, 0) != cudaSuccess)
         return cuda_status(cudaGetLastError(), "fork the shared expert");
-    int rc = launch_seg_lists(nullptr, 0, El, 0, t_real, gu_list, L->ffn / 64 / bdiv, L->shared_ffn / 64 / bdiv, dn_list,
-                              H / kTileRows / bdiv, kBNTc, s2);
+    int rc = launch_seg_lists(nullptr, 0, El, 0, t_real, gu_list, L->ffn / 64, L->shared_ffn / 64, dn_list,
+                              H / kTileRows, kBNTc, s2);
     if (rc) return rc;
     const int rt = (T + kBNTc - 1) / kBNTc;
     TcLaunch g{};
@@ -403,7 +394,6 @@ static int launch_shared_side(const fm_layer* L, const uint16_t* xb, const float
     g.h_out = h_rows;
     g.h_ld = h_ld;
     g.err = err;
-    g.cta_pair = bdiv == 2;
     if ((rc = launch_expert_tc(true, g, s2))) return rc;
     TcLaunch d{};
     d.max_items = rt * (H / kTileRows);
@@ -425,7 +415,6 @@ static int launch_shared_side(const fm_layer* L, const uint16_t* xb, const float
     d.shared_base = 0;
     d.sgate = sgate;
     d.err = err;
-    d.cta_pair = bdiv == 2;
     if ((rc = launch_expert_tc(false, d, s2))) return rc;
     if (cudaEventRecord(side->join, s2) != cudaSuccess) return cuda_status(cudaGetLastError(), "join event");
     return FM_OK;
@@ -437,7 +426,6 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     const bool shared_on = L->shared_ffn > 0 && sgate && L->shared_gate_up && L->shared_down && t_real > 0;
     if (pick_path(L, T) == Path::Gemv) return run_block_gemv(L, xb, res, idx, w, sgate, T, t_real, out, ws, lo, st);
     const int P = t_real * k;
-    const int bdiv = tc_pair(L) ? 2 : 1;   // list entries are band pairs for the CTA-pair kernel
     // (the caller cleared the status words before this call's first kernel: clear_status)
     const int nblk = (P + kChunk - 1) / kChunk;
     // rows of the sorted space: routed [0, P), shared [P_cap, P_cap + t_real) with P_cap = T * k
@@ -454,12 +442,12 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
         return cuda_status(cudaGetLastError(), "out = res");
     if (side && (rc = launch_shared_side(L, xb, sgate, T, t_real, out, at<int>(ws, lo.gu_list_sh),
                                          at<int>(ws, lo.dn_list_sh), at<uint16_t>(ws, lo.hperm) + (size_t)Pcap * lo.fmax,
-                                         lo.fmax, bdiv, 0, at<int>(ws, lo.err) + 1, side, st)))
+                                         lo.fmax, 0, at<int>(ws, lo.err) + 1, side, st)))
         return rc;
     prof_begin(kStageDispatch, st);
     rc = launch_dispatch(idx, P, L->e_begin, L->e_local, E, Pcap, 0, at<int>(ws, lo.blk_hist), nblk,
                          at<int>(ws, lo.counts), at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
-                         at<int>(ws, lo.gu_list), L->ffn / 64 / bdiv, 0, at<int>(ws, lo.dn_list), H / kTileRows / bdiv,
+                         at<int>(ws, lo.gu_list), L->ffn / 64, 0, at<int>(ws, lo.dn_list), H / kTileRows,
                          kBNTc, at<int>(ws, lo.err), st);
     if (rc) return rc;
     prof_end(kStageDispatch, st);
@@ -485,7 +473,6 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     g.h_out = at<uint16_t>(ws, lo.hperm);
     g.h_ld = lo.fmax;
     g.err = at<int>(ws, lo.err) + 1;
-    g.cta_pair = bdiv == 2;
     prof_begin(kStageGateUp, st);
     if ((rc = launch_expert_tc(true, g, st))) return rc;
     prof_end(kStageGateUp, st);
@@ -510,7 +497,6 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     d.shared_base = Pcap;
     d.sgate = sgate;
     d.err = at<int>(ws, lo.err) + 1;
-    d.cta_pair = bdiv == 2;
     prof_begin(kStageDown, st);
     if ((rc = launch_expert_tc(false, d, st))) return rc;
     prof_end(kStageDown, st);
@@ -917,10 +903,9 @@ extern "C" FM_API int fm_ep_experts(const fm_layer* L, const uint16_t* xrecv, in
     if (rc) return rc;
     prof_end(kStageGather, st);
     prof_begin(kStageDispatch, st);
-    const int bdiv = tc_pair(L) ? 2 : 1;
     rc = launch_seg_lists(at<int>(workspace, lo.seg), El, El, R, srows, at<int>(workspace, lo.gu_list),
-                          L->ffn / 64 / bdiv, L->shared_ffn / 64 / bdiv, at<int>(workspace, lo.dn_list),
-                          H / kTileRows / bdiv, kBNTc, st);
+                          L->ffn / 64, L->shared_ffn / 64, at<int>(workspace, lo.dn_list),
+                          H / kTileRows, kBNTc, st);
     if (rc) return rc;
     prof_end(kStageDispatch, st);
     TcLaunch g{};
@@ -939,7 +924,6 @@ extern "C" FM_API int fm_ep_experts(const fm_layer* L, const uint16_t* xrecv, in
     g.h_out = at<uint16_t>(workspace, lo.hexp);
     g.h_ld = lo.fmax;
     g.err = at<int>(workspace, lo.err) + 1;
-    g.cta_pair = bdiv == 2;
     prof_begin(kStageGateUp, st);
     if ((rc = launch_expert_tc(true, g, st))) return rc;
     prof_end(kStageGateUp, st);
@@ -964,7 +948,6 @@ extern "C" FM_API int fm_ep_experts(const fm_layer* L, const uint16_t* xrecv, in
     d.sgate = shared_gate;
     d.y_rows = yrecv;
     d.err = at<int>(workspace, lo.err) + 1;
-    d.cta_pair = bdiv == 2;
     prof_begin(kStageDown, st);
     if ((rc = launch_expert_tc(false, d, st))) return rc;
     prof_end(kStageDown, st);
@@ -1164,7 +1147,6 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     // out = res before the fork: the shared expert adds into it on the side stream
     if (T > 0 && cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
         return cuda_status(cudaGetLastError(), "out = res");
-    const int bdiv = tc_pair(L) ? 2 : 1;
     // The shared expert needs no exchange: it runs on a side stream over this rank's own bf16 rows, on
     // all SMs but kScatterSms, while the rows travel; the combine waits for it (both add into out).
     SideStream* side = shared_on ? side_stream() : nullptr;
@@ -1175,13 +1157,13 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     if (shared_on && (rc = launch_shared_side(L, xb, sg, T, t_real, out, at<int>(workspace, lo.gu_list_sh),
                                               at<int>(workspace, lo.dn_list_sh),
                                               at<uint16_t>(workspace, lo.hexp) + (size_t)sl.r_cap * lo.fmax, lo.fmax,
-                                              bdiv, kScatterSms, a.err + 1, side, st)))
+                                              kScatterSms, a.err + 1, side, st)))
         return rc;
     if ((rc = launch_ep_post_counts(a, counts, st))) return rc;
     if ((rc = launch_ep_plan_peer(a, at<int>(workspace, lo.send_base), at<int>(workspace, lo.seg), st))) return rc;
     if ((rc = launch_seg_lists(at<int>(workspace, lo.seg), El, El, sl.r_cap, 0, at<int>(workspace, lo.gu_list),
-                               L->ffn / 64 / bdiv, L->shared_ffn / 64 / bdiv, at<int>(workspace, lo.dn_list),
-                               H / kTileRows / bdiv, kBNTc, st)))
+                               L->ffn / 64, L->shared_ffn / 64, at<int>(workspace, lo.dn_list),
+                               H / kTileRows, kBNTc, st)))
         return rc;
     prof_end(kStageDispatch, st);
     prof_begin(kStageGather, st);
@@ -1207,7 +1189,6 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     gu.h_out = at<uint16_t>(workspace, lo.hexp);
     gu.h_ld = lo.fmax;
     gu.err = a.err + 1;
-    gu.cta_pair = bdiv == 2;
     prof_begin(kStageGateUp, st);
     if ((rc = launch_expert_tc(true, gu, st))) return rc;
     prof_end(kStageGateUp, st);
@@ -1232,7 +1213,6 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     d.meta = reinterpret_cast<const int*>(mine + sl.meta);
     for (int i = 0; i < G; ++i) d.yret[i] = reinterpret_cast<uint16_t*>(a.sym[i] + sl.y);
     d.err = a.err + 1;
-    d.cta_pair = bdiv == 2;
     prof_begin(kStageDown, st);
     if ((rc = launch_expert_tc(false, d, st))) return rc;
     if ((rc = launch_ep_signal(a, 2, st))) return rc;

@@ -35,12 +35,16 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_hist_kernel(const int32
 }
 
 // Work list entry: (group, band, row0, nrows). list[0] = number of entries. Row tiles outer, bands
-// inner, so consecutive items share their activation rows in L2.
+// inner, so consecutive items share their activation rows in L2. A group's cnt rows make ceil(cnt / bn)
+// tiles of equal size (rounded up to 16 rows, the MMA's N step; the last takes the rest), so that no
+// tile is a sliver whose MMAs cost their issue time rather than their width.
 __device__ void emit_tiles(int* list, int first, int g, int bands, int row0, int cnt, int bn) {
+    const int nt = (cnt + bn - 1) / bn;
+    const int step = nt > 0 ? min(bn, ((cnt + nt - 1) / nt + 15) & ~15) : bn;
     int i = first;
-    for (int r = 0; r < cnt; r += bn)
+    for (int r = 0; r < cnt; r += step)
         for (int b = 0; b < bands; ++b, ++i) {
-            int4 t = make_int4(g, b, row0 + r, min(bn, cnt - r));
+            int4 t = make_int4(g, b, row0 + r, min(step, cnt - r));
             reinterpret_cast<int4*>(list + 4)[i] = t;
         }
 }

@@ -9,9 +9,9 @@
 //   warp 1      TMEM owner and MMA issuer: four tcgen05.mma (M=128, N=n rounded to 16, K=16) per
 //               slab into one of two TMEM accumulators (2 x 256 columns), commits release the rings;
 //   warps 2-9   dequantisers, two groups taking alternate slabs: thread r of a group turns row r of
-//               the raw tile (two GGUF blocks) into 64 bf16
-//               values in the 128-byte-swizzled K-major layout the MMA reads (w = q*d + m in f32 with
-//               the fp16 d, m widened exactly, rounded once to bf16);
+//               the raw tile (two GGUF blocks) into 64 bf16 values in the 128-byte-swizzled K-major
+//               layout the MMA reads (w = q*d + m in f32 with the fp16 d, m widened exactly, paired
+//               f32x2 FMAs, rounded once to bf16);
 //   warps 10-   epilogue (gate_up 4 warps; down 8 in two halves taking alternate 32-token chunks),
 //               overlapped with the next item's main loop through the second accumulator:
 //               GATE_UP  rows 0-63 of a gate_up tile are gate rows, rows 64-127 the up rows of the same
@@ -45,7 +45,7 @@ struct TcRoles {
     static constexpr int THREADS = 32 * (BWARP + 1);
 };
 constexpr int TC_BOX_BIG = 128;            // activation rows per large TMA box
-constexpr int TC_BN = 256;                 // max tokens per work item (MMA N)
+constexpr int TC_BN = kTcItemRows;         // max tokens per work item (MMA N)
 constexpr int TC_A_BYTES = 128 * 128;      // 128 rows x 64 bf16
 constexpr int TC_B_BYTES = TC_BN * 128;    // 256 rows x 64 bf16
 constexpr int TC_BOX_ROWS = 32;
@@ -58,15 +58,18 @@ constexpr int TC_EPI_BYTES = 2 * TC_HALF_BYTES + 2 * 256 * 4;   // two halves + 
 // Shared-memory layout. gate_up (K = 2048: 32 slabs per item, a light epilogue): 4 dequantised A stages,
 // 4 raw weight tiles, the gate/up exchange and h staging of one epilogue half (12 KB); down (K = 512, two
 // epilogue halves with 32 x 132 f32 staging each and the token / weight lists): 2 A stages, 6 raw tiles.
-// Both: 128 KB of activation stages (4 of 256 rows for one CTA per item, 8 of 128 rows for a CTA-pair
-// member). Two dequantiser groups take alternate slabs, so with 4 A stages each group has a second
-// stage to fill while the tensor core still reads its first.
-template <bool GATE_UP, bool PAIR>
+// Both: 4 activation stages of 256 rows (128 KB). Two dequantiser groups take alternate slabs, so with 4
+// A stages each group has a second stage to fill while the tensor core still reads its first.
+// Shared-memory bandwidth, not the tensor pipe, bounds the main loop: per 64-K slab of a 256-token item
+// the activation stage is written by TMA and read by the MMAs (32 KB each way), the A stage written by
+// the dequantisers and read by the MMAs (16 KB each way) and the raw tile written and read (5 KB each),
+// about 210 bytes per clock at the MMAs' full rate against the SM's 128.
+template <bool GATE_UP>
 struct TcSmem {
     static constexpr int SA = GATE_UP ? 4 : 2;
-    static constexpr int SB = PAIR ? 8 : 4;
+    static constexpr int SB = 4;
     static constexpr int SR = GATE_UP ? 4 : 6;    // raw weight tiles in flight (streamed from HBM)
-    static constexpr int B_STAGE = PAIR ? TC_B_BYTES / 2 : TC_B_BYTES;
+    static constexpr int B_STAGE = TC_B_BYTES;
     static constexpr int EPI = GATE_UP ? 3 * 16 * 64 * 4 : TC_EPI_BYTES;
     // offsets from the 1024-aligned dynamic smem base
     static constexpr int a = 0;
@@ -79,9 +82,7 @@ struct TcSmem {
     static constexpr int tmem = bars + nbars * 8;
     static constexpr int total = tmem + 16 + 1024;   // + alignment slack
 };
-static_assert(TcSmem<true, true>::total <= 232448 && TcSmem<true, false>::total <= 232448 &&
-                  TcSmem<false, true>::total <= 232448 && TcSmem<false, false>::total <= 232448,
-              "shared memory per CTA");
+static_assert(TcSmem<true>::total <= 232448 && TcSmem<false>::total <= 232448, "shared memory per CTA");
 
 struct TcArgs {
     const int* list;
@@ -123,35 +124,40 @@ __device__ __forceinline__ void fail(int* err, int code) { atomicCAS(err, 0, cod
 // follows.
 __device__ __forceinline__ float code_f(uint32_t t, uint32_t sel) { return __uint_as_float(__byte_perm(t, 0x3F000000u, sel)); }
 
-// Four codes (bytes of t) -> two bf16x2 words of q*d + m, with D = 256 d and C = m - 128 d.
-__device__ __forceinline__ uint2 deq4(uint32_t t, float D, float C) {
-    const float a = fmaf(code_f(t, 0x7044), D, C);
-    const float b = fmaf(code_f(t, 0x7144), D, C);
-    const float c = fmaf(code_f(t, 0x7244), D, C);
-    const float e = fmaf(code_f(t, 0x7344), D, C);
-    return make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, e));
+// (x, y) * (D, D) + (C, C) as one packed f32x2 FMA.
+__device__ __forceinline__ float2 fma2(float2 x, float2 D, float2 C) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(r)
+        : "l"(*reinterpret_cast<unsigned long long*>(&x)), "l"(*reinterpret_cast<unsigned long long*>(&D)),
+          "l"(*reinterpret_cast<unsigned long long*>(&C)));
+    return *reinterpret_cast<float2*>(&r);
 }
 
-// One GGUF block's 16 nibble bytes (4 words) -> 4 chunks of 8 bf16 (K = 0-7, 8-15, 16-23, 24-31).
-__device__ __forceinline__ void deq_block(uint4 n, float d, float m, uint4* ch) {
-    const float D = 256.0f * d, C = fmaf(-128.0f, d, m);
+// Four codes (bytes 0-3 of t) -> two bf16x2 words of q*d + m: (byte 0, byte 1) and (byte 2, byte 3).
+__device__ __forceinline__ uint2 deq4(uint32_t t, float2 D, float2 C) {
+    const float2 a = fma2(make_float2(code_f(t, 0x7044), code_f(t, 0x7144)), D, C);
+    const float2 b = fma2(make_float2(code_f(t, 0x7244), code_f(t, 0x7344)), D, C);
+    return make_uint2(pack_bf16x2(a.x, a.y), pack_bf16x2(b.x, b.y));
+}
+
+// One GGUF block in the tile's word order (word c = bytes b(2c), b(2c+1), b(2c+8), b(2c+9); byte j holds
+// value j in its low nibble, value j + 16 in its high one) -> its 16 bf16x2 words in K order (word j =
+// values 2j, 2j+1) at out[0..15].
+__device__ __forceinline__ void deq_block(uint4 n, float d, float m, uint32_t* out) {
+    const float2 D = make_float2(256.0f * d, 256.0f * d);
+    const float cm = fmaf(-128.0f, d, m);
+    const float2 C = make_float2(cm, cm);
     const uint32_t w[4] = {n.x, n.y, n.z, n.w};
-    uint2 lo[4], hi[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        lo[i] = deq4(w[i] & 0x0F0F0F0Fu, D, C);
-        hi[i] = deq4((w[i] >> 4) & 0x0F0F0F0Fu, D, C);
+    for (int c = 0; c < 4; ++c) {
+        const uint2 lo = deq4(w[c] & 0x0F0F0F0Fu, D, C);          // values 2c, 2c+1 | 2c+8, 2c+9
+        const uint2 hi = deq4((w[c] >> 4) & 0x0F0F0F0Fu, D, C);   // values 2c+16, 2c+17 | 2c+24, 2c+25
+        out[c] = lo.x;
+        out[c + 4] = lo.y;
+        out[c + 8] = hi.x;
+        out[c + 12] = hi.y;
     }
-    ch[0] = make_uint4(lo[0].x, lo[0].y, lo[1].x, lo[1].y);   // values 0-7: low nibbles of bytes 0-7
-    ch[1] = make_uint4(lo[2].x, lo[2].y, lo[3].x, lo[3].y);   // values 8-15
-    ch[2] = make_uint4(hi[0].x, hi[0].y, hi[1].x, hi[1].y);   // values 16-23: high nibbles of bytes 0-7
-    ch[3] = make_uint4(hi[2].x, hi[2].y, hi[3].x, hi[3].y);   // values 24-31
-}
-
-// A tile block's 4 words in fragment order (see repack.cu) -> GGUF byte order b0..b15.
-__device__ __forceinline__ uint4 gguf_order(uint4 t) {
-    return make_uint4(__byte_perm(t.x, t.y, 0x5410), __byte_perm(t.z, t.w, 0x5410), __byte_perm(t.x, t.y, 0x7632),
-                      __byte_perm(t.z, t.w, 0x7632));
 }
 
 struct Item {
@@ -159,13 +165,11 @@ struct Item {
     const uint8_t* w;
 };
 
-// PAIR: list entries name band pairs; CTA `crank` of the pair takes band 2 * entry + crank.
-template <bool PAIR>
-__device__ __forceinline__ Item decode_item(const TcArgs& a, int i, uint32_t crank) {
+__device__ __forceinline__ Item decode_item(const TcArgs& a, int i) {
     const int4 it = reinterpret_cast<const int4*>(a.list + 4)[i];
     Item r;
     r.g = it.x;
-    r.band = PAIR ? 2 * it.y + (int)crank : it.y;
+    r.band = it.y;
     r.row0 = it.z;
     r.n = it.w;
     const bool sh = r.g == a.shared_group;
@@ -176,19 +180,11 @@ __device__ __forceinline__ Item decode_item(const TcArgs& a, int i, uint32_t cra
     return r;
 }
 
-// PAIR: a cluster of two CTAs on two SMs works each item as one M = 256 MMA (tcgen05 cta_group::2):
-// CTA r dequantises band 2p + r into its own A ring and loads rows [r N/2, (r + 1) N/2) of the
-// item's tokens into its own B ring, so each SM streams half the activation bytes per MMA. The first
-// CTA's barriers gate the MMAs: its A-full barrier counts one arrival per dequantiser warp of both
-// CTAs, its B-full barrier the bytes of both CTAs' activation loads (the second CTA's loads complete
-// on it directly), its accumulator-empty barrier one arrival per epilogue warp of both CTAs; the
-// first CTA issues the MMAs and commits the stage / accumulator releases to both CTAs' barriers. No
-// load is shared between the CTAs and no multicast copy is used.
-template <bool GATE_UP, bool PAIR>
+template <bool GATE_UP>
 __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel(const __grid_constant__ CUtensorMap bmap,
                                                                   const __grid_constant__ CUtensorMap bmap_big, TcArgs a) {
     using R = TcRoles<GATE_UP>;
-    using Sm = TcSmem<GATE_UP, PAIR>;
+    using Sm = TcSmem<GATE_UP>;
     constexpr int SA = Sm::SA, SB = Sm::SB, SR = Sm::SR, B_STAGE = Sm::B_STAGE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -207,35 +203,27 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_items = a.list[0];
-    const uint32_t crank = PAIR ? cluster_ctarank() : 0;
-    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;   // item stride: one per CTA or pair
-    const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int unit = (int)blockIdx.x, n_units = (int)gridDim.x;
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
         // a dequantiser group (4 warps, 128 threads) consumes a raw tile and fills an A stage
         for (int i = 0; i < SR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 128); }
         for (int i = 0; i < SB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
-        // arrivals are per warp: 4 dequantiser / 4 or 8 epilogue warps per CTA, both CTAs' on the first CTA's
-        for (int i = 0; i < SA; ++i) { mbar_init(&a_full[i], (PAIR ? 2 : 1) * 4); mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], (PAIR ? 2 : 1) * R::EPI); }
+        // arrivals are per warp: 4 dequantiser / 4 or 8 epilogue warps
+        for (int i = 0; i < SA; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], R::EPI); }
         mbar_init(drain, 1);
         mbar_fence_init();
         prefetch_tmap(&bmap);
         prefetch_tmap(&bmap_big);
     }
     if (warp == 1) {
-        if (PAIR) {
-            tmem_alloc_pair(tmem_slot, 512);
-            tmem_relinquish_pair();
-        } else {
-            tmem_alloc(tmem_slot, 512);
-            tmem_relinquish();
-        }
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
     }
     tc_fence_before();
-    if (PAIR) cluster_sync();   // barriers initialised in both CTAs before any cross-CTA arrival
-    else __syncthreads();
+    __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -252,10 +240,9 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
             uint32_t ph = 0, issued = 0;   // bit i: slot i has a fill in flight or landed
             bool ok = true;
             for (int i = unit; i < n_items && ok; i += n_units) {
-                const Item it = decode_item<PAIR>(a, i, crank);
-                // this CTA's token rows: all n (single), or its half of N = n rounded up to 16 (pair)
-                const int nhalf = PAIR ? ((it.n + 15) & ~15) / 2 : it.n;
-                const int rbase = it.row0 + (int)crank * nhalf;
+                const Item it = decode_item(a, i);
+                const int nhalf = it.n;
+                const int rbase = it.row0;
                 // whole 128-row boxes, then 32-row boxes for the rest
                 const int nbig = nhalf / TC_BOX_BIG;
                 const int nsmall = (nhalf - nbig * TC_BOX_BIG + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
@@ -267,20 +254,15 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                         bulk_load(smem + Sm::raw + st * kTileBytes, it.w + (size_t)s * kTileBytes, kTileBytes, &raw_full[st]);
                         issued |= 1u << st;
                     } else {
-                        // the first CTA arms its B-full barrier for both halves; the second CTA's loads
-                        // complete their bytes on that barrier
-                        if (crank == 0) mbar_expect_tx(&b_full[st], (PAIR ? 2 : 1) * rows_loaded * 128);
+                        mbar_expect_tx(&b_full[st], rows_loaded * 128);
                         for (int j = 0; j < nbig + nsmall; ++j) {
                             const bool big = j < nbig;
                             const int r0 = big ? j * TC_BOX_BIG : nbig * TC_BOX_BIG + (j - nbig) * TC_BOX_ROWS;
                             const CUtensorMap* map = big ? &bmap_big : &bmap;
                             uint8_t* dst = smem + Sm::b + st * B_STAGE + r0 * 128;
-                            if (PAIR)
-                                tma_load_2d_pair(dst, map, s * kTileK, rbase + r0, mapa_shared(&b_full[st], 0));
-                            else
-                                tma_load_2d(dst, map, s * kTileK, rbase + r0, &b_full[st]);
+                            tma_load_2d(dst, map, s * kTileK, rbase + r0, &b_full[st]);
                         }
-                        if (crank == 0) issued |= 1u << st;
+                        issued |= 1u << st;
                     }
                     if (++st == S) { st = 0; ph ^= 1; }
                 }
@@ -297,68 +279,46 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
             }
         }
     } else if (warp == 1) {
-        if (!PAIR || crank == 0) {
-            // -------------------------------------------------------- MMA issuer (first CTA of a pair)
-            if (lane == 0) {
-                int as = 0, bs = 0;
-                uint32_t aph = 0, bph = 0;
-                bool ok = true, issued = false;
-                int local = 0;
-                const uint32_t peer = 1;
-                for (int i = unit; i < n_items && ok; i += n_units, ++local) {
-                    const Item it = decode_item<PAIR>(a, i, crank);
-                    const int acc = local & 1;
-                    const uint32_t accph = (local >> 1) & 1;
-                    if (!mbar_wait_cluster(&acc_empty[acc], accph ^ 1)) { ok = false; break; }
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int as = 0, bs = 0;
+            uint32_t aph = 0, bph = 0;
+            bool ok = true, issued = false;
+            int local = 0;
+            for (int i = unit; i < n_items && ok; i += n_units, ++local) {
+                const Item it = decode_item(a, i);
+                const int acc = local & 1;
+                const uint32_t accph = (local >> 1) & 1;
+                if (!mbar_wait(&acc_empty[acc], accph ^ 1)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * 256;
+                const uint32_t idesc = idesc_bf16(128, (it.n + 15) & ~15);
+                for (int s = 0; s < it.slabs; ++s) {
+                    if (!mbar_wait(&a_full[as], aph) || !mbar_wait(&b_full[bs], bph)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + acc * 256;
-                    const int N = (it.n + 15) & ~15;
-                    const uint32_t idesc = idesc_bf16(PAIR ? 256 : 128, N);
-                    for (int s = 0; s < it.slabs; ++s) {
-                        if (!mbar_wait_cluster(&a_full[as], aph) || !mbar_wait(&b_full[bs], bph)) { ok = false; break; }
-                        tc_fence_after();
-                        const uint32_t sa = smem_u32(smem + Sm::a + as * TC_A_BYTES);
-                        const uint32_t sb = smem_u32(smem + Sm::b + bs * B_STAGE);
+                    const uint32_t sa = smem_u32(smem + Sm::a + as * TC_A_BYTES);
+                    const uint32_t sb = smem_u32(smem + Sm::b + bs * B_STAGE);
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk) {
-                            if (PAIR)
-                                tc_mma_f16_pair(d_tmem, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc,
-                                                (s > 0 || kk > 0) ? 1u : 0u);
-                            else
-                                tc_mma_f16(d_tmem, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc,
-                                           (s > 0 || kk > 0) ? 1u : 0u);
-                        }
-                        issued = true;
-                        if (PAIR) {   // both CTAs' stages are free once these MMAs completed
-                            tc_commit_pair(mapa_shared(&a_empty[as], 0));
-                            tc_commit_pair(mapa_shared(&a_empty[as], peer));
-                            tc_commit_pair(mapa_shared(&b_empty[bs], 0));
-                            tc_commit_pair(mapa_shared(&b_empty[bs], peer));
-                        } else {
-                            tc_commit(&a_empty[as]);
-                            tc_commit(&b_empty[bs]);
-                        }
-                        if (++as == SA) { as = 0; aph ^= 1; }
-                        if (++bs == SB) { bs = 0; bph ^= 1; }
-                    }
-                    if (!ok) break;
-                    if (PAIR) {
-                        tc_commit_pair(mapa_shared(&acc_full[acc], 0));
-                        tc_commit_pair(mapa_shared(&acc_full[acc], peer));
-                    } else {
-                        tc_commit(&acc_full[acc]);
-                    }
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma_f16(d_tmem, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc,
+                                   (s > 0 || kk > 0) ? 1u : 0u);
+                    issued = true;
+                    tc_commit(&a_empty[as]);
+                    tc_commit(&b_empty[bs]);
+                    if (++as == SA) { as = 0; aph ^= 1; }
+                    if (++bs == SB) { bs = 0; bph ^= 1; }
                 }
-                if (!ok) {
-                    fail(a.err, FM_ETIMEOUT);
-                    atomicExch(&abort_flag, 1);
-                }
-                // every MMA of this CTA (and its commits' arrivals) done before the pair may exit
-                if (issued) {
-                    if (PAIR) tc_commit_pair(mapa_shared(drain, 0));
-                    else tc_commit(drain);
-                    mbar_wait(drain, 0);
-                }
+                if (!ok) break;
+                tc_commit(&acc_full[acc]);
+            }
+            if (!ok) {
+                fail(a.err, FM_ETIMEOUT);
+                atomicExch(&abort_flag, 1);
+            }
+            // every MMA of this CTA (and its commits' arrivals) done before the CTA may exit
+            if (issued) {
+                tc_commit(drain);
+                mbar_wait(drain, 0);
             }
         }
     } else if (warp < R::EPI0) {
@@ -373,23 +333,23 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
         bool ok = true;
         int sc = 0;   // running slab index over this CTA's items
         for (int i = unit; i < n_items && ok; i += n_units) {
-            const Item it = decode_item<PAIR>(a, i, crank);
+            const Item it = decode_item(a, i);
             for (int s = 0; s < it.slabs; ++s, ++sc) {
                 if (sc % NG != grp) continue;
                 const int rs = sc % SR, as = sc % SA;
                 const uint32_t rph = (sc / SR) & 1, aph = (sc / SA) & 1;
                 if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[rs], rph))) { ok = false; break; }
                 const uint32_t raw = smem_u32(smem + Sm::raw + rs * kTileBytes);
-                const uint4 n0 = gguf_order(lds128(raw + r * 32));
-                const uint4 n1 = gguf_order(lds128(raw + r * 32 + 16));
+                const uint4 n0 = lds128(raw + r * 32);
+                const uint4 n1 = lds128(raw + r * 32 + 16);
                 const uint2 sc2 = lds64(raw + kTileNibBytes + r * 8);
                 const float d0 = __half2float(__ushort_as_half((unsigned short)(sc2.x & 0xFFFF)));
                 const float m0 = __half2float(__ushort_as_half((unsigned short)(sc2.x >> 16)));
                 const float d1 = __half2float(__ushort_as_half((unsigned short)(sc2.y & 0xFFFF)));
                 const float m1 = __half2float(__ushort_as_half((unsigned short)(sc2.y >> 16)));
-                uint4 ch[8];
-                deq_block(n0, d0, m0, ch);
-                deq_block(n1, d1, m1, ch + 4);
+                uint32_t wv[32];   // the row's 64 values in K order: 16-byte chunk c = words 4c..4c+3
+                deq_block(n0, d0, m0, wv);
+                deq_block(n1, d1, m1, wv + 16);
                 // The raw slot goes back to the weight producer, whose next bulk copy (async proxy)
                 // overwrites it, only after this thread's loads from it have delivered their values (the
                 // dequantised words depend on them) and a proxy fence: releasing it right after issuing
@@ -400,13 +360,11 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                 if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[as], aph ^ 1))) { ok = false; break; }
                 const uint32_t arow = smem_u32(smem + Sm::a + as * TC_A_BYTES + r * 128);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) sts128(arow + ((c ^ (r & 7)) << 4), ch[c]);
+                for (int c = 0; c < 8; ++c)
+                    sts128(arow + ((c ^ (r & 7)) << 4), make_uint4(wv[4 * c], wv[4 * c + 1], wv[4 * c + 2], wv[4 * c + 3]));
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) {   // the warp's 32 rows are in place (on the first CTA's barrier)
-                    if (PAIR && crank == 1) mbar_arrive_cluster(mapa_shared(&a_full[as], 0));
-                    else mbar_arrive(&a_full[as]);
-                }
+                if (lane == 0) mbar_arrive(&a_full[as]);   // the warp's 32 rows are in place
             }
         }
         if (!ok) {
@@ -437,7 +395,7 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
         named_bar(3, 32 * R::EPI);
         int local = 0;
         for (int i = unit; i < n_items; i += n_units, ++local) {
-            const Item it = decode_item<PAIR>(a, i, crank);
+            const Item it = decode_item(a, i);
             const int acc = local & 1;
             const uint32_t accph = (local >> 1) & 1;
             // DOWN: where the item's rows go -- 0 weighted red.add into out, 1 a bf16 row of y_rows,
@@ -562,10 +520,7 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {   // the warp's TMEM reads are done (on the first CTA's barrier)
-                if (PAIR && crank == 1) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
-                else mbar_arrive(&acc_empty[acc]);
-            }
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);   // the warp's TMEM reads are done
         }
         if (epi_abort) {
             fail(a.err, FM_ETIMEOUT);
@@ -574,12 +529,10 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
         if (!GATE_UP && a.meta) __threadfence_system();   // the peer stores land before the rank signals
     }
     tc_fence_before();
-    if (PAIR) cluster_sync();   // neither CTA leaves while the other may still signal its barriers
-    else __syncthreads();
+    __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        if (PAIR) tmem_dealloc_pair(tmem_base, 512);
-        else tmem_dealloc(tmem_base, 512);
+        tmem_dealloc(tmem_base, 512);
     }
 }
 
@@ -621,23 +574,13 @@ int make_bmap(CUtensorMap* m, const uint16_t* base, int rows, int cols, int ld, 
     return FM_OK;
 }
 
-template <bool GATE_UP, bool PAIR>
+template <bool GATE_UP>
 static cudaError_t launch_tc_variant(const CUtensorMap& bmap, const CUtensorMap& bmap_big, const TcArgs& a, int grid,
-                                     int sm, cudaStream_t st) {
-    if (cudaError_t e = raise_smem_limit((const void*)expert_tc_kernel<GATE_UP, PAIR>, sm)) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(TcRoles<GATE_UP>::THREADS);
-    cfg.dynamicSmemBytes = sm;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = PAIR ? 2 : 1;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, expert_tc_kernel<GATE_UP, PAIR>, bmap, bmap_big, a);
+                                     cudaStream_t st) {
+    const int sm = TcSmem<GATE_UP>::total;
+    if (cudaError_t e = raise_smem_limit((const void*)expert_tc_kernel<GATE_UP>, sm)) return e;
+    expert_tc_kernel<GATE_UP><<<grid, TcRoles<GATE_UP>::THREADS, sm, st>>>(bmap, bmap_big, a);
+    return cudaGetLastError();
 }
 
 int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
@@ -669,19 +612,9 @@ int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
     a.err = L.err;
     int sms = device_sm_count();
     if (L.max_ctas > 0 && L.max_ctas < sms) sms = L.max_ctas;
-    const int sm_single = gate_up ? TcSmem<true, false>::total : TcSmem<false, false>::total;
-    const int sm_pair = gate_up ? TcSmem<true, true>::total : TcSmem<false, true>::total;
-    cudaError_t e;
-    if (L.cta_pair) {
-        // one pair per two SMs; items are band pairs
-        const int pairs = L.max_items < sms / 2 ? L.max_items : sms / 2;
-        e = gate_up ? launch_tc_variant<true, true>(bmap, bmap_big, a, 2 * pairs, sm_pair, st)
-                    : launch_tc_variant<false, true>(bmap, bmap_big, a, 2 * pairs, sm_pair, st);
-    } else {
-        const int grid = L.max_items < sms ? L.max_items : sms;
-        e = gate_up ? launch_tc_variant<true, false>(bmap, bmap_big, a, grid, sm_single, st)
-                    : launch_tc_variant<false, false>(bmap, bmap_big, a, grid, sm_single, st);
-    }
+    const int grid = L.max_items < sms ? L.max_items : sms;
+    const cudaError_t e = gate_up ? launch_tc_variant<true>(bmap, bmap_big, a, grid, st)
+                                  : launch_tc_variant<false>(bmap, bmap_big, a, grid, st);
     if (e != cudaSuccess) {
         note_launch();
         return cuda_status(e, gate_up ? "expert_tc<gate_up>" : "expert_tc<down>");

@@ -32,6 +32,8 @@ int launch_dispatch(const int32_t* idx, int P, int e_begin, int e_local, int E, 
                     int* dn_list, int dn_bands, int bn, int* err, cudaStream_t st);
 int launch_gather(const uint16_t* xb, const int* pair, const int* counts, const int* offsets, int e_local, int shared_base,
                   int k, int H, int max_rows, uint16_t* xperm, cudaStream_t st);
+// Most rows (tokens) of one tcgen05 work item: the MMA's N, one of the kernel's two TMEM accumulators.
+constexpr int kTcItemRows = 256;
 struct TcLaunch {
     int max_items;
     const int* list;
@@ -56,7 +58,6 @@ struct TcLaunch {
     const int* meta;                 // peer expert-parallel DOWN (see expert_tc.cu)
     uint16_t* yret[kMaxRanks];
     int* err;
-    bool cta_pair;                   // CTA-pair kernel (M = 256 MMAs); the list entries are band pairs
     int max_ctas;                    // grid cap (0: one CTA per SM); leaves SMs to concurrent work
 };
 int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st);

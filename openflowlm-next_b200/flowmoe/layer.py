@@ -243,13 +243,13 @@ class MoELayer:
                           router.data_ptr(), _ptr(self.router_bias))
         self._ws: torch.Tensor | None = None
 
-    PATHS = {"auto": 0, "tc": 2, "gemv": 3, "tc2": 4}
+    PATHS = {"auto": 0, "tc": 2, "gemv": 3}
 
     @property
     def path(self) -> str:
         """Kernel choice: "auto" (the GEMV up to 128 tokens while tokens x top_k <= 1024, else the tcgen05
-        grouped GEMM), or forced "tc" (tcgen05, one CTA per item), "tc2" (tcgen05 as CTA pairs where the
-        band counts allow), "gemv" (the GEMV, within the same limits; tcgen05 past them)."""
+        grouped GEMM), or forced "tc" (tcgen05) or "gemv" (the GEMV, within the same limits; tcgen05 past
+        them)."""
         return {v: k for k, v in self.PATHS.items()}[self._L.flags]
 
     @path.setter
