@@ -49,6 +49,15 @@ extern "C" {
 #define FM_ETIMEOUT 5      /* a bounded device wait gave up */
 #define FM_EWORKSPACE 6    /* the caller's workspace is smaller than fm_workspace_size() */
 
+/* fm_layer.flags bit: every token's expert terms are added in ascending expert order (the scatter order
+ * of the reference's Core::moe_block, src/open_qwen36/core.cpp:5163-5165, :5236-5255), so a call's output is
+ * bit-reproducible and independent of the other tokens in the call -- a prompt run layer by layer over
+ * all its tokens gives the same bits as block by block (on one kernel path: the GEMV and the tcgen05 GEMM
+ * sum a row's products in different orders). On the tcgen05 path this routes the down GEMM's y rows
+ * through f32 scratch (about T * (top_k + 1) * H * 4 bytes of workspace) and a combine kernel instead of
+ * atomic adds; on the GEMV path it turns off the K splits, whose count follows the call's size. */
+#define FM_FIXED_ORDER 0x100
+
 /* Activation dtypes accepted for xm. */
 #define FM_F32 0
 #define FM_BF16 1
@@ -67,7 +76,7 @@ typedef struct fm_layer {
     int32_t flags;      /* 0 = pick kernels by size (the GEMV up to 128 tokens while T * top_k <= 1024 and
                            e_local < 1024, else the tcgen05 grouped GEMM);
                            2 = force tcgen05, 3 = force the GEMV (within the same limits, tcgen05 past
-                           them); any other value is rejected (FM_EINVAL_SHAPE) */
+                           them); plus FM_FIXED_ORDER; any other value is rejected (FM_EINVAL_SHAPE) */
     const uint8_t* gate_up;   /* tiles, e_local x (2 x F x H x 5/8 B): gate then up, per expert */
     const uint8_t* down;      /* tiles, e_local x (H x F x 5/8 B) */
     const uint8_t* shared_gate_up; /* tiles of the shared expert, or NULL */

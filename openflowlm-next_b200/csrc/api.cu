@@ -105,6 +105,10 @@ int cuda_status(cudaError_t e, const char* what) {
 constexpr int kBN = 64;        // rows per work item the list sizes assume (>= the real items' rows)
 constexpr int kBNTc = kTcItemRows;   // rows per expert work item (expert_tc)
 constexpr int kFlagTc = 2, kFlagGemv = 3;   // 1 and 4 were retired kernel variants
+constexpr int kFlagPath = 0xFF;                // the kernel choice bits of fm_layer.flags
+// FM_FIXED_ORDER (include/flowmoe.h): every token's expert terms added in ascending expert order, so a
+// call's output is bit-reproducible and does not depend on the other tokens in the call
+static bool fixed_order(const fm_layer* L) { return (L->flags & FM_FIXED_ORDER) != 0; }
 
 // The GEMV path up to this many tokens, auto or forced (flags = 3), while T * top_k <= 1024 (the
 // single-CTA dispatch). Measured on B200 from 48 to 128 tokens (C30 and C36 layers): 2.2-2.5x faster
@@ -112,7 +116,7 @@ constexpr int kFlagTc = 2, kFlagGemv = 3;   // 1 and 4 were retired kernel varia
 constexpr int kDecodeMaxT = 128;
 constexpr int kGemvMaxT = 128;
 
-static int gemv_max_t(const fm_layer* L) { return L->flags == kFlagGemv ? kGemvMaxT : kDecodeMaxT; }
+static int gemv_max_t(const fm_layer* L) { return (L->flags & kFlagPath) == kFlagGemv ? kGemvMaxT : kDecodeMaxT; }
 constexpr int kGemvRowsApi = 8;    // sorted rows per GEMV item (decode.cu)
 constexpr int kChunk = 2048;   // dispatch chunk (dispatch.cu)
 
@@ -179,8 +183,10 @@ static int validate(const fm_layer* L, int T) {
         set_error("router_block: topk %d past the expert count %d (or > %d)", k, E, kMaxTopK);
         return FM_EINVAL_SHAPE;
     }
-    if (L->flags != 0 && L->flags != kFlagTc && L->flags != kFlagGemv) {
-        set_error("flags %d is not a kernel choice (0 size default, 2 tcgen05, 3 GEMV)", L->flags);
+    const int path = L->flags & kFlagPath;
+    if ((L->flags & ~(kFlagPath | FM_FIXED_ORDER)) || (path != 0 && path != kFlagTc && path != kFlagGemv)) {
+        set_error("flags 0x%x: the kernel choice is 0 (size default), 2 (tcgen05) or 3 (GEMV), plus FM_FIXED_ORDER",
+                  L->flags);
         return FM_EINVAL_SHAPE;
     }
     if (L->e_begin < 0 || L->e_local < 0 || L->e_begin + L->e_local > E) {
@@ -217,7 +223,7 @@ static Layout make_layout(const fm_layer* L, int T) {
     auto take = [&](size_t bytes) { size_t at = off; off = align256(off + bytes); return at; };
     o.err = take(16);   // first: fm_moe_check reads the counter at the workspace start
     o.xb = take((size_t)T * H * 2);
-    o.logits = take(router_scratch_bytes(T, H, E));
+    o.logits = take(router_scratch_bytes(T, H, E, fixed_order(L)));
     o.counts = take((size_t)G * 4);
     o.offsets = take((size_t)(G + 1) * 4);
     o.blk_hist = take((size_t)o.nblk * L->e_local * 4);
@@ -227,7 +233,8 @@ static Layout make_layout(const fm_layer* L, int T) {
     o.dn_list = take((size_t)(4 + 4 * o.max_dn) * 4);
     o.xperm = take((size_t)o.rows * H * 2);
     o.hperm = take((size_t)o.rows * o.fmax * 2);
-    o.yperm = take(decode ? (size_t)o.rows * H * 4 : 0);   // f32 y rows: the GEMV path only
+    // f32 y rows: the GEMV path, and the tcgen05 path's fixed-order combine
+    o.yperm = take(decode || fixed_order(L) ? (size_t)o.rows * H * 4 : 0);
     o.sgate = take((size_t)T * 4);
     o.idx = take((size_t)o.P * 4);
     o.w = take((size_t)o.P * 4);
@@ -287,7 +294,7 @@ enum class Path { Tc, Gemv };
 // limits).
 static Path pick_path(const fm_layer* L, int T) {
     const bool gemv_ok = T <= gemv_max_t(L) && L->e_local < 1024 && T * L->top_k <= 1024;
-    switch (L->flags) {
+    switch (L->flags & kFlagPath) {
         case kFlagTc: return Path::Tc;
         default: break;
     }
@@ -300,13 +307,16 @@ static int run_block_gemv(const fm_layer* L, const uint16_t* xb, const float* re
     const int H = L->hidden, k = L->top_k;
     const bool shared_on = L->shared_ffn > 0 && sgate && L->shared_gate_up && L->shared_down && t_real > 0;
     const int P = t_real * k, Pcap = lo.P;
-    prof_begin(kStageDispatch, st);   // the dispatch kernel clears the status words
+    // the dispatch kernel clears the status words, except in the fixed-order mode, where the caller did
+    // before the router (whose tcgen05 kernel may report a timeout)
+    prof_begin(kStageDispatch, st);
     int rc = launch_dispatch_small(idx, P, L->e_begin, L->e_local, Pcap, shared_on ? t_real : 0, at<int>(ws, lo.counts),
                                    at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
                                    at<int>(ws, lo.gu_list), L->ffn / 64, shared_on ? L->shared_ffn / 64 : 0,
                                    H / kTileK, at<int>(ws, lo.dn_list), H / kTileRows, L->ffn / kTileK,
                                    shared_on ? L->shared_ffn / kTileK : L->ffn / kTileK, lo.kc_cap,
-                                   at<int>(ws, lo.done), at<int>(ws, lo.err), st);
+                                   fixed_order(L) ? 0 : 1, fixed_order(L) ? 0 : 1, at<int>(ws, lo.done),
+                                   at<int>(ws, lo.err), st);
     if (rc) return rc;
     prof_end(kStageDispatch, st);
     GemvLaunch g{};
@@ -336,6 +346,7 @@ static int run_block_gemv(const fm_layer* L, const uint16_t* xb, const float* re
     g.y_rows = lo.rows;
     g.H = H;
     g.err = at<int>(ws, lo.err) + 1;
+    g.tc_min = fixed_order(L) ? 8 : 1;
     prof_begin(kStageGateUp, st);
     if ((rc = launch_gemv(true, g, st))) return rc;
     prof_end(kStageGateUp, st);
@@ -431,24 +442,29 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     // rows of the sorted space: routed [0, P), shared [P_cap, P_cap + t_real) with P_cap = T * k
     const int Pcap = lo.P;
     // the shared expert reads x directly and runs on a side stream while the routed rows are dispatched
-    // and gathered (those kernels leave most SMs idle); out = res must precede it
-    SideStream* side = shared_on ? side_stream() : nullptr;
-    if (shared_on && !side) {
+    // and gathered (those kernels leave most SMs idle); out = res must precede it. In the fixed-order mode
+    // the down GEMM writes every y row (shared rows too, as one more group) and the combine kernel sums
+    // each token's terms in ascending expert order, writing all of out.
+    const bool fixed = fixed_order(L);
+    const bool shared_in_lists = shared_on && fixed;
+    SideStream* side = (shared_on && !fixed) ? side_stream() : nullptr;
+    if (shared_on && !fixed && !side) {
         set_error("could not create the side stream");
         return FM_ECUDA;
     }
     int rc = FM_OK;
-    if (cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    if (!fixed && cudaMemcpyAsync(out, res, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
         return cuda_status(cudaGetLastError(), "out = res");
     if (side && (rc = launch_shared_side(L, xb, sgate, T, t_real, out, at<int>(ws, lo.gu_list_sh),
                                          at<int>(ws, lo.dn_list_sh), at<uint16_t>(ws, lo.hperm) + (size_t)Pcap * lo.fmax,
                                          lo.fmax, 0, at<int>(ws, lo.err) + 1, side, st)))
         return rc;
     prof_begin(kStageDispatch, st);
-    rc = launch_dispatch(idx, P, L->e_begin, L->e_local, E, Pcap, 0, at<int>(ws, lo.blk_hist), nblk,
-                         at<int>(ws, lo.counts), at<int>(ws, lo.offsets), at<int>(ws, lo.pos), at<int>(ws, lo.pair),
-                         at<int>(ws, lo.gu_list), L->ffn / 64, 0, at<int>(ws, lo.dn_list), H / kTileRows,
-                         kBNTc, at<int>(ws, lo.err), st);
+    rc = launch_dispatch(idx, P, L->e_begin, L->e_local, E, Pcap, shared_in_lists ? t_real : 0, at<int>(ws, lo.blk_hist),
+                         nblk, at<int>(ws, lo.counts), at<int>(ws, lo.offsets), at<int>(ws, lo.pos),
+                         at<int>(ws, lo.pair), at<int>(ws, lo.gu_list), L->ffn / 64,
+                         shared_in_lists ? L->shared_ffn / 64 : 0, at<int>(ws, lo.dn_list), H / kTileRows, kBNTc,
+                         at<int>(ws, lo.err), st);
     if (rc) return rc;
     prof_end(kStageDispatch, st);
     prof_begin(kStageGather, st);
@@ -456,7 +472,8 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
                             k, H, lo.rows, at<uint16_t>(ws, lo.xperm), st)))
         return rc;
     prof_end(kStageGather, st);
-    // out = res was set above (rows past t_real stay res); the down GEMM adds w * y into it
+    // out = res was set above (rows past t_real stay res); the down GEMM adds w * y into it (or, in the
+    // fixed-order mode, writes the y rows the combine then sums)
     TcLaunch g{};
     g.max_items = lo.max_gu;
     g.list = at<int>(ws, lo.gu_list);
@@ -497,11 +514,19 @@ static int run_block(const fm_layer* L, const uint16_t* xb, const float* res, co
     d.shared_base = Pcap;
     d.sgate = sgate;
     d.err = at<int>(ws, lo.err) + 1;
+    d.y_f32 = fixed ? at<float>(ws, lo.yperm) : nullptr;
     prof_begin(kStageDown, st);
     if ((rc = launch_expert_tc(false, d, st))) return rc;
     prof_end(kStageDown, st);
     if (side && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
         return cuda_status(cudaGetLastError(), "join the shared expert");
+    if (fixed) {
+        prof_begin(kStageCombine, st);
+        rc = launch_combine(res, at<float>(ws, lo.yperm), at<int>(ws, lo.pos), idx, w, sgate, shared_on ? 1 : 0, T,
+                            t_real, k, H, Pcap, out, st);
+        prof_end(kStageCombine, st);
+        if (rc) return rc;
+    }
     return FM_OK;
 }
 
@@ -541,7 +566,7 @@ extern "C" FM_API int fm_router_topk(const fm_layer* L, const void* xm, int32_t 
     if (int rc = clear_status(workspace, lo, st)) return rc;
     const uint16_t* xb = nullptr;
     if (int rc = xm_to_bf16(L, xm, xm_dtype, T, workspace, lo, &xb, st)) return rc;
-    return launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k, at<float>(workspace, lo.logits), probs,
+    return launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k, fixed_order(L), at<float>(workspace, lo.logits), probs,
                          idx, w, shared_gate, at<int>(workspace, lo.err), st);
 }
 
@@ -559,7 +584,7 @@ extern "C" FM_API int fm_moe_block(const fm_layer* L, const void* xm, int32_t xm
     if (int rc = check_ws(lo, workspace, workspace_bytes)) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     const uint16_t* xb = nullptr;
-    if (pick_path(L, T) == Path::Tc)
+    if (pick_path(L, T) == Path::Tc || fixed_order(L))   // else the GEMV path's dispatch kernel clears them
         if (int rc = clear_status(workspace, lo, st)) return rc;
     if (int rc = xm_to_bf16(L, xm, xm_dtype, T, workspace, lo, &xb, st)) return rc;
     return run_block(L, xb, res, idx, w, shared_gate, T, t_real, out, workspace, lo, st);
@@ -573,10 +598,10 @@ static int moe_layer_xb(const fm_layer* L, const uint16_t* xb, const float* res,
     int32_t* ids = idx ? idx : at<int32_t>(workspace, lo.idx);
     float* ws_w = w ? w : at<float>(workspace, lo.w);
     float* sg = at<float>(workspace, lo.sgate);
-    if (pick_path(L, T) == Path::Tc)
+    if (pick_path(L, T) == Path::Tc || fixed_order(L))   // else the GEMV path's dispatch kernel clears them
         if (int rc = clear_status(workspace, lo, st)) return rc;
     prof_begin(kStageRouter, st);
-    if (int rc = launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k,
+    if (int rc = launch_router(xb, L->router, L->router_bias, T, L->hidden, L->n_experts, L->top_k, fixed_order(L),
                                at<float>(workspace, lo.logits), nullptr, ids, ws_w, sg, at<int>(workspace, lo.err), st))
         return rc;
     prof_end(kStageRouter, st);
@@ -747,7 +772,7 @@ static EpDispatchLayout ep_dispatch_layout(const fm_layer* L, int T) {
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t a = off; off = align256(off + bytes); return a; };
     o.err = take(16);
-    o.logits = take(router_scratch_bytes(T, H, E));
+    o.logits = take(router_scratch_bytes(T, H, E, fixed_order(L)));
     o.counts = take((size_t)(E + 1) * 4);
     o.offsets = take((size_t)(E + 2) * 4);
     o.blk_hist = take((size_t)o.nblk * E * 4);
@@ -853,7 +878,7 @@ extern "C" FM_API int fm_ep_dispatch(const fm_layer* L, const void* xm, int32_t 
     if (cudaMemsetAsync(at<int>(workspace, lo.err), 0, 16, st) != cudaSuccess)
         return cuda_status(cudaGetLastError(), "memset");
     prof_begin(kStageRouter, st);
-    if (int rc = launch_router(xb, L->router, L->router_bias, T, H, E, k, at<float>(workspace, lo.logits), nullptr, idx, w,
+    if (int rc = launch_router(xb, L->router, L->router_bias, T, H, E, k, fixed_order(L), at<float>(workspace, lo.logits), nullptr, idx, w,
                                shared_gate, at<int>(workspace, lo.err), st))
         return rc;
     prof_end(kStageRouter, st);
@@ -1014,7 +1039,7 @@ static EpPeerLayout ep_peer_layout(const fm_layer* L, const fm_ep_group* g, int 
     auto take = [&](size_t bytes) { size_t a = off; off = align256(off + bytes); return a; };
     o.err = take(16);
     o.xb = take((size_t)T * H * 2);
-    o.logits = take(router_scratch_bytes(T, H, E));
+    o.logits = take(router_scratch_bytes(T, H, E, fixed_order(L)));
     o.counts = take((size_t)(E + 1) * 4);
     o.offsets = take((size_t)(E + 2) * 4);
     o.blk_hist = take((size_t)nblk * E * 4);
@@ -1133,7 +1158,7 @@ extern "C" FM_API int fm_ep_peer_layer(const fm_layer* L, const fm_ep_group* g, 
     const int P = t_real * k;
     int rc = FM_OK;
     prof_begin(kStageRouter, st);
-    if (T > 0 && (rc = launch_router(xb, L->router, L->router_bias, T, H, E, k, at<float>(workspace, lo.logits), nullptr,
+    if (T > 0 && (rc = launch_router(xb, L->router, L->router_bias, T, H, E, k, fixed_order(L), at<float>(workspace, lo.logits), nullptr,
                                      ids, wts, sg, a.err, st)))
         return rc;
     prof_end(kStageRouter, st);

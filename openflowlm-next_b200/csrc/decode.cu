@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
     const int32_t* __restrict__ idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
     int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ pos, int* __restrict__ pair,
     int* __restrict__ gu_list, int gu_bands, int gu_bands_shared, int gu_slabs, int* __restrict__ dn_list, int dn_bands,
-    int dn_slabs, int dn_slabs_shared, int kc_cap, int target, int* __restrict__ done, int* __restrict__ err) {
+    int dn_slabs, int dn_slabs_shared, int kc_cap, int split, int target, int clear, int* __restrict__ done, int* __restrict__ err) {
     extern __shared__ int sm[];
     int* cnt = sm;                                  // [e_local]
     int* wcnt = cnt + e_local;                      // [32][e_local]
@@ -92,7 +92,8 @@ __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
     int* gu0 = off_s + e_local + 1;                 // [e_local + 2] first GEMV slot of each group (gate/up)
     int* dn0 = gu0 + e_local + 2;                   // [e_local + 2] (down)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x < 4) err[threadIdx.x] = 0;   // this call's status words (bad ids, GEMV timeouts)
+    // this call's status words (bad ids, GEMV timeouts), unless the caller cleared them before its router
+    if (clear && threadIdx.x < 4) err[threadIdx.x] = 0;
     __syncthreads();
     for (int e = threadIdx.x; e < e_local; e += blockDim.x) {
         cnt[e] = 0;
@@ -181,8 +182,11 @@ __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
     int2 tot;
     const int2 slot = block_exclusive_scan2_1024(make_int2(bgu, bdn), scan_sh, &tot);
     const int tot_gu = tot.x, tot_dn = tot.y, slot_gu = slot.x, slot_dn = slot.y;
-    const int kc_gu = choose_chunks(tot_gu, gu_slabs, 0, kc_cap, target);
-    const int kc_dn = choose_chunks(tot_dn, dn_slabs, shared_rows > 0 ? dn_slabs_shared : 0, kc_cap, target);
+    // K chunks: their count follows the call's item count (so a token's sums would depend on the other
+    // tokens of the call) and the down GEMM adds its chunks into y with red.add (an unfixed order): both
+    // off in the fixed-order mode
+    const int kc_gu = split ? choose_chunks(tot_gu, gu_slabs, 0, kc_cap, target) : 1;
+    const int kc_dn = split ? choose_chunks(tot_dn, dn_slabs, shared_rows > 0 ? dn_slabs_shared : 0, kc_cap, target) : 1;
     if (gi <= G) {
         gu0[gi] = gi < G ? slot_gu : tot_gu;
         dn0[gi] = gi < G ? slot_dn : tot_dn;
@@ -243,6 +247,7 @@ struct GemvArgs {
     const int* dn_list;       // GATE_UP: the down list, whose K-chunk count says whether y starts at zero
     int y_rows;               // rows of y_out
     int* err;                 // FM_ETIMEOUT when a bounded wait gives up
+    int tc_min;               // least token columns per item (8: one scale group per block at every n)
 };
 
 // CTA = one producer warp + GV_WARPS consumer warps working on one item at a time; GV_CTAS_PER_SM such
@@ -518,7 +523,10 @@ __global__ void __launch_bounds__(GV_THREADS, GV_CTAS_PER_SM) gemv_kernel(GemvAr
             const GvItem it = gv_decode(a, e0, KC);
             e0 = e1;
             float acc[2][4] = {};
-            const int tc = it.n <= 1 ? 1 : it.n <= 2 ? 2 : it.n <= 4 ? 4 : 8;
+            // token columns: fewer tokens leave room for several blocks per MMA column group (gv_item),
+            // which changes the order of a token's sums with the item's token count; tc_min = 8 keeps
+            // one order for every count (the fixed-order mode)
+            const int tc = max(a.tc_min, it.n <= 1 ? 1 : it.n <= 2 ? 2 : it.n <= 4 ? 4 : 8);
             switch (tc) {
                 case 1: ok = gv_item<1>(smem, full, empty, st, ph, it.slabs, j, lane, acc); break;
                 case 2: ok = gv_item<2>(smem, full, empty, st, ph, it.slabs, j, lane, acc); break;
@@ -619,8 +627,8 @@ int gemv_chunk_cap(int T) {
 
 int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
                           int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
-                          int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int kc_cap,
-                          int* done, int* err, cudaStream_t st) {
+                          int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int kc_cap, int split,
+                          int clear, int* done, int* err, cudaStream_t st) {
     const size_t sm = (size_t)(e_local * 33 + 64 + 3 * (e_local + 2)) * 4;
     // the limit for the largest group count (e_local < 1024) at once, so no later call (one being
     // captured into a graph, say) has to raise it again
@@ -629,8 +637,8 @@ int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, i
     const int target = GV_CTAS_PER_SM * device_sm_count();   // one item per CTA slot
     dispatch_small_kernel<<<1, kDispSmallThreads, sm, st>>>(idx, P, e_begin, e_local, shared_base, shared_rows, counts,
                                                            offsets, pos, pair, gu_list, gu_bands, gu_bands_shared,
-                                                           gu_slabs, dn_list, dn_bands, dn_slabs, dn_slabs_shared, kc_cap,
-                                                           target, done, err);
+                                                           gu_slabs, dn_list, dn_bands, dn_slabs, dn_slabs_shared, kc_cap, split,
+                                                           target, clear, done, err);
     FM_LAUNCH_CHECK("dispatch_small");
     return FM_OK;
 }
@@ -663,6 +671,7 @@ int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st) {
     a.dn_list = L.dn_list;
     a.y_rows = L.y_rows;
     a.err = L.err;
+    a.tc_min = L.tc_min;
     const int slots = GV_CTAS_PER_SM * device_sm_count();
     const int grid = L.max_items < slots ? L.max_items : slots;
     const void* fn = gate_up ? (const void*)gemv_kernel<true> : (const void*)gemv_kernel<false>;

@@ -20,7 +20,8 @@
 //               DOWN     out[token][row] += w * y (the weighted scatter of core.cpp:5236-5255, routing
 //                        weight or shared-expert gate per row): the weighted 32-token chunk is staged
 //                        in shared memory, then each warp adds 8 token rows with red.global.add.v4.f32;
-//                        or unweighted bf16 y rows (expert parallel: in the received order, or straight
+//                        or unweighted f32 y rows for a fixed-order combine after the kernel; or
+//                        unweighted bf16 y rows (expert parallel: in the received order, or straight
 //                        into the sending rank's buffer over peer memory).
 // Every mbarrier wait is bounded (sm100.cuh); a give-up records FM_ETIMEOUT in the error word and
 // the CTA drains its own copies, frees TMEM and returns.
@@ -107,6 +108,9 @@ struct TcArgs {
     // expert order), with ymap they are added into out (expert parallel: out holds this rank's tokens)
     uint16_t* y_rows;
     const int* ymap;
+    // DOWN, f32 row mode (the fixed-order combine): every row's y, unweighted f32, goes to y_f32[r] (routed
+    // and shared rows alike); a combine kernel then sums each token in ascending expert order
+    float* y_f32;
     // DOWN, peer expert-parallel mode: routed row r's y, unweighted bf16, goes straight to the rank that
     // sent the row: yret[meta[r] >> 24] + (meta[r] & 0xFFFFFF) rows, a store over NVLink; skipped once
     // the status word *err is set (a failed exchange: the peers may be gone)
@@ -401,7 +405,8 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
             // DOWN: where the item's rows go -- 0 weighted red.add into out, 1 a bf16 row of y_rows,
             // 2 a bf16 row in the sending rank's buffer (peer store)
             const bool shared_item = it.g == a.shared_group;
-            const int mode = shared_item ? ((a.y_rows && !a.ymap && !a.meta) ? 1 : 0) : (a.meta ? 2 : (a.y_rows ? 1 : 0));
+            const int mode = a.y_f32 ? 3
+                             : shared_item ? ((a.y_rows && !a.ymap && !a.meta) ? 1 : 0) : (a.meta ? 2 : (a.y_rows ? 1 : 0));
             // DOWN: thread et looks up the destination and weight of row et while the accumulator
             // fills; it goes to shared memory after the barrier below, when every thread is done with
             // the previous item's lists
@@ -409,8 +414,8 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
             float wk = 0.f;
             if (!GATE_UP && et < it.n) {
                 const int rrow = it.row0 + et;
-                if (mode == 1) {
-                    tk = (a.ymap && !shared_item) ? a.ymap[rrow] : rrow;
+                if (mode == 1 || mode == 3) {
+                    tk = (mode == 1 && a.ymap && !shared_item) ? a.ymap[rrow] : rrow;
                     wk = 1.0f;
                 } else if (shared_item) {
                     tk = rrow - a.shared_base;
@@ -436,8 +441,8 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                     const int rrow = it.row0 + rr;
                     int t2;
                     float w2;
-                    if (mode == 1) {
-                        t2 = (a.ymap && !shared_item) ? a.ymap[rrow] : rrow;
+                    if (mode == 1 || mode == 3) {
+                        t2 = (mode == 1 && a.ymap && !shared_item) ? a.ymap[rrow] : rrow;
                         w2 = 1.0f;
                     } else if (shared_item) {
                         t2 = rrow - a.shared_base;
@@ -503,6 +508,8 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                             const float4 y = *reinterpret_cast<const float4*>(ys + j * TC_EPI_LD + lane * 4);
                             if (mode == 0) {
                                 red_add_v4(a.out + (size_t)tok[c0 + j] * a.H + it.band * 128 + lane * 4, y);
+                            } else if (mode == 3) {
+                                *reinterpret_cast<float4*>(a.y_f32 + (size_t)tok[c0 + j] * a.H + it.band * 128 + lane * 4) = y;
                             } else if (mode == 2) {
                                 const int m = tok[c0 + j];
                                 if (m >= 0)
@@ -607,6 +614,7 @@ int launch_expert_tc(bool gate_up, const TcLaunch& L, cudaStream_t st) {
     a.sgate = L.sgate;
     a.y_rows = L.y_rows;
     a.ymap = L.ymap;
+    a.y_f32 = L.y_f32;
     a.meta = L.meta;
     for (int i = 0; i < kMaxRanks; ++i) a.yret[i] = L.yret[i];
     a.err = L.err;

@@ -11,21 +11,18 @@ int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st);
 int launch_rmsnorm_bf16(const float* x, const uint16_t* w, float eps, int T, int H, uint16_t* xb, cudaStream_t st);
 // The router of T tokens (idx, w, sgate, optional probs): the logits into `logits`, from kRouterTcMinT
 // tokens (E <= 496) by the tcgen05 kernel of router_tc.cu (row stride router_tc_ld(E); bounded waits
-// report FM_ETIMEOUT in err[1]), below by the split-K logits kernel; then a top-k kernel.
+// report FM_ETIMEOUT in err[1]), below by the split-K logits kernel; then a top-k kernel. `fixed` (the
+// fixed-order mode) takes one form at every T, so that a token's logits do not depend on the call's other
+// tokens: the tcgen05 kernel where E <= 496, else one K chunk.
 constexpr int kRouterTcMinT = 256;
-bool router_tc_ok(int T, int E, int k);
+bool router_tc_ok(int T, int E, int k, bool fixed);
 int router_tc_ld(int E);
-int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
+int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k, bool fixed,
                   float* logits, float* probs, int32_t* idx, float* w, float* sgate, int* err, cudaStream_t st);
 int launch_router_tc_logits(const uint16_t* xb, const uint16_t* router, int T, int H, int E, float* logits, int* err,
                             cudaStream_t st);
 // The per-device side stream of the tcgen05 path (shared expert), created now if it does not exist yet.
 int prepare_side_stream();
-bool router_tc_ok(int T, int E, int k);
-int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
-                  float* logits, float* probs, int32_t* idx, float* w, float* sgate, int* err, cudaStream_t st);
-int launch_router_tc(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
-                     float* probs, int32_t* idx, float* w, float* sgate, int* err, cudaStream_t st);
 int launch_dispatch(const int32_t* idx, int P, int e_begin, int e_local, int E, int shared_base, int shared_rows,
                     int* blk_hist, int nblk,
                     int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
@@ -55,6 +52,7 @@ struct TcLaunch {
     const float* sgate;
     uint16_t* y_rows;                // DOWN row mode (see expert_tc.cu)
     const int* ymap;
+    float* y_f32;                    // DOWN f32 row mode (fixed-order combine)
     const int* meta;                 // peer expert-parallel DOWN (see expert_tc.cu)
     uint16_t* yret[kMaxRanks];
     int* err;
@@ -87,13 +85,14 @@ struct GemvLaunch {
     const int* dn_list;   // GATE_UP: the down list (its K-chunk count)
     int y_rows;           // rows of y_out (cleared by GATE_UP when the down GEMM splits K)
     int* err;
+    int tc_min;           // least token columns of an item's MMA (8 in the fixed-order mode)
 };
-int router_ksplit(int T, int H, int E);
-size_t router_scratch_bytes(int T, int H, int E);   // the logits scratch of launch_router
+int router_ksplit(int T, int H, int E, bool fixed);
+size_t router_scratch_bytes(int T, int H, int E, bool fixed);   // the logits scratch of launch_router
 int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, int shared_base, int shared_rows,
                           int* counts, int* offsets, int* pos, int* pair, int* gu_list, int gu_bands, int gu_bands_shared,
-                          int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int kc_cap,
-                          int* done, int* err, cudaStream_t st);
+                          int gu_slabs, int* dn_list, int dn_bands, int dn_slabs, int dn_slabs_shared, int kc_cap, int split,
+                          int clear, int* done, int* err, cudaStream_t st);
 int gemv_chunk_cap(int T);    // most K chunks per GEMV item at T tokens (sizes the partial-sum buffer)
 constexpr int kGemvWarps = 4; // consumer warps of a GEMV CTA (one completion counter per item slot each)
 int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st);

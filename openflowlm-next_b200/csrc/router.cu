@@ -309,23 +309,23 @@ int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st) {
 
 // K chunks of the router GEMM: enough CTAs to cover the SMs when few tokens give few tiles. The logits
 // rows hold E + 1 values (the last is the shared-gate logit).
-size_t router_scratch_bytes(int T, int H, int E) {
-    if (router_tc_ok(T, E, 1)) return (size_t)T * router_tc_ld(E) * 4;
-    return (size_t)router_ksplit(T, H, E) * T * (E + 1) * 4;
+size_t router_scratch_bytes(int T, int H, int E, bool fixed) {
+    if (router_tc_ok(T, E, 1, fixed)) return (size_t)T * router_tc_ld(E) * 4;
+    return (size_t)router_ksplit(T, H, E, fixed) * T * (E + 1) * 4;
 }
 
-int router_ksplit(int T, int H, int E) {
-    if (T >= kRouterTcMinT) return 1;
+int router_ksplit(int T, int H, int E, bool fixed) {
+    if (fixed || T >= kRouterTcMinT) return 1;
     const int tiles = ((E + 1 + RG_BN - 1) / RG_BN) * ((T + RG_BM - 1) / RG_BM);
     int ks = 1;
     while (ks < kMaxKSplit && tiles * ks < 148 && H % (2 * ks * RG_BK) == 0) ks *= 2;
     return ks;
 }
 
-int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k,
+int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias, int T, int H, int E, int k, bool fixed,
                   float* logits, float* probs, int32_t* idx, float* w, float* sgate, int* err, cudaStream_t st) {
-    const bool tc = router_tc_ok(T, E, k);
-    const int ks = tc ? 1 : router_ksplit(T, H, E);
+    const bool tc = router_tc_ok(T, E, k, fixed);
+    const int ks = tc ? 1 : router_ksplit(T, H, E, fixed);
     const int ld = tc ? router_tc_ld(E) : E + 1;
     if (tc) {
         if (int rc = launch_router_tc_logits(xb, router, T, H, E, logits, err, st)) return rc;

@@ -158,7 +158,9 @@ __global__ void __launch_bounds__(RT_THREADS, 1) router_tc_kernel(const __grid_c
     }
 }
 
-bool router_tc_ok(int T, int E, int k) { return T >= kRouterTcMinT && E <= 496 && k <= kMaxTopK; }
+bool router_tc_ok(int T, int E, int k, bool fixed) {
+    return (fixed || T >= kRouterTcMinT) && E <= 496 && k <= kMaxTopK;
+}
 
 int router_tc_ld(int E) { return (E + 1 + 3) & ~3; }
 

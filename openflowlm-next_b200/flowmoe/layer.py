@@ -244,17 +244,30 @@ class MoELayer:
         self._ws: torch.Tensor | None = None
 
     PATHS = {"auto": 0, "tc": 2, "gemv": 3}
+    FIXED_ORDER = 0x100   # FM_FIXED_ORDER (include/flowmoe.h)
 
     @property
     def path(self) -> str:
         """Kernel choice: "auto" (the GEMV up to 128 tokens while tokens x top_k <= 1024, else the tcgen05
         grouped GEMM), or forced "tc" (tcgen05) or "gemv" (the GEMV, within the same limits; tcgen05 past
         them)."""
-        return {v: k for k, v in self.PATHS.items()}[self._L.flags]
+        return {v: k for k, v in self.PATHS.items()}[self._L.flags & 0xFF]
 
     @path.setter
     def path(self, name: str) -> None:
-        self._L.flags = self.PATHS[name]
+        self._L.flags = (self._L.flags & ~0xFF) | self.PATHS[name]
+
+    @property
+    def fixed_order(self) -> bool:
+        """Every token's expert terms added in ascending expert order (the reference's scatter order,
+        core.cpp:5163-5165): outputs bit-reproducible and independent of the other tokens of a call, so a
+        prompt run layer-major (each layer over all its tokens) matches block-major bit for bit. Costs the
+        tcgen05 path f32 y-row scratch and a combine kernel, the GEMV path its K splits."""
+        return bool(self._L.flags & self.FIXED_ORDER)
+
+    @fixed_order.setter
+    def fixed_order(self, on: bool) -> None:
+        self._L.flags = (self._L.flags | self.FIXED_ORDER) if on else (self._L.flags & ~self.FIXED_ORDER)
 
     # ---- construction from the reference's block layout
     @classmethod

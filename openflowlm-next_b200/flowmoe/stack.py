@@ -28,25 +28,32 @@ class MoEStack:
         self._graph = None
         self._bufs = None
 
-    def _run(self, x: torch.Tensor, bufs, layer_hook=None) -> torch.Tensor:
+    def _run(self, x: torch.Tensor, bufs, layer_hook=None, t_real=None) -> torch.Tensor:
         cur = x
         for i, (layer, nw) in enumerate(zip(self.layers, self.norm_ws)):
             nxt = bufs[i & 1]
-            layer.forward_norm(cur, nw, self.eps, out=nxt)
+            layer.forward_norm(cur, nw, self.eps, out=nxt, t_real=t_real)
             if layer_hook is not None:
                 layer_hook(i)
             cur = nxt
         return cur
 
-    def forward(self, x: torch.Tensor, layer_hook=None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, layer_hook=None, t_real: int | None = None) -> torch.Tensor:
         """x f32 [T, H] -> the stack's output (a new tensor unless a captured graph is replayed).
-        ``layer_hook(i)`` (eager passes only) is called after layer i is enqueued."""
-        if self._graph is not None and x.shape == self._x.shape and layer_hook is None:
+        ``layer_hook(i)`` (eager passes only) is called after layer i is enqueued; rows past ``t_real`` are
+        padding (carried through every layer as they are).
+
+        Given a whole prompt, this is the reference's layer-major prefill schedule for the MoE half of
+        each layer (Core::step_gemm_prompt, src/open_qwen36/core.cpp:3734-3846): every token through layer
+        l's MoE in one call, then layer l + 1, so each layer's experts stream from HBM once per prompt;
+        with the layers' ``fixed_order`` set, the result is bit for bit that of running the prompt in
+        blocks."""
+        if self._graph is not None and x.shape == self._x.shape and layer_hook is None and t_real is None:
             self._x.copy_(x)
             self._graph.replay()
             return self._y
         bufs = [torch.empty_like(x), torch.empty_like(x)]
-        return self._run(x, bufs, layer_hook)
+        return self._run(x, bufs, layer_hook, t_real)
 
     __call__ = forward
 

@@ -18,6 +18,9 @@ Fixtures:
   moe.npz     ``replica.moe_decode`` (fp64, HF-faithful) over 4 tokens of a small Qwen3.6-shaped
               block (H=2048 as replica.py fixes it, E=16, F=128, shared F=128, top-8) whose Q4_1
               experts come from the reference's block generator (seed 0).
+  q4nx.npz    the SHA-256 of what the reference's .q4nx reader (open_kernels/model/q4nx.py) dequantises
+              from a one-layer container the oracle writes (2 experts, shared expert with a signed-
+              quantiser matrix, router).
   expert_pool.npz  the SHA-256 of the MoE expert pool regions (gate_up stripes and down slices) the
               engine's pack ops write for 2 seeded experts (F=512, H=256), built from the reference's
               own pack_q4_1_pool, stripe_transpose and down_perm, and of their source blocks.
@@ -156,7 +159,48 @@ def main() -> int:
                         blocks_sha=sha(np.concatenate([b.reshape(-1) for b in pu + pg + pd])),
                         gate_up_sha=sha(gu_pool), down_sha=sha(dn_pool),
                         gate_up_bytes=gu_pool.size, down_bytes=dn_pool.size)
-    for f in ("q4_1.npz", "router.npz", "moe.npz", "expert_pool.npz"):
+    # ---- a one-layer .q4nx container (2 routed experts of F 512 at H 2048, shared expert, router, gate,
+    # post-attention norm) written by the oracle's writer and read back by the reference's own reader
+    # (open_kernels/model/q4nx.py, Q4NX): the SHA-256 of every matrix that reader dequantises. The shared
+    # expert's up matrix is stored by the signed quantiser (mins written as zero), which the reader
+    # transcodes (recipes/pack.py is_signed_q4 / q4_0_to_q4_1).
+    import tempfile
+    import q4nx as RQ                             # open_kernels/model/q4nx.py
+    sys.path.insert(0, str(HERE.parents[1]))
+    from oracle import q4nx as OQX
+    rng = np.random.default_rng(11)
+    Ex, Fx, Hx = 2, 512, 2048
+    ex = {k: [QP.random_q4_1_blocks(Fx if k != "down" else Hx, Hx if k != "down" else Fx, rng) for _ in range(Ex)]
+          for k in ("gate", "up", "down")}
+    sh = {k: QP.random_q4_1_blocks(Fx if k != "down" else Hx, Hx if k != "down" else Fx, rng) for k in ("gate", "up", "down")}
+    d16 = np.ascontiguousarray(sh["up"][..., 0:2]).view(np.float16)
+    sh["up"][..., 2:4] = (d16.astype(bfloat16).astype(np.float32) * -8).astype(np.float16).view(np.uint8)
+    wr = bf16_vals(rng.normal(0, 0.02, (Hx, 8)).astype(np.float32)).astype(bfloat16).view(np.uint16)
+    sgw = bf16_vals(rng.normal(0, 0.02, Hx).astype(np.float32)).astype(bfloat16).view(np.uint16)
+    pln = bf16_vals(1 + rng.normal(0, 0.01, Hx).astype(np.float32)).astype(bfloat16).view(np.uint16)
+    L = "model.layer.0."
+    tens = {L + "post_attention_layernorm.weight": ("BF16", pln), L + "moe_router.weight": ("BF16", wr),
+            L + "shared_expert_gate.weight": ("BF16", sgw)}
+    for k in ("gate", "up", "down"):
+        tens[L + f"mlp.{k}_exps_proj.weight"] = ("I8", np.concatenate([OQX.q4nx_matrix(b) for b in ex[k]]))
+        tens[L + f"mlp.share_{k}_exps_proj.weight"] = ("I8", OQX.signed_q4_matrix(sh[k]) if k == "up"
+                                                       else OQX.q4nx_matrix(sh[k]))
+    shas = {}
+    with tempfile.TemporaryDirectory() as td:
+        path = Path(td) / "l0.q4nx"
+        OQX.write_q4nx(path, tens)
+        container_sha = hashlib.sha256(path.read_bytes()).hexdigest()
+        m = RQ.Q4NX(path)
+        for k in ("gate", "up", "down"):
+            for e in range(Ex):
+                shas[f"expert_{k}_{e}"] = sha(m.expert_w(0, k, e))
+            shas[f"shared_{k}"] = sha(m.shared_w(0, k))
+        shas["router"] = sha(m.bf16(L + "moe_router.weight"))
+        m.mm.close()
+        m.f.close()
+    np.savez_compressed(HERE / "q4nx.npz", seed=11, E=Ex, F=Fx, H=Hx, container_sha=container_sha,
+                        **{k: v for k, v in shas.items()})
+    for f in ("q4_1.npz", "router.npz", "moe.npz", "expert_pool.npz", "q4nx.npz"):
         print(f"wrote {HERE / f} ({(HERE / f).stat().st_size} B)")
     return 0
 

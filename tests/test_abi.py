@@ -38,7 +38,7 @@ def _layer(**kw):
     g = dict(hidden=2048, n_experts=128, top_k=8, ffn=768, shared_ffn=0, e_begin=0, e_local=128, flags=0)
     g.update(kw)
     return FmLayer(g["hidden"], g["n_experts"], g["top_k"], g["ffn"], g["shared_ffn"], g["e_begin"], g["e_local"],
-                   0, None, None, None, None, None)
+                   g["flags"], None, None, None, None, None)
 
 
 def test_workspace_size_grows_with_tokens():
@@ -58,6 +58,26 @@ def test_bad_geometry_is_rejected(kw, code):
     rc = _lib.lib.fm_workspace_size(ctypes.byref(_layer(**kw)), 16, ctypes.byref(n))
     assert rc == code
     assert _lib.last_error()
+
+
+@pytest.mark.parametrize("flags,ok", [(0, True), (2, True), (3, True), (0x100, True), (0x102, True), (0x103, True),
+                                      (1, False), (4, False), (0x101, False), (0x200, False), (0x302, False)])
+def test_flags_checked(flags, ok):
+    """fm_layer.flags: a kernel path (0 auto, 2 tcgen05, 3 GEMV) plus optionally FM_FIXED_ORDER (0x100)."""
+    from flowmoe import _lib
+    n = ctypes.c_size_t()
+    rc = _lib.lib.fm_workspace_size(ctypes.byref(_layer(flags=flags)), 16, ctypes.byref(n))
+    assert (rc == 0) == ok and (ok or rc == _lib.FM_EINVAL_SHAPE)
+
+
+def test_fixed_order_workspace_holds_f32_rows():
+    """The fixed-order mode's tcgen05 path keeps every y row in f32: T * (top_k + 1) * H * 4 bytes more."""
+    from flowmoe import _lib
+    a, b = ctypes.c_size_t(), ctypes.c_size_t()
+    T, L = 4096, dict(shared_ffn=512)
+    _lib.call("fm_workspace_size", ctypes.byref(_layer(**L)), T, ctypes.byref(a))
+    _lib.call("fm_workspace_size", ctypes.byref(_layer(flags=0x100, **L)), T, ctypes.byref(b))
+    assert b.value - a.value >= T * 9 * 2048 * 4
 
 
 def test_topk_past_experts_raises_like_reference():

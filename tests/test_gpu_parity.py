@@ -398,3 +398,66 @@ def test_expert_pool_import_bit_exact(dev, golden):
     a = flowmoe.MoELayer.from_expert_pool(cfg, gu, dn, Wr, device=dev)
     b = flowmoe.MoELayer.from_q4_1(cfg, gb, ub, db, Wr, device=dev)
     assert torch.equal(a.gate_up, b.gate_up) and torch.equal(a.down, b.down)
+
+
+def _fixed_run(layer, x, res, t_real=None):
+    probs, idx, w = layer.router_block(x)
+    sg = layer.shared_gate_buf if layer.cfg.shared_ffn else None
+    return layer.moe_block(x, res, idx, w, t_real=t_real, shared_gate=sg).cpu().numpy(), idx.cpu().numpy(), \
+        w.cpu().numpy()
+
+
+@pytest.mark.parametrize("path", ["tc", "gemv"])
+def test_fixed_order_matches_oracle(dev, path):
+    """FM_FIXED_ORDER on both kernel paths: shared expert, padding rows, against the fp64 oracle."""
+    c = cases.make_case(H=2048, E=16, F=512, FS=512, k=8, T=40, seed=11)
+    layer = _layer(c, dev, path)
+    layer.fixed_order = True
+    assert layer.path == path and layer.fixed_order
+    x = torch.from_numpy(c["x"]).to(dev).to(torch.bfloat16)
+    res = torch.from_numpy(c["res"]).to(dev)
+    out, idx, w = _fixed_run(layer, x, res, t_real=37)
+    ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], t_real=37, shared=c["shared"])
+    assert _rel(out, ref, c["res"]) < TOL
+    np.testing.assert_array_equal(out[37:], c["res"][37:])
+    again, _, _ = _fixed_run(layer, x, res, t_real=37)
+    np.testing.assert_array_equal(again, out)
+
+
+@pytest.mark.parametrize("path,T,blocks", [("tc", 600, [128, 200, 16, 256]), ("gemv", 40, [1] * 40),
+                                           ("gemv", 96, [32, 7, 57])])
+def test_fixed_order_layer_major_equals_block_major(dev, path, T, blocks):
+    """A prompt through the layer in one call (layer-major prefill) gives the same bits as the same
+    prompt in blocks, and as one token at a time on the GEMV path, once the order is fixed."""
+    c = cases.make_case(H=1024, E=32, F=256, FS=256, k=8, T=T, seed=12)
+    layer = _layer(c, dev, path)
+    layer.fixed_order = True
+    x = torch.from_numpy(c["x"]).to(dev).to(torch.bfloat16)
+    res = torch.from_numpy(c["res"]).to(dev)
+    whole, idx, w = _fixed_run(layer, x, res)
+    parts, b0 = [], 0
+    for n in blocks:
+        parts.append(_fixed_run(layer, x[b0:b0 + n].contiguous(), res[b0:b0 + n].contiguous())[0])
+        b0 += n
+    assert b0 == T
+    np.testing.assert_array_equal(np.concatenate(parts), whole)
+    ref = OM.moe_block_f64(c["x"], c["res"], idx, w, c["gate"], c["up"], c["down"], shared=c["shared"])
+    assert _rel(whole, ref, c["res"]) < TOL
+
+
+def test_fixed_order_stack_prompt_layer_major(dev):
+    """Three layers of the RMSNorm stack over a 300-token prompt in one pass per layer equal the same stack
+    run block by block (blocks of 100), bit for bit."""
+    from flowmoe.stack import MoEStack
+    rng = np.random.default_rng(5)
+    layers, nws = [], []
+    for l in range(3):
+        c = cases.make_case(H=512, E=16, F=256, FS=128, k=4, T=4, seed=200 + l)
+        layers.append(_layer(c, dev, "tc"))
+        layers[-1].fixed_order = True
+        nws.append(torch.from_numpy(OM.bf16_round((1.0 + rng.normal(0, 0.01, 512)).astype(np.float32))))
+    st = MoEStack(layers, nws)
+    x = torch.from_numpy(rng.normal(0, 1, (300, 512)).astype(np.float32)).to(dev)
+    whole = st.forward(x).cpu().numpy()
+    blocks = np.concatenate([st.forward(x[i:i + 100].contiguous()).cpu().numpy() for i in range(0, 300, 100)])
+    np.testing.assert_array_equal(blocks, whole)
