@@ -167,6 +167,17 @@ FM_API int fm_moe_layer_norm(const fm_layer* L, const float* x, const uint16_t* 
 FM_API int fm_rmsnorm_bf16(const float* x, const uint16_t* norm_w, float eps, int32_t T, int32_t H, uint16_t* xb,
                            void* stream);
 
+/* Dense Q4_1 projection (the prefill projections beside the MoE block): y [T, N] f32 = bf16(x) [T, K] .
+ * dequant(W) [N, K]^T, f32 accumulation, on the tcgen05 GEMM. Replaces the reference's gemm_q4_prefill
+ * design (open_kernels/designs/gemm_q4_prefill/gemm_q4_prefill.py:1-3, Y[N_WEIGHT, T] = W(q4_1)[N_WEIGHT,
+ * K] @ X^T[K, T]); y here is token-major, the transpose of that device layout. w_tiles = W in the tile
+ * layout (fm_q4_1_to_tiles of GGUF blocks uint8[N, K/32, 20], or of fm_pool_to_q4_1's blocks for the
+ * reference's pool bytes). N % 128 == 0, K % 64 == 0; x f32 or bf16 [T, K]; x, y and the workspace
+ * 16-byte aligned. A device wait that gives up is reported by fm_moe_check(workspace). */
+FM_API int fm_q4_gemm_workspace_size(int32_t N, int32_t K, int32_t T, int32_t x_dtype, size_t* bytes);
+FM_API int fm_q4_gemm(const uint8_t* w_tiles, int32_t N, int32_t K, const void* x, int32_t x_dtype, int32_t T, float* y,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
 /* The dispatch stage alone: per local expert counts [e_local], exclusive offsets [e_local + 1] (the
  * last = routed pair count), pos [t_real, k] = row of each (token, slot) pair in the expert-sorted
  * order (-1 for an id outside the local range) and pair [offsets[e_local]] = its inverse (t * k + s).

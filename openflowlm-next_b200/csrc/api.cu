@@ -95,6 +95,8 @@ void set_error(const char* fmt, ...) {
     va_end(ap);
 }
 
+void clear_error() { g_err[0] = 0; }
+
 int cuda_status(cudaError_t e, const char* what) {
     set_error("%s: %s", what, cudaGetErrorString(e));
     return FM_ECUDA;

@@ -19,6 +19,7 @@ constexpr int kMaxRanks = FM_EP_MAX_RANKS;   // expert-parallel group size limit
 
 // Status recorded by the host API for the calling thread.
 void set_error(const char* fmt, ...);
+void clear_error();   // an entry point's first step: the calling thread's message is for this call only
 int cuda_status(cudaError_t e, const char* what);
 
 // Kernel launches made by this library in this process (reported by fm_launch_count).

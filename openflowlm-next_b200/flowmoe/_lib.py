@@ -66,6 +66,8 @@ SIGNATURES = {
     "fm_moe_dispatch": [LP, P, I32, I32, P, P, P, P, P, SZ, P],
     "fm_moe_layer_norm": [LP, P, P, ctypes.c_float, I32, I32, P, P, P, P, SZ, P],
     "fm_moe_layer_noalloc": [LP, P, I32, P, I32, I32, P, P, P, P],
+    "fm_q4_gemm_workspace_size": [I32, I32, I32, I32, ctypes.POINTER(SZ)],
+    "fm_q4_gemm": [P, I32, I32, P, I32, I32, P, P, SZ, P],
     "fm_ep_workspace_size": [LP, I32, I32, I32, ctypes.POINTER(SZ)],
     "fm_ep_dispatch": [LP, P, I32, I32, I32, P, P, P, P, P, P, P, P, SZ, P],
     "fm_ep_experts": [LP, P, I32, P, I32, P, P, P, I32, I32, P, P, P, SZ, P],

@@ -151,6 +151,15 @@ def shared_gate(xm: np.ndarray, sgw: np.ndarray, round_x: bool = True) -> np.nda
     return 1.0 / (1.0 + np.exp(-d))
 
 
+def q4_gemm_f64(x: np.ndarray, blocks: np.ndarray) -> np.ndarray:
+    """y [T, n] = x [T, k] . dequant(W)^T in fp64 over GGUF Q4_1 blocks W uint8[n, k/32, 20], x rounded to bf16
+    first (the activation precision of the device path). The reference's dense prefill GEMM checks
+    against the same product computed per token from its pool bytes, ``q4_1_pack.pool_reference``
+    (``open_kernels/q4_1_pack.py:183-191``, used by ``designs/gemm_q4_prefill/make_test.py:89-94``)."""
+    xb = bf16_round(np.asarray(x, np.float32)).astype(np.float64)
+    return (xb @ dequant_q4_1(blocks).astype(np.float64).T).astype(np.float32)
+
+
 def moe_block_f64(xm, res, idx, w, gate_blocks, up_blocks, down_blocks, t_real=None, shared=None,
                   engine_rounding: bool = True, y_bf16: bool = False):
     """out [T, H] = res + (shared) + sum over each token's experts, ascending expert order, fp64.

@@ -18,4 +18,4 @@ def pytest_configure(config):
 def golden():
     import numpy as np
     d = ROOT / "tests" / "golden"
-    return {n: np.load(d / f"{n}.npz") for n in ("q4_1", "router", "moe", "expert_pool", "q4nx")}
+    return {n: np.load(d / f"{n}.npz") for n in ("q4_1", "router", "moe", "expert_pool", "q4nx", "gemm_q4")}

@@ -21,6 +21,10 @@ Fixtures:
   q4nx.npz    the SHA-256 of what the reference's .q4nx reader (open_kernels/model/q4nx.py) dequantises
               from a one-layer container the oracle writes (2 experts, shared expert with a signed-
               quantiser matrix, router).
+  gemm_q4.npz the reference's gemm_q4_prefill test recipe (designs/gemm_q4_prefill/make_test.py:73-97) at a
+              small shape (n 256, k 512, T 32): a random_q4_1_blocks weight (seed 0) packed by
+              pack_q4_1_pool (rs 2, bf16 scales), T distinct bf16 token rows, and pool_reference (fp64 from
+              the pool bytes) per token. ``--only gemm`` writes this fixture alone.
   expert_pool.npz  the SHA-256 of the MoE expert pool regions (gate_up stripes and down slices) the
               engine's pack ops write for 2 seeded experts (F=512, H=256), built from the reference's
               own pack_q4_1_pool, stripe_transpose and down_perm, and of their source blocks.
@@ -51,6 +55,7 @@ def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("OFLM_REFERENCE"),
                     help="the reference tree (required; default: $OFLM_REFERENCE)")
+    ap.add_argument("--only", default=None, help="write one fixture only (gemm)")
     a = ap.parse_args()
     if not a.ref:
         ap.error("--ref (or OFLM_REFERENCE) must name the reference tree")
@@ -62,6 +67,18 @@ def main() -> int:
     import replica_block as RB                   # open_kernels/model/replica_block.py
     import replica as RP                         # open_kernels/model/replica.py
     from ml_dtypes import bfloat16
+
+    # ---- gemm_q4: the reference's dense prefill GEMM recipe
+    rng = np.random.default_rng(0)
+    gn, gk, gT = 256, 512, 32
+    gpool = QP.pack_q4_1_pool(QP.random_q4_1_blocks(gn, gk, rng), 2)
+    gx = [rng.standard_normal(gk).astype(np.float32).astype(bfloat16) for _ in range(gT)]
+    gy = np.stack([QP.pool_reference(gpool, gx[t].astype(np.float32), gn, gk, rs=2) for t in range(gT)])
+    np.savez_compressed(HERE / "gemm_q4.npz", n=gn, k=gk, T=gT, rs=2, pool=gpool,
+                        x_bf16=np.stack(gx).view(np.uint16), y=gy.astype(np.float32))
+    if a.only == "gemm":
+        print(f"wrote {HERE / 'gemm_q4.npz'} ({(HERE / 'gemm_q4.npz').stat().st_size} B)")
+        return 0
 
     # ---- q4_1
     rng = np.random.default_rng(0)
@@ -200,7 +217,7 @@ def main() -> int:
         m.f.close()
     np.savez_compressed(HERE / "q4nx.npz", seed=11, E=Ex, F=Fx, H=Hx, container_sha=container_sha,
                         **{k: v for k, v in shas.items()})
-    for f in ("q4_1.npz", "router.npz", "moe.npz", "expert_pool.npz", "q4nx.npz"):
+    for f in ("gemm_q4.npz", "q4_1.npz", "router.npz", "moe.npz", "expert_pool.npz", "q4nx.npz"):
         print(f"wrote {HERE / f} ({(HERE / f).stat().st_size} B)")
     return 0
 

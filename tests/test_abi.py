@@ -125,3 +125,30 @@ def test_token_counts_outside_range_are_rejected(T, t_real):
     rc = _lib.lib.fm_moe_block(ctypes.byref(_layer()), None, 0, None, None, None, None, T, t_real, None, None, 0, None)
     assert rc == _lib.FM_EINVAL_SHAPE
     assert _lib.last_error()
+
+
+@pytest.mark.parametrize("N,K,T,dt,ok", [(256, 512, 300, 0, True), (2560, 2560, 256, 1, True), (128, 64, 0, 1, True),
+                                        (200, 512, 8, 1, False), (256, 500, 8, 1, False), (256, 512, -1, 1, False),
+                                        (256, 512, 8, 7, False)])
+def test_q4_gemm_shape_checks(N, K, T, dt, ok):
+    """fm_q4_gemm: N a multiple of 128, K of 64, T >= 0, x f32 (0) or bf16 (1); the f32 input needs a bf16
+    copy of x in the workspace."""
+    from flowmoe import _lib
+    n = ctypes.c_size_t()
+    rc = _lib.lib.fm_q4_gemm_workspace_size(N, K, T, dt, ctypes.byref(n))
+    assert (rc == 0) == ok and (ok or rc == _lib.FM_EINVAL_SHAPE)
+    if ok and T > 0:
+        m = ctypes.c_size_t()
+        _lib.call("fm_q4_gemm_workspace_size", N, K, T, 1 - dt, ctypes.byref(m))
+        assert (n.value - m.value if dt == 0 else m.value - n.value) >= T * K * 2
+
+
+def test_q4_gemm_rejects_before_device_work():
+    """Zero tokens is a no-op; a NULL pointer or a short workspace is refused on the host."""
+    from flowmoe import _lib
+    assert _lib.lib.fm_q4_gemm(None, 256, 512, None, 1, 0, None, None, 0, None) == 0
+    assert _lib.lib.fm_q4_gemm(None, 256, 512, None, 1, 4, None, None, 0, None) == _lib.FM_EINVAL_SHAPE
+    buf = (ctypes.c_uint8 * 64)()
+    p = ctypes.addressof(buf) + (-ctypes.addressof(buf)) % 16
+    rc = _lib.lib.fm_q4_gemm(p, 256, 512, p, 1, 4, p, p, 16, None)
+    assert rc == _lib.FM_EWORKSPACE and "workspace" in _lib.last_error()

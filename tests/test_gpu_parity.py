@@ -461,3 +461,40 @@ def test_fixed_order_stack_prompt_layer_major(dev):
     whole = st.forward(x).cpu().numpy()
     blocks = np.concatenate([st.forward(x[i:i + 100].contiguous()).cpu().numpy() for i in range(0, 300, 100)])
     np.testing.assert_array_equal(blocks, whole)
+
+
+def test_q4_gemm_reference_fixture(dev, golden):
+    """The dense Q4_1 projection GEMM on the reference's own gemm_q4_prefill test vectors: its pool bytes
+    (pack_q4_1_pool, bf16 scales) imported as they are, its bf16 token rows, against its fp64 pool_reference;
+    the reference design's gate is rel_fro <= 5e-3 (designs/gemm_q4_prefill/compare.py)."""
+    import flowmoe
+    g = golden["gemm_q4"]
+    n, k = int(g["n"]), int(g["k"])
+    lin = flowmoe.Q4Linear.from_pool(g["pool"], n, k, rs=int(g["rs"]), device=dev)
+    x = torch.from_numpy(g["x_bf16"].astype(np.int16)).view(torch.bfloat16).to(dev)
+    y = lin.forward(x).cpu().numpy()
+    lin.check()
+    ref = g["y"]
+    assert float(np.linalg.norm(y - ref) / np.linalg.norm(ref)) <= 5e-3
+    assert np.abs(y - ref).max() / np.abs(ref).max() < TOL
+
+
+@pytest.mark.parametrize("N,K,T,f32", [(2560, 2560, 256, False), (256, 512, 300, True), (1024, 2048, 8192, False),
+                                       (128, 64, 17, True)])
+def test_q4_gemm_matches_oracle(dev, N, K, T, f32):
+    """fm_q4_gemm against the fp64 oracle: the reference's qkv projection shape (2560 x 2560, T 256), ragged
+    token counts (300, 17: a partial last item), f32 input (rounded to bf16 on the device), and a
+    prefill-sized call (T 8192: 32 row chunks per band) checked on a sample of rows."""
+    import flowmoe
+    rng = np.random.default_rng(N + K + T)
+    blocks = OQ.random_q4_1_blocks(N, K, rng)
+    lin = flowmoe.Q4Linear.from_q4_1(blocks, N, K, device=dev)
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    xt = torch.from_numpy(x).to(dev)
+    y = lin.forward(xt if f32 else xt.to(torch.bfloat16)).cpu().numpy()
+    lin.check()
+    rows = np.arange(T) if T <= 512 else np.sort(rng.choice(T, 64, replace=False))
+    ref = OM.q4_gemm_f64(x[rows], blocks)
+    got = y[rows]
+    assert float(np.linalg.norm(got - ref) / np.linalg.norm(ref)) <= 5e-3
+    assert np.abs(got - ref).max() / np.abs(ref).max() < TOL

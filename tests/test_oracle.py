@@ -240,3 +240,16 @@ def test_expert_pool_matches_reference_bytes(golden):
         st = gu[e * per:(e + 1) * per].reshape(F // 128, 2, -1)
         u_back = OQ.pool_to_blocks(st[:, 0].reshape(-1), F, H, 4)
         assert np.array_equal(OQ.dequant_q4_1(u_back), OQ.dequant_q4_1(up[e], bf16_scales=True))
+
+
+def test_gemm_oracle_matches_reference_pool_reference(golden):
+    """The dense Q4_1 GEMM oracle over the blocks recovered from the reference's pool bytes equals the
+    reference's own fp64 pool_reference (designs/gemm_q4_prefill/make_test.py recipe), token by token."""
+    g = golden["gemm_q4"]
+    n, k = int(g["n"]), int(g["k"])
+    blocks = OQ.pool_to_blocks(g["pool"], n, k, int(g["rs"]))
+    x = OM.bf16_to_f32(g["x_bf16"])
+    y = OM.q4_gemm_f64(x, blocks)
+    ref = g["y"]
+    assert y.shape == ref.shape == (int(g["T"]), n)
+    assert np.abs(y - ref).max() <= 1e-6 * np.abs(ref).max()
