@@ -70,6 +70,11 @@ struct TcSmem {
     static constexpr int SA = GATE_UP ? 4 : 2;
     static constexpr int SB = 4;
     static constexpr int SR = GATE_UP ? 4 : 6;    // raw weight tiles in flight (streamed from HBM)
+    // Slabs per pipeline stage: the MMA issuer waits, issues and commits once per stage, so the hand-off
+    // between the roles (barrier waits, commits) is paid once per KS slabs' MMAs. gate_up takes two 64-K
+    // slabs per stage (8 MMAs), one per dequantiser group; down (K = 512, 8 slabs) keeps one.
+    static constexpr int KS = GATE_UP ? 2 : 1;
+    static constexpr int SAQ = SA / KS, SBQ = SB / KS;   // stages of the A and activation rings
     static constexpr int B_STAGE = TC_B_BYTES;
     static constexpr int EPI = GATE_UP ? 3 * 16 * 64 * 4 : TC_EPI_BYTES;
     // offsets from the 1024-aligned dynamic smem base
@@ -79,7 +84,7 @@ struct TcSmem {
     static constexpr int epi = raw + SR * kTileBytes;
     static constexpr int bars = epi + EPI;
     // raw, activation, A and accumulator rings + drain
-    static constexpr int nbars = 2 * SR + 2 * SB + 2 * SA + 4 + 1;
+    static constexpr int nbars = 2 * SR + 2 * SBQ + 2 * SAQ + 4 + 1;
     static constexpr int tmem = bars + nbars * 8;
     static constexpr int total = tmem + 16 + 1024;   // + alignment slack
 };
@@ -189,17 +194,17 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                                                                   const __grid_constant__ CUtensorMap bmap_big, TcArgs a) {
     using R = TcRoles<GATE_UP>;
     using Sm = TcSmem<GATE_UP>;
-    constexpr int SA = Sm::SA, SB = Sm::SB, SR = Sm::SR, B_STAGE = Sm::B_STAGE;
+    constexpr int SR = Sm::SR, B_STAGE = Sm::B_STAGE, KS = Sm::KS, SAQ = Sm::SAQ, SBQ = Sm::SBQ;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sm::bars);
     uint64_t* raw_full = bars;
     uint64_t* raw_empty = raw_full + SR;
-    uint64_t* b_full = raw_empty + SR;
-    uint64_t* b_empty = b_full + SB;
-    uint64_t* a_full = b_empty + SB;
-    uint64_t* a_empty = a_full + SA;
-    uint64_t* acc_full = a_empty + SA;
+    uint64_t* b_full = raw_empty + SR;           // per stage of KS slabs
+    uint64_t* b_empty = b_full + SBQ;
+    uint64_t* a_full = b_empty + SBQ;
+    uint64_t* a_empty = a_full + SAQ;
+    uint64_t* acc_full = a_empty + SAQ;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;             // the MMA issuer's last commit
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Sm::tmem);
@@ -213,9 +218,9 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
         abort_flag = 0;
         // a dequantiser group (4 warps, 128 threads) consumes a raw tile and fills an A stage
         for (int i = 0; i < SR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 128); }
-        for (int i = 0; i < SB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
-        // arrivals are per warp: 4 dequantiser / 4 or 8 epilogue warps
-        for (int i = 0; i < SA; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < SBQ; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
+        // arrivals are per warp: the dequantiser warps filling a stage (4 per slab) / 4 or 8 epilogue warps
+        for (int i = 0; i < SAQ; ++i) { mbar_init(&a_full[i], 4 * KS); mbar_init(&a_empty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], R::EPI); }
         mbar_init(drain, 1);
         mbar_fence_init();
@@ -237,7 +242,8 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
         // rows (TMA, SB deep). Separate threads, so the weight stream runs ahead of the activations.
         const bool weights = warp == 0;
         if (lane == 0) {
-            const int S = weights ? SR : SB;
+            const int S = weights ? SR : SBQ;
+            const int KU = weights ? 1 : KS;   // slabs per fill: one raw tile, or a stage of activations
             uint64_t* full = weights ? raw_full : b_full;
             uint64_t* empty = weights ? raw_empty : b_empty;
             int st = 0;
@@ -251,21 +257,23 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                 const int nbig = nhalf / TC_BOX_BIG;
                 const int nsmall = (nhalf - nbig * TC_BOX_BIG + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
                 const int rows_loaded = nbig * TC_BOX_BIG + nsmall * TC_BOX_ROWS;
-                for (int s = 0; s < it.slabs; ++s) {
+                for (int s = 0; s < it.slabs; s += KU) {
                     if (!mbar_wait(&empty[st], ph ^ 1)) { ok = false; break; }
                     if (weights) {
                         mbar_expect_tx(&raw_full[st], kTileBytes);
                         bulk_load(smem + Sm::raw + st * kTileBytes, it.w + (size_t)s * kTileBytes, kTileBytes, &raw_full[st]);
                         issued |= 1u << st;
                     } else {
-                        mbar_expect_tx(&b_full[st], rows_loaded * 128);
-                        for (int j = 0; j < nbig + nsmall; ++j) {
-                            const bool big = j < nbig;
-                            const int r0 = big ? j * TC_BOX_BIG : nbig * TC_BOX_BIG + (j - nbig) * TC_BOX_ROWS;
-                            const CUtensorMap* map = big ? &bmap_big : &bmap;
-                            uint8_t* dst = smem + Sm::b + st * B_STAGE + r0 * 128;
-                            tma_load_2d(dst, map, s * kTileK, rbase + r0, &b_full[st]);
-                        }
+                        const int ns = min(KU, it.slabs - s);   // slabs in this stage
+                        mbar_expect_tx(&b_full[st], ns * rows_loaded * 128);
+                        for (int h = 0; h < ns; ++h)
+                            for (int j = 0; j < nbig + nsmall; ++j) {
+                                const bool big = j < nbig;
+                                const int r0 = big ? j * TC_BOX_BIG : nbig * TC_BOX_BIG + (j - nbig) * TC_BOX_ROWS;
+                                const CUtensorMap* map = big ? &bmap_big : &bmap;
+                                uint8_t* dst = smem + Sm::b + (st * KS + h) * B_STAGE + r0 * 128;
+                                tma_load_2d(dst, map, (s + h) * kTileK, rbase + r0, &b_full[st]);
+                            }
                         issued |= 1u << st;
                     }
                     if (++st == S) { st = 0; ph ^= 1; }
@@ -297,20 +305,23 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * 256;
                 const uint32_t idesc = idesc_bf16(128, (it.n + 15) & ~15);
-                for (int s = 0; s < it.slabs; ++s) {
+                for (int s = 0; s < it.slabs; s += KS) {
                     if (!mbar_wait(&a_full[as], aph) || !mbar_wait(&b_full[bs], bph)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(smem + Sm::a + as * TC_A_BYTES);
-                    const uint32_t sb = smem_u32(smem + Sm::b + bs * B_STAGE);
+                    const int ns = min(KS, it.slabs - s);
+                    for (int h = 0; h < ns; ++h) {
+                        const uint32_t sa = smem_u32(smem + Sm::a + (as * KS + h) * TC_A_BYTES);
+                        const uint32_t sb = smem_u32(smem + Sm::b + (bs * KS + h) * B_STAGE);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        tc_mma_f16(d_tmem, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc,
-                                   (s > 0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < 4; ++kk)
+                            tc_mma_f16(d_tmem, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc,
+                                       (s > 0 || h > 0 || kk > 0) ? 1u : 0u);
+                    }
                     issued = true;
                     tc_commit(&a_empty[as]);
                     tc_commit(&b_empty[bs]);
-                    if (++as == SA) { as = 0; aph ^= 1; }
-                    if (++bs == SB) { bs = 0; bph ^= 1; }
+                    if (++as == SAQ) { as = 0; aph ^= 1; }
+                    if (++bs == SBQ) { bs = 0; bph ^= 1; }
                 }
                 if (!ok) break;
                 tc_commit(&acc_full[acc]);
@@ -327,49 +338,62 @@ __global__ void __launch_bounds__(TcRoles<GATE_UP>::THREADS, 1) expert_tc_kernel
         }
     } else if (warp < R::EPI0) {
         // ------------------------------------------------------------ dequantisers
-        // Groups of 4 warps; group g takes the slabs whose running index sc has sc % NG == g, so NG
-        // slabs are dequantised at once (the per-slab chain of barrier, shared loads and stores is
-        // latency-bound). Thread t of a group rebuilds row t of the tile (both 32-value blocks).
+        // Groups of 4 warps; thread t of a group rebuilds row t of a tile (both 32-value blocks). With two
+        // slabs per stage (gate_up) group g takes slab g of every stage, so both groups fill a stage at
+        // once; with one (down) the groups take alternate stages. Either way two slabs are dequantised at
+        // once (the per-slab chain of barrier, shared loads and stores is latency-bound).
         constexpr int NG = R::DQ / 4;
         const int t = threadIdx.x - 64;
         const int grp = t >> 7;
         const int r = t & 127;
+        const int h = KS == NG ? grp : 0;   // this group's slab within a stage
         bool ok = true;
-        int sc = 0;   // running slab index over this CTA's items
+        int qc = 0, scb = 0;   // running stage index over this CTA's items; slabs of its earlier items
         for (int i = unit; i < n_items && ok; i += n_units) {
             const Item it = decode_item(a, i);
-            for (int s = 0; s < it.slabs; ++s, ++sc) {
-                if (sc % NG != grp) continue;
-                const int rs = sc % SR, as = sc % SA;
-                const uint32_t rph = (sc / SR) & 1, aph = (sc / SA) & 1;
-                if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[rs], rph))) { ok = false; break; }
-                const uint32_t raw = smem_u32(smem + Sm::raw + rs * kTileBytes);
-                const uint4 n0 = lds128(raw + r * 32);
-                const uint4 n1 = lds128(raw + r * 32 + 16);
-                const uint2 sc2 = lds64(raw + kTileNibBytes + r * 8);
-                const float d0 = __half2float(__ushort_as_half((unsigned short)(sc2.x & 0xFFFF)));
-                const float m0 = __half2float(__ushort_as_half((unsigned short)(sc2.x >> 16)));
-                const float d1 = __half2float(__ushort_as_half((unsigned short)(sc2.y & 0xFFFF)));
-                const float m1 = __half2float(__ushort_as_half((unsigned short)(sc2.y >> 16)));
+            const int nst = (it.slabs + KS - 1) / KS;
+            for (int q = 0; q < nst; ++q, ++qc) {
+                if (KS == 1 && qc % NG != grp) continue;
+                const int s = q * KS + h;
+                const bool has = s < it.slabs;   // the last stage of an odd slab count has one slab
+                const int as = qc % SAQ;
+                const uint32_t aph = (qc / SAQ) & 1;
                 uint32_t wv[32];   // the row's 64 values in K order: 16-byte chunk c = words 4c..4c+3
-                deq_block(n0, d0, m0, wv);
-                deq_block(n1, d1, m1, wv + 16);
-                // The raw slot goes back to the weight producer, whose next bulk copy (async proxy)
-                // overwrites it, only after this thread's loads from it have delivered their values (the
-                // dequantised words depend on them) and a proxy fence: releasing it right after issuing
-                // the loads let the copy land under loads still in flight on B200 (wrong weights for a
-                // slab, intermittently).
-                fence_proxy_async_smem();
-                mbar_arrive(&raw_empty[rs]);
+                if (has) {
+                    const int rs = (scb + s) % SR;
+                    const uint32_t rph = ((scb + s) / SR) & 1;
+                    if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[rs], rph))) { ok = false; break; }
+                    const uint32_t raw = smem_u32(smem + Sm::raw + rs * kTileBytes);
+                    const uint4 n0 = lds128(raw + r * 32);
+                    const uint4 n1 = lds128(raw + r * 32 + 16);
+                    const uint2 sc2 = lds64(raw + kTileNibBytes + r * 8);
+                    const float d0 = __half2float(__ushort_as_half((unsigned short)(sc2.x & 0xFFFF)));
+                    const float m0 = __half2float(__ushort_as_half((unsigned short)(sc2.x >> 16)));
+                    const float d1 = __half2float(__ushort_as_half((unsigned short)(sc2.y & 0xFFFF)));
+                    const float m1 = __half2float(__ushort_as_half((unsigned short)(sc2.y >> 16)));
+                    deq_block(n0, d0, m0, wv);
+                    deq_block(n1, d1, m1, wv + 16);
+                    // The raw slot goes back to the weight producer, whose next bulk copy (async proxy)
+                    // overwrites it, only after this thread's loads from it have delivered their values (the
+                    // dequantised words depend on them) and a proxy fence: releasing it right after issuing
+                    // the loads let the copy land under loads still in flight on B200 (wrong weights for a
+                    // slab, intermittently).
+                    fence_proxy_async_smem();
+                    mbar_arrive(&raw_empty[rs]);
+                }
                 if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[as], aph ^ 1))) { ok = false; break; }
-                const uint32_t arow = smem_u32(smem + Sm::a + as * TC_A_BYTES + r * 128);
+                if (has) {
+                    const uint32_t arow = smem_u32(smem + Sm::a + (as * KS + h) * TC_A_BYTES + r * 128);
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    sts128(arow + ((c ^ (r & 7)) << 4), make_uint4(wv[4 * c], wv[4 * c + 1], wv[4 * c + 2], wv[4 * c + 3]));
-                fence_proxy_async_smem();
+                    for (int c = 0; c < 8; ++c)
+                        sts128(arow + ((c ^ (r & 7)) << 4),
+                               make_uint4(wv[4 * c], wv[4 * c + 1], wv[4 * c + 2], wv[4 * c + 3]));
+                    fence_proxy_async_smem();
+                }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&a_full[as]);   // the warp's 32 rows are in place
+                if (lane == 0) mbar_arrive(&a_full[as]);   // the warp's 32 rows are in place (or absent)
             }
+            scb += it.slabs;
         }
         if (!ok) {
             fail(a.err, FM_ETIMEOUT);
