@@ -4,6 +4,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include <map>
@@ -19,6 +20,14 @@ static thread_local char g_err[512];
 static std::atomic<unsigned long long> g_launches{0};
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool pdl_on() {
+    static const bool on = [] {
+        const char* v = std::getenv("FLOWMOE_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
 
 int device_sm_count() {
     constexpr int kDevs = 64;

@@ -24,6 +24,8 @@ __global__ void combine_kernel(const float* __restrict__ res, const YT* __restri
                                const int32_t* __restrict__ idx, const float* __restrict__ w,
                                const float* __restrict__ sgate, int shared_on, int T, int t_real, int k, int H, int P,
                                float* __restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int t = blockIdx.x;
     __shared__ int srow[kMaxTopK];
     __shared__ float sw[kMaxTopK];
@@ -85,8 +87,8 @@ int launch_combine(const float* res, const float* y, const int* pos, const int32
                    const float* sgate, int shared_on, int T, int t_real, int k, int H, int P, float* out, cudaStream_t st) {
     if (T <= 0) return FM_OK;
     dim3 grid(T, (H / 4 + 255) / 256);
-    combine_kernel<float><<<grid, 256, 0, st>>>(res, y, pos, idx, w, sgate, shared_on, T, t_real, k, H, P, out);
-    FM_LAUNCH_CHECK("combine");
+    FM_LAUNCH_PDL("combine", combine_kernel<float>, grid, dim3(256), 0, st, res, y, pos, idx, w, sgate, shared_on, T, t_real,
+                  k, H, P, out);
     return FM_OK;
 }
 

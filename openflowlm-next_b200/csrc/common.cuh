@@ -41,6 +41,46 @@ cudaError_t raise_smem_limit(const void* func, int bytes);
         if (e_ != cudaSuccess) return ::fm::cuda_status(e_, what);   \
     } while (0)
 
+// Programmatic dependent launch on the decode-size chain (RMSNorm / bf16 conversion, router, single-CTA
+// dispatch, GEMVs, combine): each of those kernels may be scheduled while the one before it in the
+// stream still runs, so its launch latency and prologue overlap that kernel. On unless the environment
+// sets FLOWMOE_PDL=0.
+bool pdl_on();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_on() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// Launch through launch_pdl, counted and checked like FM_LAUNCH_CHECK.
+#define FM_LAUNCH_PDL(what, kern, grid, block, smem, st, ...)                                \
+    do {                                                                                     \
+        ::fm::note_launch();                                                                 \
+        cudaError_t e_ = ::fm::launch_pdl(kern, grid, block, smem, st, __VA_ARGS__);         \
+        const cudaError_t l_ = cudaGetLastError();                                           \
+        if (e_ == cudaSuccess) e_ = l_;                                                      \
+        if (e_ != cudaSuccess) return ::fm::cuda_status(e_, what);                           \
+    } while (0)
+
+// The device side of a programmatically launched kernel. pdl_wait() returns once the kernel before it
+// in the stream has completed and its writes are visible (at once for an ordinary launch); such a
+// kernel calls it before its first access to memory that earlier work writes or reads. Because every
+// kernel of the chain waits so, each one completes only after all work before it. pdl_launch_dependents()
+// lets the next kernel's CTAs be scheduled; it is called after pdl_wait(), so a kernel that starts early
+// finds everything two launches back complete.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Stage timing (fm_profile): CUDA events around each stage on the launching stream.
 enum Stage { kStageToBf16 = 0, kStageRouter, kStageDispatch, kStageGather, kStageGateUp, kStageDown, kStageCombine,
              kStageCount };

@@ -92,6 +92,8 @@ __global__ void __launch_bounds__(kDispSmallThreads) dispatch_small_kernel(
     int* gu0 = off_s + e_local + 1;                 // [e_local + 2] first GEMV slot of each group (gate/up)
     int* dn0 = gu0 + e_local + 2;                   // [e_local + 2] (down)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    pdl_launch_dependents();
     // this call's status words (bad ids, GEMV timeouts), unless the caller cleared them before its router
     if (clear && threadIdx.x < 4) err[threadIdx.x] = 0;
     __syncthreads();
@@ -463,6 +465,8 @@ __global__ void __launch_bounds__(GV_THREADS, GV_CTAS_PER_SM) gemv_kernel(GemvAr
     }
     if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(smem + GvSmem::zero)[threadIdx.x] = 0u;
     __syncthreads();
+    pdl_wait();
+    pdl_launch_dependents();
     const int n_items = a.list[0], KC = a.list[1];
     if (GATE_UP && a.dn_list[1] > 1) {   // the down GEMM will add its K chunks into y: clear it first
         float4* y4 = reinterpret_cast<float4*>(a.y_out);
@@ -635,11 +639,9 @@ int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, i
     if (cudaError_t e = raise_smem_limit((const void*)dispatch_small_kernel, 160 * 1024))
         return cuda_status(e, "dispatch_small smem");
     const int target = GV_CTAS_PER_SM * device_sm_count();   // one item per CTA slot
-    dispatch_small_kernel<<<1, kDispSmallThreads, sm, st>>>(idx, P, e_begin, e_local, shared_base, shared_rows, counts,
-                                                           offsets, pos, pair, gu_list, gu_bands, gu_bands_shared,
-                                                           gu_slabs, dn_list, dn_bands, dn_slabs, dn_slabs_shared, kc_cap, split,
-                                                           target, clear, done, err);
-    FM_LAUNCH_CHECK("dispatch_small");
+    FM_LAUNCH_PDL("dispatch_small", dispatch_small_kernel, dim3(1), dim3(kDispSmallThreads), sm, st, idx, P, e_begin, e_local,
+                  shared_base, shared_rows, counts, offsets, pos, pair, gu_list, gu_bands, gu_bands_shared, gu_slabs, dn_list,
+                  dn_bands, dn_slabs, dn_slabs_shared, kc_cap, split, target, clear, done, err);
     return FM_OK;
 }
 
@@ -677,10 +679,9 @@ int launch_gemv(bool gate_up, const GemvLaunch& L, cudaStream_t st) {
     const void* fn = gate_up ? (const void*)gemv_kernel<true> : (const void*)gemv_kernel<false>;
     if (cudaError_t e = raise_smem_limit(fn, GvSmem::total)) return cuda_status(e, "gemv smem");
     if (gate_up)
-        gemv_kernel<true><<<grid, GV_THREADS, GvSmem::total, st>>>(a);
+        FM_LAUNCH_PDL("gemv<gate_up>", gemv_kernel<true>, dim3(grid), dim3(GV_THREADS), GvSmem::total, st, a);
     else
-        gemv_kernel<false><<<grid, GV_THREADS, GvSmem::total, st>>>(a);
-    FM_LAUNCH_CHECK(gate_up ? "gemv<gate_up>" : "gemv<down>");
+        FM_LAUNCH_PDL("gemv<down>", gemv_kernel<false>, dim3(grid), dim3(GV_THREADS), GvSmem::total, st, a);
     return FM_OK;
 }
 

@@ -15,6 +15,8 @@ namespace fm {
 // xb[t][h] = bf16(xm[t][h]) for f32 input (the rounding the reference applies at the device
 // boundary, core.cpp:5204).
 __global__ void to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict__ xb, long long n4) {
+    pdl_wait();
+    pdl_launch_dependents();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
         const float4 v = reinterpret_cast<const float4*>(x)[i];
         uint2 o;
@@ -39,6 +41,8 @@ constexpr int kMaxKSplit = 16;
 
 __global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __restrict__ A, const uint16_t* __restrict__ B,
                                                             float* __restrict__ part, int M, int N, int K) {
+    pdl_wait();
+    pdl_launch_dependents();
     __shared__ __align__(16) uint16_t sa[2][RG_BM][RG_LD];
     __shared__ __align__(16) uint16_t sb[2][RG_BN][RG_LD];
     const int m0 = blockIdx.y * RG_BM, n0 = blockIdx.x * RG_BN;
@@ -122,6 +126,8 @@ __global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __re
 __global__ void router_topk_kernel(float* __restrict__ logits, int ld, const float* __restrict__ bias, int T, int E,
                                    int k, int ks, float* __restrict__ probs, int32_t* __restrict__ idx,
                                    float* __restrict__ w, float* __restrict__ sgate) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
     float* lg = logits + (size_t)warp * ld;
@@ -205,6 +211,8 @@ template <bool SPLIT>
 __global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, int ks, const float* __restrict__ bias,
                                     int T, int E, int k, float* __restrict__ probs, int32_t* __restrict__ idx,
                                     float* __restrict__ w, float* __restrict__ sgate) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
     const float* lg = logits + (size_t)warp * ld;
@@ -268,6 +276,8 @@ __global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, in
 // fp64 (Core::rmsnorm_host, src/open_qwen36/core.cpp:3014-3044, groups = 1; weight bf16).
 __global__ void rmsnorm_bf16_kernel(const float* __restrict__ x, const uint16_t* __restrict__ w, double eps, int T, int H,
                                     uint16_t* __restrict__ xb) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (t >= T) return;
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * H);
@@ -294,16 +304,14 @@ __global__ void rmsnorm_bf16_kernel(const float* __restrict__ x, const uint16_t*
 
 int launch_rmsnorm_bf16(const float* x, const uint16_t* w, float eps, int T, int H, uint16_t* xb, cudaStream_t st) {
     if (T <= 0) return FM_OK;
-    rmsnorm_bf16_kernel<<<(T + 7) / 8, 256, 0, st>>>(x, w, (double)eps, T, H, xb);
-    FM_LAUNCH_CHECK("rmsnorm_bf16");
+    FM_LAUNCH_PDL("rmsnorm_bf16", rmsnorm_bf16_kernel, dim3((T + 7) / 8), dim3(256), 0, st, x, w, (double)eps, T, H, xb);
     return FM_OK;
 }
 
 int launch_to_bf16(const float* x, uint16_t* xb, long long n, cudaStream_t st) {
     const long long n4 = n / 4;
     const int grid = (int)((n4 + 255) / 256 < 2048 ? (n4 + 255) / 256 : 2048);
-    to_bf16_kernel<<<grid > 0 ? grid : 1, 256, 0, st>>>(x, xb, n4);
-    FM_LAUNCH_CHECK("to_bf16");
+    FM_LAUNCH_PDL("to_bf16", to_bf16_kernel, dim3(grid > 0 ? grid : 1), dim3(256), 0, st, x, xb, n4);
     return FM_OK;
 }
 
@@ -331,18 +339,18 @@ int launch_router(const uint16_t* xb, const uint16_t* router, const float* bias,
         if (int rc = launch_router_tc_logits(xb, router, T, H, E, logits, err, st)) return rc;
     } else {
         dim3 grid((E + 1 + RG_BN - 1) / RG_BN, (T + RG_BM - 1) / RG_BM, ks);
-        router_logits_kernel<<<grid, 128, 0, st>>>(xb, router, logits, T, E + 1, H);
-        FM_LAUNCH_CHECK("router_logits");
+        FM_LAUNCH_PDL("router_logits", router_logits_kernel, grid, dim3(128), 0, st, xb, router, logits, T, E + 1, H);
     }
     if (E <= 256) {
         if (ks > 1)   // one warp per CTA: each token's ks x (E + 1) partial logits stream into its own SM
-            router_topk8_kernel<true><<<T, 32, 0, st>>>(logits, ld, ks, bias, T, E, k, probs, idx, w, sgate);
+            FM_LAUNCH_PDL("router_topk8", router_topk8_kernel<true>, dim3(T), dim3(32), 0, st, logits, ld, ks, bias, T, E,
+                          k, probs, idx, w, sgate);
         else
-            router_topk8_kernel<false><<<(T + 7) / 8, 256, 0, st>>>(logits, ld, ks, bias, T, E, k, probs, idx, w, sgate);
-        FM_LAUNCH_CHECK("router_topk8");
+            FM_LAUNCH_PDL("router_topk8", router_topk8_kernel<false>, dim3((T + 7) / 8), dim3(256), 0, st, logits, ld, ks,
+                          bias, T, E, k, probs, idx, w, sgate);
     } else {
-        router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, ld, bias, T, E, k, ks, probs, idx, w, sgate);
-        FM_LAUNCH_CHECK("router_topk");
+        FM_LAUNCH_PDL("router_topk", router_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, st, logits, ld, bias, T, E, k, ks,
+                      probs, idx, w, sgate);
     }
     return FM_OK;
 }

@@ -99,6 +99,43 @@ def test_noalloc_prefill_path_twice(dev):
     _two_calls(c, dev, _layer(c, dev), [(300, 300), (260, 257)])
 
 
+@pytest.mark.parametrize("T", [1, 32])
+def test_noalloc_captured_in_a_graph(dev, T):
+    """The use the entry point exists for: after one eager call, the call is captured into a CUDA graph
+    (the decode chain's kernels carry the programmatic-dependent-launch attribute into it) and replayed
+    on new inputs copied into the captured buffers; every replay matches an eager fm_moe_layer call on
+    the same inputs, and replays leave free device memory unchanged."""
+    from flowmoe import _lib
+    c = cases.make_case(H=2048, E=16, F=512, FS=512, k=8, T=3 * T, seed=14 + T)
+    lay = _layer(c, dev)
+    x = torch.from_numpy(c["x"][:T]).to(dev).to(torch.bfloat16)
+    res = torch.from_numpy(c["res"][:T]).to(dev)
+    out = torch.empty_like(res)
+    idx = torch.empty(T, 8, dtype=torch.int32, device=dev)
+    w = torch.empty(T, 8, device=dev)
+    assert _noalloc(lay, x, res, T, T, out, idx, w) == _lib.FM_OK, _lib.last_error()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        assert _noalloc(lay, x, res, T, T, out, idx, w) == _lib.FM_OK, _lib.last_error()
+    inputs = []
+    for r in range(3):   # the eager references first, so that no torch allocation falls between replays
+        xs = torch.from_numpy(c["x"][r * T:(r + 1) * T]).to(dev).to(torch.bfloat16)
+        rs = torch.from_numpy(c["res"][r * T:(r + 1) * T]).to(dev)
+        inputs.append((xs, rs, lay.forward(xs, rs).cpu().numpy()))
+    free = _free()
+    for r, (xs, rs, want) in enumerate(inputs):
+        x.copy_(xs)
+        res.copy_(rs)
+        out.fill_(float("nan"))
+        g.replay()
+        got = out.cpu().numpy()
+        err = np.abs(got - want).max() / np.abs(want - c["res"][r * T:(r + 1) * T]).max()
+        assert err < TOL, f"replay {r}: max rel err {err:.3e} against fm_moe_layer"
+    assert _free() == free, "a replay changed free device memory"
+    del g
+
+
 def test_noalloc_rejects_more_tokens_than_the_static_array(dev):
     from flowmoe import _lib
     c = cases.make_case(H=2048, E=16, F=512, FS=512, k=8, T=4, seed=13)
