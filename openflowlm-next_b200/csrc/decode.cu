@@ -467,7 +467,11 @@ __global__ void __launch_bounds__(GV_THREADS, GV_CTAS_PER_SM) gemv_kernel(GemvAr
     __syncthreads();
     pdl_wait();
     pdl_launch_dependents();
+    // the item count and this CTA's first entry load together (the entry's slot exists: the grid is no
+    // larger than the list's capacity); the entry is dropped when it lies past the count
+    const int4 first = __ldg(reinterpret_cast<const int4*>(a.list + 4) + blockIdx.x);
     const int n_items = a.list[0], KC = a.list[1];
+    const int4 e_first = (int)blockIdx.x < n_items ? first : make_int4(0, 0, 0, 0);
     if (GATE_UP && a.dn_list[1] > 1) {   // the down GEMM will add its K chunks into y: clear it first
         float4* y4 = reinterpret_cast<float4*>(a.y_out);
         const long long n4 = (long long)a.y_rows * a.H / 4;
@@ -483,7 +487,7 @@ __global__ void __launch_bounds__(GV_THREADS, GV_CTAS_PER_SM) gemv_kernel(GemvAr
         // list entries two items ahead and source rows one item ahead are in flight while an item's
         // slabs are issued
         const int G = gridDim.x;
-        int4 e0 = gv_entry(a, blockIdx.x, n_items), e1 = gv_entry(a, blockIdx.x + G, n_items);
+        int4 e0 = e_first, e1 = gv_entry(a, blockIdx.x + G, n_items);
         int row0 = gv_src_row<GATE_UP>(a, e0, lane);
         for (int i = blockIdx.x; i < n_items && ok; i += G) {
             const int4 e2 = gv_entry(a, i + 2 * G, n_items);
@@ -521,7 +525,7 @@ __global__ void __launch_bounds__(GV_THREADS, GV_CTAS_PER_SM) gemv_kernel(GemvAr
         int st = 0;
         uint32_t ph = 0;
         bool ok = true;
-        int4 e0 = gv_entry(a, blockIdx.x, n_items);
+        int4 e0 = e_first;
         for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
             const int4 e1 = gv_entry(a, i + gridDim.x, n_items);   // the next item's entry, in flight
             const GvItem it = gv_decode(a, e0, KC);
@@ -589,18 +593,42 @@ __global__ void __launch_bounds__(GV_THREADS, GV_CTAS_PER_SM) gemv_kernel(GemvAr
                 if (lane == 0) last = atomicAdd(&a.done[it.slot * GV_WARPS + j], 1) == KC - 1;
                 if (!__shfl_sync(0xffffffffu, last, 0)) continue;
                 __threadfence();
+                // each owned value's KC partial sums, added in chunk order; the loads of four chunks for
+                // all of the lane's values are issued before their adds, so the reduction costs
+                // ceil(KC / 4) L2 round trips rather than one per partial sum
+                const size_t zs = (size_t)a.part_rows * ncols;
+                float v[2][2][2] = {};
+                for (int q0 = 0; q0 < KC; q0 += 4) {
+                    float pv[4][2][2][2];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+#pragma unroll
+                        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                                for (int cc = 0; cc < 2; ++cc)
+                                    pv[u][mt][h][cc] = own[cc] && q0 + u < KC
+                                                           ? __ldcg(a.part + (size_t)(q0 + u) * zs +
+                                                                    (size_t)(it.row0 + 2 * c + cc) * ncols + colof(mt, h))
+                                                           : 0.f;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+#pragma unroll
+                        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                                for (int cc = 0; cc < 2; ++cc)
+                                    if (q0 + u < KC) v[mt][h][cc] += pv[u][mt][h][cc];
+                }
 #pragma unroll
                 for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
                     for (int h = 0; h < 2; ++h)
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc)
-                            if (own[cc]) {
-                                const size_t o = (size_t)(it.row0 + 2 * c + cc) * ncols + colof(mt, h);
-                                float v = 0.f;
-                                for (int q = 0; q < KC; ++q) v += __ldcg(a.part + (size_t)q * a.part_rows * ncols + o);
-                                acc[mt][2 * h + cc] = v;
-                            }
+                            if (own[cc]) acc[mt][2 * h + cc] = v[mt][h][cc];
             }
 #pragma unroll
             for (int h = 0; h < 2; ++h)

@@ -189,21 +189,6 @@ __global__ void router_topk_kernel(float* __restrict__ logits, int ld, const flo
     }
 }
 
-// Logit e of a token row lg summed over the ks K chunks (chunk stride zs) in chunk order, every chunk's
-// load issued before the first add.
-template <bool SPLIT>
-__device__ __forceinline__ float chunk_sum(const float* lg, size_t zs, int ks, int e) {
-    if (!SPLIT) return lg[e];
-    float part[kMaxKSplit];
-#pragma unroll
-    for (int z = 0; z < kMaxKSplit; ++z) part[z] = z < ks ? lg[(size_t)z * zs + e] : 0.f;
-    float v = part[0];
-#pragma unroll
-    for (int z = 1; z < kMaxKSplit; ++z)
-        if (z < ks) v += part[z];
-    return v;
-}
-
 // The same result for E <= 256, with each lane's (up to 8) probabilities kept in registers: the ks K
 // chunks summed in chunk order (as above), one exp per expert, then k rounds of (lane max, warp arg-max).
 // The shared-gate logit is the logits row's column E.
@@ -217,12 +202,34 @@ __global__ void router_topk8_kernel(const float* __restrict__ logits, int ld, in
     if (warp >= T) return;
     const float* lg = logits + (size_t)warp * ld;
     const size_t zs = (size_t)T * ld;
-    const float gl = sgate ? chunk_sum<SPLIT>(lg, zs, ks, E) : 0.f;
+    // the lane's eight logits and the shared-gate logit (slot 8), each summed over the ks K chunks in
+    // chunk order (ks = 1 without SPLIT); the loads of four chunks for all nine are issued before their
+    // adds, so the sums cost ceil(ks / 4) round trips to L2
+    float s[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) s[i] = 0.f;
+    for (int z0 = 0; z0 < ks; z0 += 4) {
+        float pv[4][9];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < 9; ++i) {
+                const int e = i < 8 ? lane + 32 * i : E;
+                const bool on = z0 + u < ks && (i < 8 ? e < E : sgate != nullptr);
+                pv[u][i] = on ? lg[(size_t)(z0 + u) * zs + e] : 0.f;
+            }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < 9; ++i)
+                if (z0 + u < ks) s[i] = z0 + u == 0 ? pv[u][i] : s[i] + pv[u][i];
+    }
+    const float gl = s[8];
     float v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int e = lane + 32 * i;
-        v[i] = e < E ? chunk_sum<SPLIT>(lg, zs, ks, e) + (bias ? bias[e] : 0.f) : -INFINITY;
+        v[i] = e < E ? s[i] + (bias ? bias[e] : 0.f) : -INFINITY;
     }
     float mx = v[0];
 #pragma unroll
