@@ -15,7 +15,7 @@
 // i.e. the oracle's exact dequantisation (q4_1_pack.py:104-109) with only f32 roundings. With few tokens
 // per item the MMA's 8 columns hold several blocks (column = token x block phase), so the per-block
 // scale work is done once per 8 / tokens blocks instead of per block.
-// K is split into chunks only when there are fewer items than CTA slots. gate/up: the last warp to
+// K is split into chunks only when there are fewer than two items per SM. gate/up: the last warp to
 // finish a (slot, rows) reduces the chunks' partial sums in chunk order (deterministic), then applies
 // SwiGLU; down: chunks add into the y rows with red.add (the gate/up kernel clears them first).
 //   GATE_UP: tile rows 0-63 gate, 64-127 up of 64 features -> h = bf16(silu(g) * u) (moe_batch.h:181-202)
@@ -64,7 +64,7 @@ __device__ int2 block_exclusive_scan2_1024(int2 v, int* sh, int2* tot) {
 }
 
 // K chunks per item: the smallest divisor of the slab counts (at least two slabs per chunk, at most
-// kc_cap chunks) that gives `target` items (one per GEMV CTA slot), else the largest such divisor. Splits
+// kc_cap chunks) that gives `target` items (two per SM), else the largest such divisor. Splits
 // are kept few: each costs a round trip of n x 128 partial sums through L2, a completion counter and
 // the ramp of another item, measured dearer than the load imbalance they remove.
 __device__ int choose_chunks(int base_items, int slabs, int slabs_other, int kc_cap, int target) {
@@ -666,7 +666,10 @@ int launch_dispatch_small(const int32_t* idx, int P, int e_begin, int e_local, i
     // captured into a graph, say) has to raise it again
     if (cudaError_t e = raise_smem_limit((const void*)dispatch_small_kernel, 160 * 1024))
         return cuda_status(e, "dispatch_small smem");
-    const int target = GV_CTAS_PER_SM * device_sm_count();   // one item per CTA slot
+    // K chunks are added until a call has two items per SM (half the CTA slots): filling every slot
+    // measured slower at 1-8 tokens, its extra chunks costing more in partial sums and second rounds of
+    // items than they add in parallel loads
+    const int target = 2 * device_sm_count();
     FM_LAUNCH_PDL("dispatch_small", dispatch_small_kernel, dim3(1), dim3(kDispSmallThreads), sm, st, idx, P, e_begin, e_local,
                   shared_base, shared_rows, counts, offsets, pos, pair, gu_list, gu_bands, gu_bands_shared, gu_slabs, dn_list,
                   dn_bands, dn_slabs, dn_slabs_shared, kc_cap, split, target, clear, done, err);
